@@ -1,0 +1,142 @@
+"""Plain PyTorch twins of the engine's kernels, one per kernel, for tests only.
+
+They serve two purposes. On the GPU each hand-written kernel is compared with its twin.
+On the CPU the twins stand in for the kernel table, so that the cache manager, the step
+function, the scheduler and the parts can be exercised where no GPU is present. They are
+slow, use no cache-specific tricks (pages are gathered into dense tensors, one segment at
+a time) and are not part of the package.
+"""
+
+from __future__ import annotations
+
+import torch
+
+
+class TorchKernels:
+    name = "torch-twin"
+    max_top_k = 64
+
+    def __init__(self, device="cpu"):
+        self.device = torch.device(device)
+        self.launches = 0
+
+    def check_status(self):
+        pass
+
+    # ------------------------------------------------------------------ elementwise
+    def embedding(self, table, token_ids):
+        return table[token_ids.long()].to(torch.float32)
+
+    def add_rmsnorm(self, residual, delta, weight, eps, out_dtype):
+        if delta is not None:
+            residual += delta.to(torch.float32)
+        scale = torch.rsqrt(residual.pow(2).mean(dim=-1, keepdim=True) + eps)
+        return (residual * scale * weight.to(torch.float32)).to(out_dtype)
+
+    def swiglu(self, gate_up):
+        inter = gate_up.shape[1] // 2
+        g, u = gate_up[:, :inter].float(), gate_up[:, inter:].float()
+        return (g / (1 + torch.exp(-g)) * u).to(gate_up.dtype)
+
+    def gather_rows(self, x, rows):
+        return x[rows.long()].clone()
+
+    def linear(self, x, w, out_dtype=None):
+        return (x.float() @ w.float().t()).to(out_dtype or x.dtype)
+
+    # ------------------------------------------------------------------ attention
+    def rope_kv_write(self, qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True):
+        T = qkv.shape[0]
+        x = qkv.view(T, heads + 2 * kv_heads, head_dim)
+        n_rot = heads + kv_heads
+        if rotary_dim:
+            half = rotary_dim // 2
+            angles = batch.positions.to(torch.float32)[:, None] * inv_freq[None, :]
+            cos, sin = torch.cos(angles)[:, None, :], torch.sin(angles)[:, None, :]
+            a = x[:, :n_rot, :half].float().clone()
+            b = x[:, :n_rot, half:rotary_dim].float().clone()
+            x[:, :n_rot, :half] = (a * cos - b * sin).to(qkv.dtype)
+            x[:, :n_rot, half:rotary_dim] = (b * cos + a * sin).to(qkv.dtype)
+        if not write_kv or view is None:
+            return
+        P = view.page_size
+        pos = batch.positions.long()
+        pages = view.block_table[batch.seg_of_token.long(), pos // P].long()
+        view.keys[pages, :, pos % P, :] = x[:, heads:heads + kv_heads, :]
+        view.values[pages, :, pos % P, :] = x[:, heads + kv_heads:, :]
+
+    def paged_attention(self, qkv, batch, heads, kv_heads, head_dim, scale, view):
+        T = qkv.shape[0]
+        q_all = qkv.view(T, heads + 2 * kv_heads, head_dim)[:, :heads, :].float()
+        out = torch.empty(T, heads, head_dim, dtype=torch.float32, device=qkv.device)
+        P = view.page_size
+        start = 0
+        for r, n in enumerate(batch.seg_lens):
+            pos0 = batch.seg_pos0_list[r]
+            ctx = pos0 + n
+            n_pages = -(-ctx // P)
+            pages = view.block_table[r, :n_pages].long()
+            k = view.keys[pages].permute(0, 2, 1, 3).reshape(n_pages * P, kv_heads, head_dim)[:ctx].float()
+            v = view.values[pages].permute(0, 2, 1, 3).reshape(n_pages * P, kv_heads, head_dim)[:ctx].float()
+            rep = heads // kv_heads
+            k, v = k.repeat_interleave(rep, dim=1), v.repeat_interleave(rep, dim=1)
+            q = q_all[start:start + n]
+            scores = torch.einsum("thd,shd->hts", q, k) * scale
+            qpos = torch.arange(pos0, ctx, device=qkv.device)[:, None]
+            kpos = torch.arange(ctx, device=qkv.device)[None, :]
+            visible = kpos <= qpos
+            if view.window:
+                visible &= kpos > qpos - view.window
+            scores = scores.masked_fill(~visible[None], float("-inf"))
+            out[start:start + n] = torch.einsum("hts,shd->thd", torch.softmax(scores, dim=-1), v)
+            start += n
+        return out.reshape(T, heads * head_dim).to(qkv.dtype)
+
+    # ------------------------------------------------------------------ sampling
+    @staticmethod
+    def uniform(seed: int, counter: int) -> float:
+        """u in [0, 1) from (seed, counter): a 64-bit mix, top 24 bits."""
+        mask = (1 << 64) - 1
+        x = (seed & mask) ^ ((counter + 0x9E3779B97F4A7C15) & mask)
+        x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & mask
+        x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & mask
+        x ^= x >> 31
+        return (x >> 40) / 16777216.0
+
+    def sample(self, logits, temperature=None, top_k=None, top_p=None, seeds=None, counters=None):
+        rows, vocab = logits.shape
+        out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+        for r in range(rows):
+            l = logits[r].float().cpu()
+            best = int(torch.argmax(l))          # torch.argmax gives the first of equal maxima on the CPU
+            temp = float(temperature[r]) if temperature is not None else 0.0
+            if not temp > 0:
+                out[r] = best
+                continue
+            u = self.uniform(int(seeds[r]), int(counters[r]))
+            k = int(top_k[r]) if top_k is not None else 0
+            p_limit = float(top_p[r]) if top_p is not None else 1.0
+            probs = torch.exp((l - l[best]) / temp)
+            if k <= 0:
+                cdf = torch.cumsum(probs.double(), 0)
+                target = u * float(cdf[-1])
+                pick = int(torch.searchsorted(cdf, torch.tensor(target, dtype=torch.float64), right=True))
+                out[r] = min(pick, vocab - 1)
+                continue
+            k = min(k, vocab, self.max_top_k)
+            order = sorted(range(vocab), key=lambda i: (-float(l[i]), i))[:k]
+            cand = probs[order].double()
+            keep = k
+            if p_limit < 1.0:
+                tail = 0.0
+                for c in range(k - 1, 0, -1):
+                    tail += float(cand[c] / cand.sum())
+                    if tail <= 1.0 - p_limit:
+                        keep = c
+                    else:
+                        break
+            cdf = torch.cumsum(cand[:keep], 0)
+            target = u * float(cdf[-1])
+            pick = int(torch.searchsorted(cdf, torch.tensor(target, dtype=torch.float64), right=True))
+            out[r] = order[min(pick, keep - 1)]
+        return out

@@ -1,0 +1,260 @@
+"""The cache manager.
+
+Layers that ask the same thing of the cache form a group: all keys (PagedKV without a
+window), a window of them (PagedKV with one), or a tensor of fixed size per request
+(SlotState). Each paged group has its own page pool, its own device storage
+[units, 2, pages + 1, kv_heads, page_size, head_dim] and, per live request, its own list of
+pages (the block table row). Pages are given back when the request ends, and, in a
+windowed group, as soon as the window has passed them; given-back pages are handed out
+again first. Every live request also owns a slot, which indexes the fixed-size state
+tensors [units, max_slots, ...] of SlotState groups (zeroed at admission).
+
+The reference keeps per-layer key and value tensors [num_blocks, kv_heads, block_size,
+head_dim] and takes block tables from its caller
+(src/tt_transformers/llm_runtime/paged_kv_cache.py:90-101,159-241); allocation, reuse and
+release per request are this engine's own.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+
+from ..parts.base import PagedKV, PagedKVView, SlotState, SlotStateView
+from .pages import PagePool
+
+
+class OutOfPages(RuntimeError):
+    """A request needs more pages than its group's pool has free."""
+
+    def __init__(self, request_id, group, needed, free):
+        super().__init__(f"request {request_id!r} needs {needed} more pages in cache group {group}, {free} are free")
+        self.request_id, self.group, self.needed, self.free = request_id, group, needed, free
+
+
+class OutOfSlots(RuntimeError):
+    """More requests are live than the engine has slots."""
+
+
+@dataclass
+class _Group:
+    index: int
+    request: object                       # PagedKV or SlotState
+    units: List[int] = field(default_factory=list)     # layer-order entries that own a unit here
+    pool: Optional[PagePool] = None
+    storage: Optional[torch.Tensor] = None
+    table: Optional[np.ndarray] = None    # int32 [max_slots, table_width]: the block table of every slot
+
+
+@dataclass
+class _Live:
+    slot: int
+    length: int = 0                                           # tokens whose keys are cached
+    pages: Dict[int, List[int]] = field(default_factory=dict)  # group -> page of every page index (0: none)
+    reserved_to: int = 0                                      # pages cover positions < reserved_to
+
+
+class CacheManager:
+    def __init__(self, cache_requests, page_size: int, num_pages: int, max_slots: int, max_seq_len: int,
+                 device, dtype: torch.dtype, allocate_storage: bool = True):
+        """cache_requests: per entry of the layer order a PagedKV, a SlotState, None, or the
+        index of the entry whose unit it reads (as DecoderModel.cache_requests() gives)."""
+        self.page_size, self.num_pages, self.max_slots = int(page_size), int(num_pages), int(max_slots)
+        self.max_seq_len = int(max_seq_len)
+        self.table_width = -(-self.max_seq_len // self.page_size)
+        self.device, self.dtype = device, dtype
+        self.groups: List[_Group] = []
+        self._unit_of_entry: Dict[int, tuple] = {}             # entry -> (group index, unit index)
+        by_request: Dict[object, _Group] = {}
+        for entry, req in enumerate(cache_requests):
+            if req is None or isinstance(req, int):
+                continue
+            if not isinstance(req, (PagedKV, SlotState)):
+                raise TypeError(f"layer-order entry {entry}: unknown cache request {req!r}")
+            if req not in by_request:
+                by_request[req] = _Group(index=len(self.groups), request=req)
+                self.groups.append(by_request[req])
+            group = by_request[req]
+            self._unit_of_entry[entry] = (group.index, len(group.units))
+            group.units.append(entry)
+        for entry, req in enumerate(cache_requests):
+            if isinstance(req, int) and not isinstance(req, bool):
+                if req not in self._unit_of_entry:
+                    raise ValueError(f"layer-order entry {entry} reads the cache of entry {req}, which has none")
+                self._unit_of_entry[entry] = self._unit_of_entry[req]
+        for g in self.groups:
+            if isinstance(g.request, PagedKV):
+                g.pool = PagePool(self.num_pages)
+                g.table = np.zeros((self.max_slots, self.table_width), dtype=np.int32)
+                if allocate_storage:
+                    g.storage = torch.zeros(len(g.units), 2, self.num_pages + 1, g.request.num_kv_heads,
+                                            self.page_size, g.request.head_dim, dtype=dtype, device=device)
+            elif allocate_storage:
+                g.storage = torch.zeros(len(g.units), self.max_slots, *g.request.shape,
+                                        dtype=torch.float32, device=device)
+        self._free_slots = list(range(self.max_slots - 1, -1, -1))
+        self._live: Dict[object, _Live] = {}
+
+    # ------------------------------------------------------------------ requests
+    def is_live(self, request_id) -> bool:
+        return request_id in self._live
+
+    def live_requests(self):
+        return list(self._live)
+
+    def length(self, request_id) -> int:
+        return self._live[request_id].length
+
+    def slot(self, request_id) -> int:
+        return self._live[request_id].slot
+
+    @property
+    def free_slots(self) -> int:
+        return len(self._free_slots)
+
+    def free_pages(self, group: int = None) -> int:
+        """Free pages of one paged group, or the fewest over all paged groups."""
+        pools = [g.pool for g in self.groups if g.pool is not None and (group is None or g.index == group)]
+        return min((p.free_count for p in pools), default=1 << 30)
+
+    def admit(self, request_id) -> int:
+        """Give the request a slot (and zeroed fixed-size state). Raises OutOfSlots."""
+        if request_id in self._live:
+            raise ValueError(f"request {request_id!r} is live already")
+        if not self._free_slots:
+            raise OutOfSlots(f"all {self.max_slots} slots are taken; request {request_id!r} cannot be admitted")
+        slot = self._free_slots.pop()
+        live = _Live(slot=slot)
+        for g in self.groups:
+            if g.pool is not None:
+                live.pages[g.index] = []
+                g.table[slot, :] = 0
+            elif g.storage is not None:
+                g.storage[:, slot].zero_()
+        self._live[request_id] = live
+        return slot
+
+    def pages_needed(self, request_id, new_length: int) -> int:
+        """How many pages (in the most demanding group) reserve(new_length) would take."""
+        live = self._live[request_id]
+        have = -(-live.reserved_to // self.page_size)
+        want = -(-new_length // self.page_size)
+        return max(0, want - have)
+
+    def reserve(self, request_id, new_length: int) -> None:
+        """Make sure pages cover positions below new_length, in every paged group, or take
+        nothing and raise OutOfPages."""
+        live = self._live[request_id]
+        if new_length > self.max_seq_len:
+            raise ValueError(f"request {request_id!r} would hold {new_length} tokens; the limit is {self.max_seq_len}")
+        have = -(-live.reserved_to // self.page_size)
+        want = -(-new_length // self.page_size)
+        if want <= have:
+            live.reserved_to = max(live.reserved_to, new_length)
+            return
+        need = want - have
+        taken = []
+        for g in self.groups:
+            if g.pool is None:
+                continue
+            pages = g.pool.allocate(need)
+            if pages is None:
+                for gg, pp in taken:
+                    gg.pool.free(pp)
+                raise OutOfPages(request_id, g.index, need, g.pool.free_count)
+            taken.append((g, pages))
+        for g, pages in taken:
+            live.pages[g.index].extend(pages)
+            g.table[live.slot, have:want] = pages
+        live.reserved_to = new_length
+
+    def trim(self, request_id) -> None:
+        """Give back pages that were reserved beyond what the request holds (a step that
+        was reserved for but did not run)."""
+        live = self._live[request_id]
+        keep = -(-live.length // self.page_size)
+        for g in self.groups:
+            if g.pool is None:
+                continue
+            row = live.pages[g.index]
+            extra = [p for p in row[keep:] if p != 0]
+            if extra:
+                g.pool.free(extra)
+            del row[keep:]
+            g.table[live.slot, keep:] = 0
+        live.reserved_to = live.length
+
+    def commit(self, request_id, new_length: int) -> None:
+        """The request now holds new_length tokens. Pages that a window has passed are freed."""
+        live = self._live[request_id]
+        if new_length > live.reserved_to:
+            raise ValueError("commit beyond what was reserved")
+        live.length = new_length
+        for g in self.groups:
+            if g.pool is None or g.request.window is None:
+                continue
+            # the next query sits at position >= new_length and reads keys > position - window
+            first_needed = max(0, new_length - g.request.window + 1)
+            dead = first_needed // self.page_size            # pages wholly below first_needed
+            row = live.pages[g.index]
+            freed = [p for p in row[:dead] if p != 0]
+            if freed:
+                g.pool.free(freed)
+                for i in range(dead):
+                    row[i] = 0
+                g.table[live.slot, :dead] = 0
+
+    def release(self, request_id) -> None:
+        """The request ended: its pages and its slot are given back."""
+        live = self._live.pop(request_id)
+        for g in self.groups:
+            if g.pool is not None:
+                g.pool.free([p for p in live.pages[g.index] if p != 0])
+                g.table[live.slot, :] = 0
+        self._free_slots.append(live.slot)
+
+    # ------------------------------------------------------------------ what a step needs
+    def table_rows(self, group: int, slots: List[int], width: int = None) -> np.ndarray:
+        """Block-table rows of the given slots: int32 [len(slots), width]."""
+        rows = self.groups[group].table[slots]
+        return rows if width is None else rows[:, :width]
+
+    def paged_groups(self):
+        return [g.index for g in self.groups if g.pool is not None]
+
+    def view(self, entry: int, batch):
+        """The cache view of a layer-order entry for this step (None if it has no cache)."""
+        if entry not in self._unit_of_entry:
+            return None
+        gi, unit = self._unit_of_entry[entry]
+        g = self.groups[gi]
+        if g.pool is not None:
+            return PagedKVView(keys=g.storage[unit, 0], values=g.storage[unit, 1],
+                               block_table=batch.block_tables[gi], page_size=self.page_size,
+                               window=g.request.window)
+        return SlotStateView(state=g.storage[unit], slots=batch.seg_slot, slot_list=batch.seg_slot_list)
+
+    # ------------------------------------------------------------------ invariants (tests)
+    def audit(self) -> None:
+        """Every page is free or held by exactly one live request; every slot likewise."""
+        for g in self.groups:
+            if g.pool is None:
+                continue
+            held = [p for live in self._live.values() for p in live.pages[g.index] if p != 0]
+            if len(held) != len(set(held)):
+                raise AssertionError(f"group {g.index}: a page is held twice")
+            if len(held) != g.pool.held_count:
+                raise AssertionError(f"group {g.index}: {g.pool.held_count} pages are out, {len(held)} are accounted for")
+            free = set(g.pool._free)
+            if free & set(held):
+                raise AssertionError(f"group {g.index}: a held page is on the free list")
+            if len(free) != len(g.pool._free):
+                raise AssertionError(f"group {g.index}: a page is on the free list twice")
+        slots = [live.slot for live in self._live.values()]
+        if len(slots) != len(set(slots)) or set(slots) & set(self._free_slots):
+            raise AssertionError("a slot is held twice")
+        if len(slots) + len(self._free_slots) != self.max_slots:
+            raise AssertionError("a slot was lost")

@@ -1,0 +1,152 @@
+// Embedding lookup, residual add + RMSNorm, SwiGLU gate, row gather.
+// The residual stream is float32 in every precision; the sum, the mean of squares
+// and the scaling are computed in float32.
+#include "common.cuh"
+
+// ---------------------------------------------------------------- embedding: out[t, :] = table[ids[t], :] as float32
+template <typename T>
+__global__ void embedding_kernel(const T* __restrict__ table, const int* __restrict__ ids, float* __restrict__ out,
+                                 int width, int vocab, int* __restrict__ status) {
+    const int t = blockIdx.x;
+    const int id = ids[t];
+    if (id < 0 || id >= vocab) {              // never read outside the table: flag it, write zeros
+        if (threadIdx.x == 0) atomicExch(status, 1 + t);
+        for (int c = threadIdx.x; c < width; c += blockDim.x) out[(size_t)t * width + c] = 0.f;
+        return;
+    }
+    const T* row = table + (size_t)id * width;
+    float* dst = out + (size_t)t * width;
+    if ((width & 7) == 0) {
+        for (int c = threadIdx.x * 8; c < width; c += blockDim.x * 8) {
+            float v[8];
+            load8(row + c, v);
+            store8(dst + c, v);
+        }
+    } else {
+        for (int c = threadIdx.x; c < width; c += blockDim.x) dst[c] = to_float(row[c]);
+    }
+}
+
+TTB_EXPORT int ttb_embedding(const void* table, int dtype, const int* ids, float* out, int tokens, int width,
+                             int vocab, int* status, cudaStream_t stream) {
+    if (tokens == 0) return TTB_OK;
+    if (!table || !ids || !out || !status) return TTB_ERR_ARGUMENT;
+    if (!aligned16(table) || !aligned16(out)) return TTB_ERR_ARGUMENT;
+    const int threads = 128;
+    if (dtype == TTB_DTYPE_BF16)
+        embedding_kernel<<<tokens, threads, 0, stream>>>((const __nv_bfloat16*)table, ids, out, width, vocab, status);
+    else if (dtype == TTB_DTYPE_F32)
+        embedding_kernel<<<tokens, threads, 0, stream>>>((const float*)table, ids, out, width, vocab, status);
+    else
+        return TTB_ERR_UNSUPPORTED;
+    return ttb_launch_status();
+}
+
+// ---------------------------------------------------------------- residual += delta; out = rmsnorm(residual) * w
+// One block per row. The summed row is kept in shared memory between the two passes.
+template <typename TD, typename TW, typename TO>
+__global__ void add_rmsnorm_kernel(float* __restrict__ residual, const TD* __restrict__ delta,
+                                   const TW* __restrict__ weight, TO* __restrict__ out, int width, float eps) {
+    extern __shared__ float row[];
+    __shared__ float scratch[32];
+    const size_t base = (size_t)blockIdx.x * width;
+    float sumsq = 0.f;
+    for (int c = threadIdx.x; c < width; c += blockDim.x) {
+        float v = residual[base + c];
+        if (delta != nullptr) {
+            v += to_float(delta[base + c]);
+            residual[base + c] = v;
+        }
+        row[c] = v;
+        sumsq += v * v;
+    }
+    sumsq = block_sum(sumsq, scratch);
+    const float scale = rsqrtf(sumsq / (float)width + eps);
+    for (int c = threadIdx.x; c < width; c += blockDim.x)
+        out[base + c] = from_float<TO>(row[c] * scale * to_float(weight[c]));
+}
+
+template <typename TD, typename TO>
+static int launch_add_rmsnorm(float* residual, const void* delta, const void* weight, int weight_dtype, void* out,
+                              int rows, int width, float eps, cudaStream_t stream) {
+    const int threads = width >= 2048 ? 512 : (width >= 512 ? 256 : 128);
+    const size_t smem = (size_t)width * sizeof(float);
+    if (weight_dtype == TTB_DTYPE_F32) {
+        auto k = add_rmsnorm_kernel<TD, float, TO>;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k<<<rows, threads, smem, stream>>>(residual, (const TD*)delta, (const float*)weight, (TO*)out, width, eps);
+    } else {
+        auto k = add_rmsnorm_kernel<TD, __nv_bfloat16, TO>;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k<<<rows, threads, smem, stream>>>(residual, (const TD*)delta, (const __nv_bfloat16*)weight, (TO*)out, width, eps);
+    }
+    return ttb_launch_status();
+}
+
+// dtype: type of delta and out (the compute dtype). weight_dtype may differ (a weight stored in 32-bit stays so).
+TTB_EXPORT int ttb_add_rmsnorm(float* residual, const void* delta, const void* weight, int weight_dtype, void* out,
+                               int dtype, int rows, int width, float eps, cudaStream_t stream) {
+    if (rows == 0) return TTB_OK;
+    if (!residual || !weight || !out) return TTB_ERR_ARGUMENT;
+    if ((size_t)width * sizeof(float) > 200 * 1024) return TTB_ERR_UNSUPPORTED;  // row must fit shared memory
+    if (weight_dtype != TTB_DTYPE_F32 && weight_dtype != TTB_DTYPE_BF16) return TTB_ERR_UNSUPPORTED;
+    if (dtype == TTB_DTYPE_BF16)
+        return launch_add_rmsnorm<__nv_bfloat16, __nv_bfloat16>(residual, delta, weight, weight_dtype, out, rows, width, eps, stream);
+    if (dtype == TTB_DTYPE_F32)
+        return launch_add_rmsnorm<float, float>(residual, delta, weight, weight_dtype, out, rows, width, eps, stream);
+    return TTB_ERR_UNSUPPORTED;
+}
+
+// ---------------------------------------------------------------- out[t, i] = silu(gate_up[t, i]) * gate_up[t, I + i]
+template <typename T>
+__global__ void swiglu_kernel(const T* __restrict__ gate_up, T* __restrict__ out, int rows, int inter) {
+    const size_t total = (size_t)rows * inter;
+    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+        const size_t t = idx / inter;
+        const int i = (int)(idx - t * inter);
+        const float g = to_float(gate_up[t * 2 * inter + i]);
+        const float u = to_float(gate_up[t * 2 * inter + inter + i]);
+        const float s = g / (1.f + expf(-g));
+        out[idx] = from_float<T>(s * u);
+    }
+}
+
+TTB_EXPORT int ttb_swiglu(const void* gate_up, void* out, int dtype, int rows, int inter, cudaStream_t stream) {
+    if (rows == 0) return TTB_OK;
+    if (!gate_up || !out) return TTB_ERR_ARGUMENT;
+    const size_t total = (size_t)rows * inter;
+    const int threads = 256;
+    const int blocks = (int)((total + threads - 1) / threads < 148 * 16 ? (total + threads - 1) / threads : 148 * 16);
+    if (dtype == TTB_DTYPE_BF16)
+        swiglu_kernel<<<blocks, threads, 0, stream>>>((const __nv_bfloat16*)gate_up, (__nv_bfloat16*)out, rows, inter);
+    else if (dtype == TTB_DTYPE_F32)
+        swiglu_kernel<<<blocks, threads, 0, stream>>>((const float*)gate_up, (float*)out, rows, inter);
+    else
+        return TTB_ERR_UNSUPPORTED;
+    return ttb_launch_status();
+}
+
+// ---------------------------------------------------------------- dst[n, :] = src[rows[n], :], rows of row_bytes bytes
+template <typename U>
+__global__ void gather_rows_kernel(const U* __restrict__ src, const int* __restrict__ rows, U* __restrict__ dst,
+                                   int units_per_row) {
+    const U* s = src + (size_t)rows[blockIdx.x] * units_per_row;
+    U* d = dst + (size_t)blockIdx.x * units_per_row;
+    for (int c = threadIdx.x; c < units_per_row; c += blockDim.x) d[c] = s[c];
+}
+
+TTB_EXPORT int ttb_gather_rows(const void* src, const int* rows, void* dst, int count, int row_bytes,
+                               cudaStream_t stream) {
+    if (count == 0) return TTB_OK;
+    if (!src || !rows || !dst) return TTB_ERR_ARGUMENT;
+    const int threads = 128;
+    if ((row_bytes & 15) == 0 && aligned16(src) && aligned16(dst))
+        gather_rows_kernel<<<count, threads, 0, stream>>>((const uint4*)src, rows, (uint4*)dst, row_bytes / 16);
+    else if ((row_bytes & 3) == 0)
+        gather_rows_kernel<<<count, threads, 0, stream>>>((const uint32_t*)src, rows, (uint32_t*)dst, row_bytes / 4);
+    else if ((row_bytes & 1) == 0)
+        gather_rows_kernel<<<count, threads, 0, stream>>>((const uint16_t*)src, rows, (uint16_t*)dst, row_bytes / 2);
+    else
+        return TTB_ERR_UNSUPPORTED;
+    return ttb_launch_status();
+}

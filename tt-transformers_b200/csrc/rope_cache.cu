@@ -1,0 +1,111 @@
+// Rotation of queries and keys by their positions, fused with the write of keys and
+// values into cache pages. Angles position * inv_freq, their sines and cosines and the
+// rotation itself are float32; accurate sincosf (no fast-math).
+//
+// qkv row layout: [ heads * head_dim | kv_heads * head_dim | kv_heads * head_dim ].
+// Rotation pairs element i with element i + rotary_dim/2 of each head, for i < rotary_dim/2;
+// elements from rotary_dim on are left as they are.
+// Page layout: [num_pages, kv_heads, page_size, head_dim].
+#include "common.cuh"
+
+template <typename T>
+__global__ void rope_kv_write_kernel(T* __restrict__ qkv, const int* __restrict__ positions,
+                                     const int* __restrict__ seg_of_token, const float* __restrict__ inv_freq,
+                                     int rotary_dim, int heads, int kv_heads, int head_dim,
+                                     T* __restrict__ key_pages, T* __restrict__ value_pages,
+                                     const int* __restrict__ block_table, int table_width, int page_size,
+                                     int num_pages, int write_kv, int* __restrict__ status) {
+    extern __shared__ float trig[];  // cos[rotary_dim/2], sin[rotary_dim/2]
+    const int t = blockIdx.x;
+    const int pos = positions[t];
+    const int half_rot = rotary_dim / 2;
+    for (int i = threadIdx.x; i < half_rot; i += blockDim.x) {
+        const float angle = (float)pos * inv_freq[i];
+        float s, c;
+        sincosf(angle, &s, &c);
+        trig[i] = c;
+        trig[half_rot + i] = s;
+    }
+    __syncthreads();
+
+    T* row = qkv + (size_t)t * (heads + 2 * kv_heads) * head_dim;
+    const int half = head_dim / 2;
+
+    // queries: rotate in place
+    for (int w = threadIdx.x; w < heads * half; w += blockDim.x) {
+        const int h = w / half, i = w - h * half;
+        if (i >= half_rot) continue;
+        T* q = row + h * head_dim;
+        const float a = to_float(q[i]), b = to_float(q[i + half_rot]);
+        const float c = trig[i], s = trig[half_rot + i];
+        q[i] = from_float<T>(a * c - b * s);
+        q[i + half_rot] = from_float<T>(b * c + a * s);
+    }
+    if (!write_kv) return;
+
+    const int page_index = pos / page_size;
+    if (page_index >= table_width) {
+        if (threadIdx.x == 0) atomicExch(status, 0x1000000 + t);
+        return;
+    }
+    const int page = block_table[(size_t)seg_of_token[t] * table_width + page_index];
+    if (page < 0 || page >= num_pages) {
+        if (threadIdx.x == 0) atomicExch(status, 0x2000000 + t);
+        return;
+    }
+    const int in_page = pos - page_index * page_size;
+    const T* k_row = row + heads * head_dim;
+    const T* v_row = k_row + kv_heads * head_dim;
+    for (int w = threadIdx.x; w < kv_heads * half; w += blockDim.x) {
+        const int g = w / half, i = w - g * half;
+        const size_t dst = (((size_t)page * kv_heads + g) * page_size + in_page) * head_dim;
+        const T* k = k_row + g * head_dim;
+        const T* v = v_row + g * head_dim;
+        // keys: element i pairs with i + half_rot when i < half_rot; the rest is copied.
+        // Work item i covers elements i and i + half, so that every element is written once.
+        if (i < half_rot) {
+            const float a = to_float(k[i]), b = to_float(k[i + half_rot]);
+            const float c = trig[i], s = trig[half_rot + i];
+            key_pages[dst + i] = from_float<T>(a * c - b * s);
+            key_pages[dst + i + half_rot] = from_float<T>(b * c + a * s);
+        }
+        value_pages[dst + i] = v[i];
+        value_pages[dst + i + half] = v[i + half];
+    }
+    // key elements outside the rotated range [rotary_dim, head_dim) are copied unchanged
+    if (rotary_dim < head_dim) {
+        const int rest = head_dim - rotary_dim;
+        for (int w = threadIdx.x; w < kv_heads * rest; w += blockDim.x) {
+            const int g = w / rest, i = rotary_dim + (w - g * rest);
+            const size_t dst = (((size_t)page * kv_heads + g) * page_size + in_page) * head_dim;
+            key_pages[dst + i] = k_row[g * head_dim + i];
+        }
+    }
+}
+
+TTB_EXPORT int ttb_rope_kv_write(void* qkv, int dtype, const int* positions, const int* seg_of_token,
+                                 const float* inv_freq, int rotary_dim, int tokens, int heads, int kv_heads,
+                                 int head_dim, void* key_pages, void* value_pages, const int* block_table,
+                                 int table_width, int page_size, int num_pages, int write_kv, int* status,
+                                 cudaStream_t stream) {
+    if (tokens == 0) return TTB_OK;
+    if (!qkv || !positions || !status) return TTB_ERR_ARGUMENT;
+    if (write_kv && (!key_pages || !value_pages || !block_table || !seg_of_token)) return TTB_ERR_ARGUMENT;
+    if (head_dim < 2 || (head_dim & 1)) return TTB_ERR_UNSUPPORTED;
+    if (rotary_dim < 0 || rotary_dim > head_dim || (rotary_dim & 1)) return TTB_ERR_UNSUPPORTED;
+    if (rotary_dim > 0 && !inv_freq) return TTB_ERR_ARGUMENT;
+    const int threads = 256;
+    const size_t smem = (size_t)(rotary_dim > 0 ? rotary_dim : 2) * sizeof(float);
+    if (dtype == TTB_DTYPE_BF16)
+        rope_kv_write_kernel<<<tokens, threads, smem, stream>>>(
+            (__nv_bfloat16*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
+            (__nv_bfloat16*)key_pages, (__nv_bfloat16*)value_pages, block_table, table_width, page_size, num_pages,
+            write_kv, status);
+    else if (dtype == TTB_DTYPE_F32)
+        rope_kv_write_kernel<<<tokens, threads, smem, stream>>>(
+            (float*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
+            (float*)key_pages, (float*)value_pages, block_table, table_width, page_size, num_pages, write_kv, status);
+    else
+        return TTB_ERR_UNSUPPORTED;
+    return ttb_launch_status();
+}

@@ -1,0 +1,175 @@
+// Token selection from float32 logits, one block per row.
+//   temperature == 0          the largest logit; among equal ones the lowest token id.
+//   temperature > 0           softmax(logits / temperature) in float32 and an inverse-CDF draw
+//                             with u in [0, 1) taken from (seed, counter) alone, so that a
+//                             request's stream does not depend on its place in the batch.
+//   top_k in 1..SAMPLE_MAX_K  only the k largest logits take part (lowest id first among equal
+//                             ones); they are walked from the largest down.
+//   top_p < 1 (needs top_k)   of those, the low tail whose cumulative probability is <= 1 - top_p
+//                             is left out; the largest always stays.
+#include "common.cuh"
+
+#define SAMPLE_THREADS 1024
+#define SAMPLE_MAX_K 64
+
+__host__ __device__ __forceinline__ float uniform_from(uint64_t seed, uint64_t counter) {
+    uint64_t x = seed ^ (counter + 0x9E3779B97F4A7C15ull);
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    x = x ^ (x >> 31);
+    return (float)(x >> 40) * (1.0f / 16777216.0f);
+}
+
+struct Best {
+    float value;
+    int index;
+};
+__device__ __forceinline__ Best better(Best a, Best b) {   // larger value, then lower index
+    if (b.value > a.value || (b.value == a.value && b.index < a.index)) return b;
+    return a;
+}
+__device__ __forceinline__ Best block_best(Best v, Best* scratch) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Best other;
+        other.value = __shfl_xor_sync(0xffffffffu, v.value, o);
+        other.index = __shfl_xor_sync(0xffffffffu, v.index, o);
+        v = better(v, other);
+    }
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    Best r = (lane < nwarps) ? scratch[lane] : Best{-INFINITY, 0x7fffffff};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Best other;
+        other.value = __shfl_xor_sync(0xffffffffu, r.value, o);
+        other.index = __shfl_xor_sync(0xffffffffu, r.index, o);
+        r = better(r, other);
+    }
+    return r;
+}
+
+__global__ void __launch_bounds__(SAMPLE_THREADS)
+sample_kernel(const float* __restrict__ logits, int ld, int vocab, const float* __restrict__ temperature,
+              const int* __restrict__ top_k, const float* __restrict__ top_p, const long long* __restrict__ seeds,
+              const int* __restrict__ counters, int* __restrict__ out) {
+    __shared__ Best best_scratch[32];
+    __shared__ float sum_scratch[32];
+    __shared__ float chunk_sum[SAMPLE_THREADS];
+    __shared__ float cand_value[SAMPLE_MAX_K];
+    __shared__ int cand_index[SAMPLE_MAX_K];
+    __shared__ int result;
+    const int row = blockIdx.x;
+    const float* l = logits + (size_t)row * ld;
+    const int tid = threadIdx.x;
+
+    Best mine{-INFINITY, 0x7fffffff};
+    for (int i = tid; i < vocab; i += SAMPLE_THREADS) mine = better(mine, Best{l[i], i});
+    const Best top = block_best(mine, best_scratch);
+    const float temp = temperature ? temperature[row] : 0.f;
+    if (!(temp > 0.f)) {
+        if (tid == 0) out[row] = top.index;
+        return;
+    }
+    const float inv_temp = 1.f / temp;
+    const float u = uniform_from((uint64_t)seeds[row], (uint64_t)(uint32_t)counters[row]);
+    int k = top_k ? top_k[row] : 0;
+    if (k > vocab) k = vocab;
+
+    if (k <= 0) {
+        // whole vocabulary: thread `tid` owns the contiguous ids [tid * chunk, (tid + 1) * chunk)
+        const int chunk = (vocab + SAMPLE_THREADS - 1) / SAMPLE_THREADS;
+        const int begin = tid * chunk, end = min(begin + chunk, vocab);
+        float s = 0.f;
+        for (int i = begin; i < end; ++i) s += expf((l[i] - top.value) * inv_temp);
+        chunk_sum[tid] = s;
+        if (tid == 0) result = -1;
+        __syncthreads();
+        if (tid == 0) {   // serial prefix over 1024 chunk sums: same numbers, same order, on every run
+            float running = 0.f;
+            for (int c = 0; c < SAMPLE_THREADS; ++c) {
+                const float before = running;
+                running += chunk_sum[c];
+                chunk_sum[c] = before;
+            }
+            sum_scratch[0] = running;
+        }
+        __syncthreads();
+        const float total = sum_scratch[0];
+        const float target = u * total;
+        const float before = chunk_sum[tid];
+        const float after = (tid + 1 < SAMPLE_THREADS) ? chunk_sum[tid + 1] : total;
+        if (begin < end && target >= before && (target < after || end == vocab)) {
+            float running = before;
+            int pick = -1, last_positive = -1;
+            for (int i = begin; i < end; ++i) {
+                const float p = expf((l[i] - top.value) * inv_temp);
+                running += p;
+                if (p > 0.f) last_positive = i;
+                if (running > target) { pick = i; break; }
+            }
+            if (pick < 0) pick = last_positive;
+            if (pick >= 0) atomicMax(&result, pick);
+        }
+        __syncthreads();
+        if (tid == 0) out[row] = result >= 0 ? result : top.index;
+        return;
+    }
+
+    // the k largest, one block-wide selection per candidate
+    if (k > SAMPLE_MAX_K) k = SAMPLE_MAX_K;
+    Best previous = top;
+    if (tid == 0) { cand_value[0] = top.value; cand_index[0] = top.index; }
+    for (int c = 1; c < k; ++c) {
+        Best m{-INFINITY, 0x7fffffff};
+        for (int i = tid; i < vocab; i += SAMPLE_THREADS) {
+            const float v = l[i];
+            const bool after_previous = v < previous.value || (v == previous.value && i > previous.index);
+            if (after_previous) m = better(m, Best{v, i});
+        }
+        previous = block_best(m, best_scratch);
+        if (tid == 0) { cand_value[c] = previous.value; cand_index[c] = previous.index; }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float prob[SAMPLE_MAX_K];
+        float total = 0.f;
+        for (int c = 0; c < k; ++c) { prob[c] = expf((cand_value[c] - top.value) * inv_temp); total += prob[c]; }
+        int keep = k;
+        const float p_limit = top_p ? top_p[row] : 1.f;
+        if (p_limit < 1.f) {
+            float tail = 0.f;
+            for (int c = k - 1; c >= 1; --c) {
+                tail += prob[c] / total;
+                if (tail <= 1.f - p_limit) keep = c; else break;
+            }
+        }
+        float kept_total = 0.f;
+        for (int c = 0; c < keep; ++c) kept_total += prob[c];
+        const float target = u * kept_total;
+        float running = 0.f;
+        int pick = cand_index[keep - 1];
+        for (int c = 0; c < keep; ++c) {
+            running += prob[c];
+            if (running > target) { pick = cand_index[c]; break; }
+        }
+        out[row] = pick;
+    }
+}
+
+TTB_EXPORT int ttb_sample(const float* logits, int ld, int rows, int vocab, const float* temperature,
+                          const int* top_k, const float* top_p, const long long* seeds, const int* counters,
+                          int* out, cudaStream_t stream) {
+    if (rows == 0) return TTB_OK;
+    if (!logits || !out || vocab < 1) return TTB_ERR_ARGUMENT;
+    if (temperature && (!seeds || !counters)) return TTB_ERR_ARGUMENT;
+    sample_kernel<<<rows, SAMPLE_THREADS, 0, stream>>>(logits, ld, vocab, temperature, top_k, top_p, seeds, counters, out);
+    return ttb_launch_status();
+}
+
+TTB_EXPORT int ttb_sample_max_top_k() { return SAMPLE_MAX_K; }
+TTB_EXPORT float ttb_sample_uniform(long long seed, int counter) {
+    return uniform_from((uint64_t)seed, (uint64_t)(uint32_t)counter);
+}

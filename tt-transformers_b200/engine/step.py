@@ -1,0 +1,226 @@
+"""The step function: one batch of (request, its next tokens) through the model.
+
+A step takes, for each request in it, the request's next tokens (a portion of its prompt,
+cut anywhere, or one decoded token) and the places among them whose logits are wanted.
+All entries run as one flat batch: the tokens' keys and values are written into the cache
+pages, every token attends to what its request holds in the cache, and float32 logits come
+back for the wanted places, in the order of the entries and of `want`. Nothing else is
+kept between steps.
+
+The reference has two entry points instead, a padded prefill wave or chunk and a
+full-lane decode step, and never mixes them (src/tt_transformers/llm_runtime/execution.py:121-222;
+src/tt_transformers/llm_runtime/prefill/plan.py:22-100; src/tt_transformers/llm_runtime/decode.py:1040-1060).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from ..cache import CacheManager, OutOfPages
+from ..config.base import read_config_json
+from ..config.engine import EngineConfig
+from ..parts import DecoderModel, Runtime, StepBatch
+from ..registry import architecture_of, get_architecture
+from ..weights.loader import check_tensors, read_safetensors
+
+_DTYPES = {"bfloat16": torch.bfloat16, "float32": torch.float32}
+
+
+@dataclass
+class StepEntry:
+    request_id: object
+    tokens: Sequence[int]
+    want: Sequence[int] = field(default_factory=list)     # offsets into `tokens`
+
+
+def _round4(n: int) -> int:
+    return (n + 3) & ~3
+
+
+class Engine:
+    def __init__(self, model: DecoderModel, runtime: Runtime, config: EngineConfig):
+        self.model, self.runtime, self.config = model, runtime, config
+        self.kernels = runtime.kernels
+        self.vocab_size = model.spec.vocab_size
+        self.max_seq_len = min(config.max_seq_len, model.spec.max_positions)
+        self.cache = CacheManager(model.cache_requests(), config.page_size, config.resolved_num_pages(),
+                                  config.max_batch_size, self.max_seq_len, runtime.device, runtime.dtype)
+        self._pinned = runtime.device.type == "cuda"
+        self._staging = [None, None]          # two host buffers in turn, each with the event of its last copy
+        self._staging_events = [None, None]
+        self._staging_turn = 0
+        self.steps_run = 0
+
+    # ------------------------------------------------------------------ requests
+    def admit(self, request_id) -> None:
+        self.cache.admit(request_id)
+
+    def finish(self, request_id) -> None:
+        """The request is over: what it holds is given back."""
+        self.cache.release(request_id)
+
+    def context_length(self, request_id) -> int:
+        return self.cache.length(request_id)
+
+    # ------------------------------------------------------------------ the batch
+    def _stage(self, count: int) -> torch.Tensor:
+        """A pinned host buffer that no copy in flight still reads."""
+        self._staging_turn ^= 1
+        i = self._staging_turn
+        if self._staging_events[i] is not None:
+            self._staging_events[i].synchronize()
+        if self._staging[i] is None or self._staging[i].numel() < count:
+            self._staging[i] = torch.empty(max(count, 4096), dtype=torch.int32, pin_memory=self._pinned)
+        return self._staging[i][:count]
+
+    def _to_device(self, host: torch.Tensor) -> torch.Tensor:
+        if not self._pinned:
+            return host.clone()
+        dev = host.to(self.runtime.device, non_blocking=True)
+        if self._staging_events[self._staging_turn] is None:
+            self._staging_events[self._staging_turn] = torch.cuda.Event()
+        self._staging_events[self._staging_turn].record()
+        return dev
+
+    def build_batch(self, entries: List[StepEntry], table_width: Optional[int] = None) -> StepBatch:
+        """Host lists -> one packed int32 buffer -> one copy to the device -> StepBatch."""
+        cache = self.cache
+        seg_lens = [len(e.tokens) for e in entries]
+        seg_pos0 = [cache.length(e.request_id) for e in entries]
+        seg_slot = [cache.slot(e.request_id) for e in entries]
+        T, R = sum(seg_lens), len(entries)
+        want_rows, base = [], 0
+        for e, n in zip(entries, seg_lens):
+            for w in e.want:
+                if not 0 <= w < n:
+                    raise ValueError(f"request {e.request_id!r}: wanted place {w} is outside its {n} tokens")
+                want_rows.append(base + w)
+            base += n
+        N = len(want_rows)
+        max_context = max(p + n for p, n in zip(seg_pos0, seg_lens))
+        groups = cache.paged_groups()
+        W = table_width or max(1, -(-max_context // cache.page_size))
+
+        o_tok, o_pos, o_seg = 0, _round4(T), 2 * _round4(T)
+        o_cu = 3 * _round4(T)
+        o_p0 = o_cu + _round4(R + 1)
+        o_slot = o_p0 + _round4(R)
+        o_want = o_slot + _round4(R)
+        o_tab = o_want + _round4(max(N, 1))
+        total = o_tab + len(groups) * _round4(R * W)
+        host = self._stage(total)
+        buf = host.numpy()
+        tokens = np.fromiter((t for e in entries for t in e.tokens), dtype=np.int64, count=T)
+        if T and (tokens.min() < 0 or tokens.max() >= self.vocab_size):
+            raise ValueError(f"a token id lies outside the vocabulary of {self.vocab_size}")
+        buf[o_tok:o_tok + T] = tokens
+        lens = np.asarray(seg_lens, dtype=np.int32)
+        cu = np.zeros(R + 1, dtype=np.int32)
+        np.cumsum(lens, out=cu[1:])
+        seg_ids = np.repeat(np.arange(R, dtype=np.int32), lens)
+        pos0 = np.asarray(seg_pos0, dtype=np.int32)
+        buf[o_seg:o_seg + T] = seg_ids
+        buf[o_pos:o_pos + T] = np.arange(T, dtype=np.int32) - cu[:-1][seg_ids] + pos0[seg_ids]
+        buf[o_cu:o_cu + R + 1] = cu
+        buf[o_p0:o_p0 + R] = pos0
+        buf[o_slot:o_slot + R] = seg_slot
+        buf[o_want:o_want + N] = want_rows
+        for i, g in enumerate(groups):
+            start = o_tab + i * _round4(R * W)
+            buf[start:start + R * W] = cache.table_rows(g, seg_slot, W).reshape(-1)
+        dev = self._to_device(host)
+        batch = StepBatch(
+            num_tokens=T, num_segments=R,
+            token_ids=dev[o_tok:o_tok + T], positions=dev[o_pos:o_pos + T], seg_of_token=dev[o_seg:o_seg + T],
+            cu_seqlens=dev[o_cu:o_cu + R + 1], seg_pos0=dev[o_p0:o_p0 + R], seg_slot=dev[o_slot:o_slot + R],
+            want_rows=dev[o_want:o_want + N], num_wanted=N,
+            seg_lens=seg_lens, seg_pos0_list=seg_pos0, seg_slot_list=seg_slot,
+            max_seg_len=max(seg_lens), max_context=max_context,
+        )
+        for i, g in enumerate(groups):
+            start = o_tab + i * _round4(R * W)
+            batch.block_tables[g] = dev[start:start + R * W].view(R, W)
+        return batch
+
+    # ------------------------------------------------------------------ the step
+    def step(self, entries: List[StepEntry]) -> torch.Tensor:
+        """Run the entries' tokens as one batch. Returns float32 logits [wanted, vocab] on
+        the device. Raises OutOfPages (nothing was taken or run) if the pages do not suffice."""
+        if not entries:
+            return torch.empty(0, self.vocab_size, dtype=torch.float32, device=self.runtime.device)
+        seen = set()
+        for e in entries:
+            if len(e.tokens) < 1:
+                raise ValueError(f"request {e.request_id!r} brings no tokens")
+            if e.request_id in seen:
+                raise ValueError(f"request {e.request_id!r} appears twice in one step")
+            seen.add(e.request_id)
+        total = sum(len(e.tokens) for e in entries)
+        if total > self.config.max_step_tokens:
+            raise ValueError(f"the step holds {total} tokens; the budget is {self.config.max_step_tokens}")
+        admitted = []
+        try:
+            for e in entries:
+                if not self.cache.is_live(e.request_id):
+                    self.cache.admit(e.request_id)
+                    admitted.append(e.request_id)
+            for e in entries:
+                self.cache.reserve(e.request_id, self.cache.length(e.request_id) + len(e.tokens))
+        except Exception:
+            for e in entries:                 # nothing of this step stays taken
+                if e.request_id in admitted:
+                    self.cache.release(e.request_id)
+                elif self.cache.is_live(e.request_id):
+                    self.cache.trim(e.request_id)
+            raise
+        batch = self.build_batch(entries)
+        logits = self.model.forward(batch, self.cache)
+        for e in entries:
+            self.cache.commit(e.request_id, self.cache.length(e.request_id) + len(e.tokens))
+        self.steps_run += 1
+        return logits
+
+    def close(self) -> None:
+        for rid in self.cache.live_requests():
+            self.cache.release(rid)
+        for g in self.cache.groups:
+            g.storage = None
+
+
+def build_engine(model_folder: str = None, engine_config: EngineConfig = None, *, config_dict: dict = None,
+                 tensors: Dict[str, torch.Tensor] = None, kernels=None, n_layers: int = None) -> Engine:
+    """From a model folder (config.json + safetensors), or from a configuration dictionary
+    and tensors held in memory, to an engine ready to step. The model class is chosen by
+    config.json's `architectures`. `kernels` None loads the CUDA kernel table of the
+    engine's device; there is no other implementation in this package."""
+    engine_config = engine_config or EngineConfig()
+    if model_folder is not None:
+        config_dict = read_config_json(model_folder)
+    elif config_dict is None or tensors is None:
+        raise ValueError("give a model folder, or config_dict and tensors")
+    arch = get_architecture(architecture_of(config_dict))
+    cfg = arch.load_config(config_dict)
+    if n_layers is not None:
+        cfg = cfg.with_layers(n_layers)
+    model = DecoderModel(arch.model_spec(cfg))
+    specs = model.tensor_specs()
+    if model_folder is not None:
+        tensors = read_safetensors(model_folder, wanted=[s.name for s in specs] if n_layers is not None else None)
+    if n_layers is not None:
+        # a model cut to its first layers leaves the other layers' tensors unused on purpose
+        check_tensors(tensors, specs, ignorable=lambda name: True)
+    else:
+        check_tensors(tensors, specs, ignorable=lambda name: arch.ignorable(cfg, name))
+    device = torch.device(engine_config.device)
+    if kernels is None:
+        from ..kernels import load_kernels
+        kernels = load_kernels(device)
+    runtime = Runtime(kernels=kernels, device=device, dtype=_DTYPES[engine_config.dtype])
+    model.bind(tensors, runtime)
+    engine = Engine(model, runtime, engine_config)
+    engine.model_config = cfg
+    return engine

@@ -1,0 +1,222 @@
+"""The kernel table: Python entry points of the hand-written CUDA kernels.
+
+`CudaKernels` loads the shared library that `build.py` compiles from csrc/ and calls
+its C entry points with raw device pointers on torch's current stream. There is no
+other implementation behind it: without a CUDA device, nvcc or the library, creating
+it raises.
+
+Library matrix products (cuBLAS through torch.mm) stand in for the large bfloat16
+products of prefill, where the reference's engine calls its own library's linear op
+(src/tt_transformers/modules/attention/attention_1d.py:507-514,
+src/tt_transformers/modules/mlp/mlp_1d.py:240-294). Everything else is ours.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from .build import BuildError, build
+
+_F32, _BF16 = 0, 1
+
+
+class KernelError(RuntimeError):
+    """A kernel refused its arguments or the launch failed."""
+
+
+class EngineDeviceError(RuntimeError):
+    """A kernel met an index outside its tables (token id, page id) and skipped the access."""
+
+
+def _dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.float32:
+        return _F32
+    if dtype == torch.bfloat16:
+        return _BF16
+    raise KernelError(f"kernels take float32 or bfloat16 tensors, not {dtype}")
+
+
+_ERRORS = {-2: "unsupported size or option", -3: "bad argument (null pointer, alignment or contradiction)"}
+
+
+class CudaKernels:
+    """All kernels of the engine, on one CUDA device."""
+
+    name = "cuda"
+    # bfloat16 products with more rows than this go to the library; fewer rows stream the
+    # weights through the hand-written skinny kernel.
+    SKINNY_ROWS = 8
+
+    def __init__(self, device: torch.device):
+        if not torch.cuda.is_available():
+            raise KernelError("no CUDA device is available; this engine has no CPU implementation")
+        self.device = torch.device(device)
+        try:
+            path = build()
+        except BuildError as e:
+            raise KernelError(f"the CUDA kernel library could not be built: {e}") from e
+        try:
+            self.lib = ctypes.CDLL(path)
+        except OSError as e:
+            raise KernelError(f"the CUDA kernel library {path} could not be loaded: {e}") from e
+        self.library_path = path
+        for name in ("ttb_embedding", "ttb_add_rmsnorm", "ttb_swiglu", "ttb_gather_rows", "ttb_rope_kv_write",
+                     "ttb_paged_attention_generic", "ttb_gemm_simt", "ttb_gemv", "ttb_sample"):
+            getattr(self.lib, name).restype = ctypes.c_int
+        self.lib.ttb_sample_uniform.restype = ctypes.c_float
+        self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
+        self.lib.ttb_sample_max_top_k.restype = ctypes.c_int
+        self.max_top_k = int(self.lib.ttb_sample_max_top_k())
+        with torch.cuda.device(self.device):
+            self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.launches = 0     # how many of our kernels were launched (counted for reports)
+
+    # ------------------------------------------------------------------ helpers
+    @staticmethod
+    def _p(t: Optional[torch.Tensor]):
+        return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+    def _stream(self):
+        return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def _check(self, code: int, what: str):
+        self.launches += 1
+        if code != 0:
+            reason = _ERRORS.get(code, f"CUDA error {code}")
+            raise KernelError(f"{what}: {reason}")
+
+    def check_status(self):
+        """Raise if a kernel flagged an index outside its tables since the last check.
+        Synchronises with the device."""
+        value = int(self.status.item())
+        if value != 0:
+            self.status.zero_()
+            kind = value >> 24
+            where = value & 0xFFFFFF
+            what = {0: f"token id out of range at token {where - 1}",
+                    1: f"position beyond the block table at token {where}",
+                    2: f"page id out of range at token {where}"}.get(kind, f"code {value}")
+            raise EngineDeviceError(what)
+
+    # ------------------------------------------------------------------ elementwise
+    def embedding(self, table: torch.Tensor, token_ids: torch.Tensor) -> torch.Tensor:
+        tokens, (vocab, width) = token_ids.shape[0], table.shape
+        out = torch.empty(tokens, width, dtype=torch.float32, device=self.device)
+        self._check(self.lib.ttb_embedding(self._p(table), _dtype_code(table.dtype), self._p(token_ids), self._p(out),
+                                           tokens, width, vocab, self._p(self.status), self._stream()), "embedding")
+        return out
+
+    def add_rmsnorm(self, residual: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Tensor, eps: float,
+                    out_dtype: torch.dtype) -> torch.Tensor:
+        rows, width = residual.shape
+        if residual.dtype != torch.float32:
+            raise KernelError("the residual stream is float32")
+        if delta is not None and (delta.dtype != out_dtype or delta.shape != residual.shape):
+            raise KernelError("add_rmsnorm: delta must have the compute dtype and the residual's shape")
+        out = torch.empty(rows, width, dtype=out_dtype, device=self.device)
+        self._check(self.lib.ttb_add_rmsnorm(self._p(residual), self._p(delta), self._p(weight),
+                                             _dtype_code(weight.dtype), self._p(out), _dtype_code(out_dtype), rows,
+                                             width, ctypes.c_float(eps), self._stream()), "add_rmsnorm")
+        return out
+
+    def swiglu(self, gate_up: torch.Tensor) -> torch.Tensor:
+        rows, two_inter = gate_up.shape
+        inter = two_inter // 2
+        out = torch.empty(rows, inter, dtype=gate_up.dtype, device=self.device)
+        self._check(self.lib.ttb_swiglu(self._p(gate_up), self._p(out), _dtype_code(gate_up.dtype), rows, inter,
+                                        self._stream()), "swiglu")
+        return out
+
+    def gather_rows(self, x: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
+        count = rows.shape[0]
+        out = torch.empty(count, x.shape[1], dtype=x.dtype, device=self.device)
+        self._check(self.lib.ttb_gather_rows(self._p(x), self._p(rows), self._p(out), count,
+                                             x.shape[1] * x.element_size(), self._stream()), "gather_rows")
+        return out
+
+    # ------------------------------------------------------------------ matrix products
+    def linear(self, x: torch.Tensor, w: torch.Tensor, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        """x [M, K] times w [N, K] transposed -> [M, N]."""
+        M, K = x.shape
+        N = w.shape[0]
+        out_dtype = out_dtype or x.dtype
+        if w.shape[1] != K or x.dtype != w.dtype:
+            raise KernelError(f"linear: x {tuple(x.shape)} {x.dtype} does not match w {tuple(w.shape)} {w.dtype}")
+        if x.stride(1) != 1 or w.stride(1) != 1:
+            raise KernelError("linear: operands must be contiguous along K")
+        if M <= self.SKINNY_ROWS:
+            out = torch.empty(M, N, dtype=out_dtype, device=self.device)
+            self._check(self.lib.ttb_gemv(self._p(x), self._p(w), self._p(out), _dtype_code(x.dtype),
+                                          _dtype_code(out_dtype), M, N, K, x.stride(0), w.stride(0), N,
+                                          self._stream()), "gemv")
+            return out
+        if x.dtype == torch.bfloat16:
+            # library product (cuBLAS), float32 accumulation
+            if out_dtype == torch.bfloat16:
+                return torch.mm(x, w.t())
+            return torch.mm(x, w.t(), out_dtype=out_dtype)
+        out = torch.empty(M, N, dtype=out_dtype, device=self.device)
+        self._check(self.lib.ttb_gemm_simt(self._p(x), self._p(w), self._p(out), _dtype_code(x.dtype),
+                                           _dtype_code(out_dtype), M, N, K, x.stride(0), w.stride(0), N,
+                                           self._stream()), "gemm_simt")
+        return out
+
+    # ------------------------------------------------------------------ attention
+    def rope_kv_write(self, qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True):
+        tokens = qkv.shape[0]
+        if qkv.shape[1] != (heads + 2 * kv_heads) * head_dim or not qkv.is_contiguous():
+            raise KernelError("rope_kv_write: qkv must be contiguous [tokens, (heads + 2 kv_heads) * head_dim]")
+        num_pages = view.keys.shape[0] if view is not None else 0
+        self._check(self.lib.ttb_rope_kv_write(
+            self._p(qkv), _dtype_code(qkv.dtype), self._p(batch.positions), self._p(batch.seg_of_token),
+            self._p(inv_freq), int(rotary_dim), tokens, heads, kv_heads, head_dim,
+            self._p(view.keys if view is not None else None), self._p(view.values if view is not None else None),
+            self._p(view.block_table if view is not None else None),
+            view.block_table.shape[1] if view is not None else 0, view.page_size if view is not None else 1,
+            num_pages, 1 if (write_kv and view is not None) else 0, self._p(self.status), self._stream()),
+            "rope_kv_write")
+
+    def paged_attention(self, qkv, batch, heads, kv_heads, head_dim, scale, view) -> torch.Tensor:
+        tokens = qkv.shape[0]
+        out = torch.empty(tokens, heads * head_dim, dtype=qkv.dtype, device=self.device)
+        if view.keys.dtype != qkv.dtype:
+            raise KernelError("paged_attention: cache pages and queries differ in dtype")
+        self._check(self.lib.ttb_paged_attention_generic(
+            self._p(qkv), qkv.stride(0), self._p(out), _dtype_code(qkv.dtype), self._p(batch.positions),
+            self._p(batch.seg_of_token), self._p(view.keys), self._p(view.values), self._p(view.block_table),
+            view.block_table.shape[1], view.page_size, tokens, heads, kv_heads, head_dim, ctypes.c_float(scale),
+            int(view.window or 0), self._stream()), "paged_attention")
+        return out
+
+    # ------------------------------------------------------------------ sampling
+    def sample(self, logits, temperature=None, top_k=None, top_p=None, seeds=None, counters=None) -> torch.Tensor:
+        """One token per row of float32 logits. temperature None: argmax everywhere."""
+        rows, vocab = logits.shape
+        if logits.dtype != torch.float32 or logits.stride(1) != 1:
+            raise KernelError("sample: logits must be float32, contiguous along the vocabulary")
+        out = torch.empty(rows, dtype=torch.int32, device=self.device)
+        self._check(self.lib.ttb_sample(self._p(logits), logits.stride(0), rows, vocab, self._p(temperature),
+                                        self._p(top_k), self._p(top_p), self._p(seeds), self._p(counters),
+                                        self._p(out), self._stream()), "sample")
+        return out
+
+    def uniform(self, seed: int, counter: int) -> float:
+        """The number in [0, 1) that the sampler draws for (seed, counter); host copy of the device function."""
+        return float(self.lib.ttb_sample_uniform(ctypes.c_longlong(seed), int(counter)))
+
+
+_CACHE = {}
+
+
+def load_kernels(device) -> CudaKernels:
+    """The kernel table of `device`, built and loaded on first use."""
+    device = torch.device(device)
+    if device.type != "cuda":
+        raise KernelError(f"this engine runs on CUDA devices only, not on {device}")
+    key = str(device)
+    if key not in _CACHE:
+        _CACHE[key] = CudaKernels(device)
+    return _CACHE[key]
