@@ -1,0 +1,230 @@
+"""Each CUDA kernel alone against its plain PyTorch twin, at sizes other than the engine's."""
+
+import math
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+from torch_kernels import TorchKernels
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = [torch.float32, torch.bfloat16]
+
+
+@pytest.fixture(scope="module")
+def kernels():
+    from tt_transformers_b200.kernels import load_kernels
+
+    return load_kernels("cuda:0")
+
+
+@pytest.fixture(scope="module")
+def twin():
+    return TorchKernels("cuda:0")
+
+
+def tol(dtype):
+    return 2e-5 if dtype == torch.float32 else 2e-2
+
+
+def close(got, ref, dtype, scale=None):
+    ref = ref.float()
+    err = float((got.float() - ref).abs().max())
+    bound = tol(dtype) * (scale if scale is not None else max(1.0, float(ref.abs().max())))
+    assert err <= bound, f"max error {err} > {bound}"
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("vocab,width,tokens", [(300, 80, 17), (1000, 2048, 5), (77, 9, 3)])
+def test_embedding(kernels, twin, dtype, vocab, width, tokens):
+    g = torch.Generator(device="cuda").manual_seed(0)
+    table = torch.randn(vocab, width, device="cuda", generator=g).to(dtype)
+    ids = torch.randint(0, vocab, (tokens,), device="cuda", generator=g, dtype=torch.int32)
+    assert torch.equal(kernels.embedding(table, ids), twin.embedding(table, ids))
+
+
+def test_embedding_flags_bad_token(kernels):
+    from tt_transformers_b200.kernels import EngineDeviceError
+
+    table = torch.randn(10, 8, device="cuda")
+    out = kernels.embedding(table, torch.tensor([3, 12], device="cuda", dtype=torch.int32))
+    assert torch.equal(out[1], torch.zeros(8, device="cuda"))
+    with pytest.raises(EngineDeviceError):
+        kernels.check_status()
+    kernels.check_status()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,width,eps,wdtype", [(5, 96, 1e-6, None), (33, 2048, 1e-5, torch.float32),
+                                                     (2, 7, 1e-3, None), (3, 8192, 1e-5, None)])
+def test_add_rmsnorm(kernels, twin, dtype, rows, width, eps, wdtype):
+    g = torch.Generator(device="cuda").manual_seed(1)
+    res = torch.randn(rows, width, device="cuda", generator=g) * 3
+    delta = torch.randn(rows, width, device="cuda", generator=g).to(dtype)
+    weight = (1 + 0.1 * torch.randn(width, device="cuda", generator=g)).to(wdtype or dtype)
+    for d in (delta, None):
+        r1, r2 = res.clone(), res.clone()
+        got = kernels.add_rmsnorm(r1, d, weight, eps, dtype)
+        ref = twin.add_rmsnorm(r2, d, weight, eps, torch.float32)
+        close(r1, r2, torch.float32)
+        close(got, ref, dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,inter", [(3, 320), (17, 200), (1, 8192), (64, 13)])
+def test_swiglu(kernels, twin, dtype, rows, inter):
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = (torch.randn(rows, 2 * inter, device="cuda", generator=g) * 3).to(dtype)
+    close(kernels.swiglu(x), twin.swiglu(x.float()), dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("width", [96, 2048, 7])
+def test_gather_rows(kernels, dtype, width):
+    x = torch.randn(20, width, device="cuda").to(dtype)
+    rows = torch.tensor([19, 0, 7, 7, 3], device="cuda", dtype=torch.int32)
+    assert torch.equal(kernels.gather_rows(x, rows), x[rows.long()])
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("M,N,K", [(1, 384, 96), (3, 100, 320), (8, 3072, 2048), (5, 77, 41), (9, 96, 64),
+                                   (50, 320, 96), (130, 200, 80), (64, 257, 1000), (200, 2048, 512)])
+def test_linear(kernels, dtype, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(M, K, device="cuda", generator=g).to(dtype)
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).to(dtype)
+    ref = x.double() @ w.double().t()
+    close(kernels.linear(x, w), ref, dtype)
+    got32 = kernels.linear(x, w, out_dtype=torch.float32)
+    assert got32.dtype == torch.float32
+    close(got32, ref, torch.float32 if dtype == torch.float32 else torch.bfloat16,
+          scale=None if dtype == torch.float32 else 0.05)
+
+
+def make_paged_case(dtype, heads, kv_heads, head_dim, page_size, segments, window=None, seed=0, num_pages=64):
+    """Random qkv for the new tokens of several segments and a cache that already holds
+    each segment's earlier keys and values on shuffled pages."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    T = sum(n for _, n in segments)
+    qkv = torch.randn(T, (heads + 2 * kv_heads) * head_dim, device="cuda", generator=g).to(dtype)
+    keys = torch.randn(num_pages + 1, kv_heads, page_size, head_dim, device="cuda", generator=g).to(dtype)
+    values = torch.randn(num_pages + 1, kv_heads, page_size, head_dim, device="cuda", generator=g).to(dtype)
+    perm = (torch.randperm(num_pages, generator=torch.Generator().manual_seed(seed)) + 1).tolist()
+    W = max(-(-(p + n) // page_size) for p, n in segments)
+    table = torch.zeros(len(segments), W, dtype=torch.int32)
+    for r, (p, n) in enumerate(segments):
+        for i in range(-(-(p + n) // page_size)):
+            table[r, i] = perm.pop()
+    positions = torch.tensor([p + i for p, n in segments for i in range(n)], dtype=torch.int32, device="cuda")
+    seg_of = torch.tensor([r for r, (p, n) in enumerate(segments) for _ in range(n)], dtype=torch.int32, device="cuda")
+    batch = SimpleNamespace(positions=positions, seg_of_token=seg_of, seg_lens=[n for _, n in segments],
+                            seg_pos0_list=[p for p, _ in segments])
+    view = SimpleNamespace(keys=keys, values=values, block_table=table.cuda(), page_size=page_size, window=window)
+    return qkv, batch, view
+
+
+ATTN_CASES = [
+    # heads, kv_heads, head_dim, page_size, segments (cached before, new tokens), window
+    (4, 2, 16, 4, [(0, 7), (13, 1), (5, 3)], None),
+    (3, 1, 32, 8, [(0, 33), (40, 1)], None),
+    (5, 5, 48, 16, [(0, 2), (130, 1), (17, 20), (255, 1)], None),
+    (8, 2, 64, 16, [(300, 1), (0, 140)], None),
+    (2, 1, 128, 16, [(100, 5)], None),
+    (4, 2, 16, 4, [(0, 40), (37, 1), (20, 9)], 11),
+    (6, 3, 80, 8, [(9, 30)], 16),
+]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", ATTN_CASES)
+def test_rope_kv_write_and_attention(kernels, twin, dtype, case):
+    heads, kv_heads, head_dim, page_size, segments, window = case
+    qkv, batch, view = make_paged_case(dtype, heads, kv_heads, head_dim, page_size, segments, window)
+    inv_freq = (1.0 / (10000.0 ** (torch.arange(0, head_dim, 2).float() / head_dim))).cuda()
+    qkv2 = qkv.clone()
+    view2 = SimpleNamespace(keys=view.keys.clone(), values=view.values.clone(), block_table=view.block_table,
+                            page_size=page_size, window=window)
+    kernels.rope_kv_write(qkv, batch, inv_freq, head_dim, heads, kv_heads, head_dim, view, True)
+    twin.rope_kv_write(qkv2, batch, inv_freq, head_dim, heads, kv_heads, head_dim, view2, True)
+    q_cols = heads * head_dim
+    close(qkv[:, :q_cols], qkv2[:, :q_cols], dtype)
+    close(view.keys, view2.keys, dtype)
+    assert torch.equal(view.values, view2.values)
+    scale = head_dim ** -0.5
+    got = kernels.paged_attention(qkv, batch, heads, kv_heads, head_dim, scale, view)
+    ref = twin.paged_attention(qkv2.float(), batch, heads, kv_heads, head_dim, scale,
+                               SimpleNamespace(keys=view2.keys.float(), values=view2.values.float(),
+                                               block_table=view.block_table, page_size=page_size, window=window))
+    close(got, ref, dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_partial_rotation_and_no_rotation(kernels, twin, dtype):
+    heads, kv_heads, head_dim, page_size = 4, 2, 32, 8
+    for rotary_dim in (16, 0):
+        qkv, batch, view = make_paged_case(dtype, heads, kv_heads, head_dim, page_size, [(3, 9), (20, 1)], seed=5)
+        inv_freq = (1.0 / (10000.0 ** (torch.arange(0, max(rotary_dim, 2), 2).float() / max(rotary_dim, 2)))).cuda()
+        qkv2 = qkv.clone()
+        view2 = SimpleNamespace(keys=view.keys.clone(), values=view.values.clone(), block_table=view.block_table,
+                                page_size=page_size, window=None)
+        kernels.rope_kv_write(qkv, batch, inv_freq if rotary_dim else None, rotary_dim, heads, kv_heads, head_dim, view)
+        twin.rope_kv_write(qkv2, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view2)
+        close(qkv[:, :heads * head_dim], qkv2[:, :heads * head_dim], dtype)
+        close(view.keys, view2.keys, dtype)
+        assert torch.equal(view.values, view2.values)
+
+
+def test_attention_finds_a_far_key(kernels):
+    """One key among hundreds is made to stand out; the output must be its value."""
+    heads, kv_heads, head_dim, page_size = 2, 1, 64, 16
+    for dtype in DTYPES:
+        for far in (0, 15, 16, 127, 128, 129, 383, 500):
+            qkv, batch, view = make_paged_case(dtype, heads, kv_heads, head_dim, page_size, [(511, 1)], seed=far)
+            q = torch.zeros(head_dim, device="cuda")
+            q[3] = 40.0
+            qkv.view(1, heads + 2, head_dim)[0, :heads] = q.to(dtype)
+            page = int(view.block_table[0, far // page_size])
+            view.keys[:, :, :, 3] = 0
+            view.keys[page, 0, far % page_size, 3] = 40.0
+            got = kernels.paged_attention(qkv, batch, heads, kv_heads, head_dim, 1.0, view)
+            want = view.values[page, 0, far % page_size].float()
+            for h in range(heads):
+                close(got.view(heads, head_dim)[h], want, dtype)
+
+
+@pytest.mark.parametrize("vocab,rows", [(384, 5), (128256, 3), (1000, 64), (33, 2)])
+def test_sample(kernels, twin, vocab, rows):
+    g = torch.Generator(device="cuda").manual_seed(4)
+    logits = torch.randn(rows, vocab, device="cuda", generator=g) * 3
+    logits[0, 7] = logits[0, 20] = logits[0].max() + 1      # equal maxima: the lower id wins
+    assert torch.equal(kernels.sample(logits).cpu(), twin.sample(logits).cpu())
+    assert int(kernels.sample(logits)[0]) == 7
+    temperature = torch.full((rows,), 0.8, device="cuda")
+    temperature[-1] = 0.0
+    seeds = torch.arange(rows, device="cuda", dtype=torch.int64) * 7919 + 1
+    for counter in range(4):
+        counters = torch.full((rows,), counter, device="cuda", dtype=torch.int32)
+        for top_k, top_p in ((0, 1.0), (5, 1.0), (40, 0.7), (1, 1.0), (64, 0.2)):
+            k = torch.full((rows,), top_k, device="cuda", dtype=torch.int32)
+            p = torch.full((rows,), top_p, device="cuda")
+            got = kernels.sample(logits, temperature, k, p, seeds, counters).cpu()
+            ref = twin.sample(logits, temperature, k, p, seeds, counters).cpu()
+            agree = (got == ref).float().mean()
+            # a draw that lands within rounding of a bin edge may fall either way
+            assert agree >= 0.9, (top_k, top_p, got.tolist(), ref.tolist())
+    for s, c in ((0, 0), (1, 5), (2 ** 40 + 3, 77)):
+        assert abs(kernels.uniform(s, c) - twin.uniform(s, c)) < 1e-7
+
+
+def test_sample_distribution(kernels):
+    """Draws over many counters follow softmax(logits / temperature)."""
+    logits = torch.tensor([[0.0, 1.0, 2.0, 3.0, -50.0]], device="cuda").repeat(4096, 1)
+    temperature = torch.full((4096,), 1.5, device="cuda")
+    seeds = torch.full((4096,), 1234, device="cuda", dtype=torch.int64)
+    counters = torch.arange(4096, device="cuda", dtype=torch.int32)
+    got = kernels.sample(logits, temperature, None, None, seeds, counters)
+    freq = torch.bincount(got.long().cpu(), minlength=5).float() / 4096
+    expect = torch.softmax(logits[0].cpu() / 1.5, 0)
+    assert float((freq - expect).abs().max()) < 0.03
