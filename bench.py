@@ -1,0 +1,285 @@
+"""bench.py --gpus 1 --steps K --warmup W: decode and prefill throughput of the engine.
+
+The model has the layer sizes of Llama 3.2 1B with random weights. The headline `value` is
+decoded tokens per second at batch 8 with every request holding about `context` tokens; a
+"step" is one decode step. It prints ONE JSON line. The engine runs on one GPU: for
+--gpus N > 1 it prints one line that says so and exits with 2.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MODEL_1B = {
+    "architectures": ["LlamaForCausalLM"],
+    "hidden_size": 2048, "num_hidden_layers": 16, "num_attention_heads": 32, "num_key_value_heads": 8,
+    "head_dim": 64, "intermediate_size": 8192, "vocab_size": 128256, "rms_norm_eps": 1e-5,
+    "max_position_embeddings": 131072, "rope_theta": 500000.0,
+    "rope_scaling": {"rope_type": "llama3", "factor": 32.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                     "original_max_position_embeddings": 8192},
+    "tie_word_embeddings": True,
+}
+FULL_LAYERS = 16
+PAGE = 16
+PREFILL_TOKENS = 2048
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.isfile(path):
+        with open(path) as f:
+            data = json.load(f)
+        return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]), "source": "measured"}
+    return {**FALLBACK_PEAKS, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi in the background while the timed region runs (reading only)."""
+
+    QUERY = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", "0", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.summary = {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        clocks, reasons, max_clock = [], set(), None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 6:
+                continue
+            try:
+                clocks.append(float(parts[0]))
+                max_clock = float(parts[1])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[2:6]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if clocks:
+            self.summary = {"sm_mhz": statistics.median(clocks), "sm_max_mhz": max_clock, "reasons": sorted(reasons)}
+
+
+def decode_bytes(cfg, layers, batch, context, elem=2):
+    """Bytes a decode step has to read: every weight it uses once, and the cache of the live requests."""
+    d, inter, vocab = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    heads, kv, hd = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
+    per_layer = (heads + 2 * kv) * hd * d + heads * hd * d + 3 * inter * d + 2 * d
+    weights = (layers * per_layer + vocab * d + d) * elem
+    cache = batch * context * layers * 2 * kv * hd * elem
+    return weights + cache
+
+
+def prefill_flops(cfg, layers, tokens):
+    d, inter, vocab = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    heads, kv, hd = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
+    linear = 2 * tokens * ((heads + 2 * kv) * hd * d + heads * hd * d + 3 * inter * d)
+    attention = 2 * 2 * heads * hd * tokens * (tokens + 1) / 2      # causal QK^T and PV
+    return layers * (linear + attention) + 2 * vocab * d            # plus one row of logits
+
+
+def main(argv=None) -> int:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=64)
+    parser.add_argument("--warmup", type=int, default=8)
+    parser.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    parser.add_argument("--batch", type=int, default=8)
+    parser.add_argument("--context", type=int, default=8192)
+    parser.add_argument("--layers", type=int, default=FULL_LAYERS)
+    parser.add_argument("--points", default="1,64", help="other decode batch sizes to report, comma separated")
+    parser.add_argument("--fill", default="prefill", choices=("prefill", "synthetic"),
+                        help="how the cache gets its context before decoding: through the engine's own prefill, "
+                             "or filled with random numbers (faster; decode time does not depend on the values)")
+    args = parser.parse_args(argv)
+
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "the reference runs only on its vendor's accelerator library (ttnn), which is not "
+                          "installed here and has no CUDA backend"}))
+        return 0
+    if args.gpus != 1:
+        print(f"bench.py: this engine runs on one GPU; --gpus {args.gpus} is not supported")
+        return 2
+    warmup = max(args.warmup, 3)
+
+    import torch
+
+    from tt_transformers_b200.config import EngineConfig
+    from tt_transformers_b200.engine.llm import LLM
+    from tt_transformers_b200.engine.step import StepEntry, build_engine
+    from tt_transformers_b200.sampling import SamplingParams
+    from tt_transformers_b200.weights import random_tensors
+
+    cfg = dict(MODEL_1B, num_hidden_layers=args.layers)
+    pk = peaks()
+    device = "cuda:0"
+    torch.cuda.set_device(0)
+    point_batches = [int(x) for x in args.points.split(",") if x]
+    max_batch = max([args.batch] + point_batches)
+    tensors = random_tensors(cfg, seed=0, dtype=torch.bfloat16, device=device)
+    pages_per_request = -(-args.context // PAGE)
+    engine = build_engine(config_dict=cfg, tensors=tensors, engine_config=EngineConfig(
+        dtype="bfloat16", page_size=PAGE, num_pages=pages_per_request * max_batch, max_batch_size=max_batch,
+        max_seq_len=args.context, max_step_tokens=PREFILL_TOKENS, max_chunk_tokens=PREFILL_TOKENS, device=device))
+    del tensors
+    llm = LLM(engine)
+    kernels = engine.kernels
+    gen = torch.Generator().manual_seed(0)
+
+    def prompt(n):
+        return torch.randint(0, cfg["vocab_size"], (n,), generator=gen).tolist()
+
+    def timed(fn, reps):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(reps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / reps
+
+    # ------------------------------------------------------------------ prefill of 2,048 tokens, one step
+    pre_tokens = prompt(PREFILL_TOKENS)
+
+    def prefill_once():
+        engine.step([StepEntry("p", pre_tokens, [PREFILL_TOKENS - 1])])
+        engine.finish("p")
+
+    for _ in range(3):
+        prefill_once()
+    prefill_ms = timed(prefill_once, 5)
+    flops = prefill_flops(cfg, args.layers, PREFILL_TOKENS)
+    prefill = {"value": round(PREFILL_TOKENS / prefill_ms * 1e3, 1), "tokens": PREFILL_TOKENS,
+               "ms": round(prefill_ms, 3), "frac": round(flops / (prefill_ms * 1e-3) / (pk["bf16_tflops"] * 1e12), 4)}
+
+    # ------------------------------------------------------------------ decode
+    def fill(batch, length):
+        """`batch` requests that hold `length` tokens each."""
+        ids = [f"d{i}" for i in range(batch)]
+        if args.fill == "synthetic":
+            for rid in ids:
+                engine.cache.admit(rid)
+                engine.cache.reserve(rid, length)
+                engine.cache.commit(rid, length)
+            for g in engine.cache.groups:
+                if g.pool is not None:
+                    g.storage.normal_(0, 1)
+            return ids
+        for rid in ids:
+            toks = prompt(length)
+            for i in range(0, length, PREFILL_TOKENS):
+                engine.step([StepEntry(rid, toks[i:i + PREFILL_TOKENS], [])])
+        return ids
+
+    def decode_run(batch, steps, warm):
+        ids = fill(batch, args.context - steps - warm - 1)
+        state = {"tokens": [1] * batch}
+
+        def one():
+            logits = engine.step([StepEntry(rid, [t], [0]) for rid, t in zip(ids, state["tokens"])])
+            state["tokens"] = kernels.sample(logits).tolist()
+
+        for _ in range(warm):
+            one()
+        before = kernels.launches
+        with ClockSampler() as clocks:
+            ms = timed(one, steps)
+        launches = kernels.launches - before
+        for rid in ids:
+            engine.finish(rid)
+        return ms, launches, clocks.summary
+
+    ms_step, launches, clocks = decode_run(args.batch, args.steps, warmup)
+    value = args.batch / ms_step * 1e3
+    need = decode_bytes(cfg, args.layers, args.batch, args.context)
+    achieved = need / (ms_step * 1e-3) / 1e9
+    points = {}
+    for b in point_batches:
+        ms_b, _, _ = decode_run(b, max(8, args.steps // 2), warmup)
+        points[f"decode_b{b}"] = round(b / ms_b * 1e3, 1)
+
+    # ------------------------------------------------------------------ end to end through the Python entry point
+    params = SamplingParams(temperature=0.0, max_new_tokens=1 << 30, ignore_eos=True)
+    length = args.context - args.steps - warmup - 2
+    if args.fill == "synthetic":
+        reqs = []
+        for i in range(args.batch):       # the prompts' last token goes through the engine; the rest is filled
+            r = llm.add_request(prompt(length), params)
+            reqs.append(r)
+        sched = llm._scheduler
+        for r in list(sched.waiting):
+            sched.waiting.remove(r)
+            engine.cache.admit(r.request_id)
+            engine.cache.reserve(r.request_id, length - 1)
+            engine.cache.commit(r.request_id, length - 1)
+            r.num_computed = length - 1
+            sched.running.append(r)
+    else:
+        for i in range(args.batch):
+            llm.add_request(prompt(length), params)
+        while any(r.num_computed < len(r.prompt) for r in llm._scheduler.running) or llm._scheduler.waiting:
+            llm.step()
+    for _ in range(warmup):
+        llm.step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        llm.step()
+    torch.cuda.synchronize()
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    e2e = {"value": round(args.batch / e2e_ms * 1e3, 1), "unit": "tokens/s",
+           "h2d_bytes_per_step": 4 * (3 * 4 * max(1, args.batch // 4 + (args.batch % 4 > 0)) + 16 + args.batch * pages_per_request),
+           "d2h_bytes_per_step": 4 * args.batch}
+
+    line = {
+        "metric": "decode tokens/s, Llama 3.2 1B sizes, batch 8", "value": round(value, 1), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: random weights N(0, 0.02), uniform-random token ids",
+        "config": {"model": "llama-3.2-1b-sizes", "layers": args.layers, "layers_full": FULL_LAYERS,
+                   "hidden": cfg["hidden_size"], "heads": cfg["num_attention_heads"],
+                   "kv_heads": cfg["num_key_value_heads"], "head_dim": cfg["head_dim"],
+                   "intermediate": cfg["intermediate_size"], "vocab": cfg["vocab_size"], "global_batch": args.batch,
+                   "seq_len": args.context, "page_size": PAGE, "prefill_tokens": PREFILL_TOKENS,
+                   "parallelism": "single-gpu", "cache_fill": args.fill,
+                   "l2": "inputs larger than L2 (weights and cache are re-read every step)",
+                   "peaks": pk["source"]},
+        "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "prefill": prefill,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4)},
+        "points": points,
+    }
+    print(json.dumps(line))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -137,6 +137,16 @@ class CacheManager:
         self._live[request_id] = live
         return slot
 
+    def room(self, request_id=None) -> int:
+        """How many more tokens could be reserved right now: for a live request, beyond what
+        it holds; for None, by a request that is not admitted yet."""
+        P = self.page_size
+        free = self.free_pages() * P
+        if request_id is None:
+            return free
+        live = self._live[request_id]
+        return free + (-(-live.reserved_to // P) * P - live.length)
+
     def pages_needed(self, request_id, new_length: int) -> int:
         """How many pages (in the most demanding group) reserve(new_length) would take."""
         live = self._live[request_id]

@@ -1,0 +1,43 @@
+"""From the logits of a step to one token per request, on the device.
+
+One call of the sampling kernel serves a batch in which every row has its own
+temperature, top_k, top_p, seed and counter. The random number of a row depends only on
+(seed, counter), the counter being the index of the token in the request's output, so a
+request draws the same tokens wherever it sits in a batch and however its prompt was cut
+(the reference's per-request stream: src/tt_transformers/modules/sampling/seed_manager_1d.py:40-55).
+"""
+
+from __future__ import annotations
+
+from typing import List, Sequence
+
+import torch
+
+from .params import SamplingParams
+
+
+class Sampler:
+    def __init__(self, kernels, device):
+        self.kernels, self.device = kernels, torch.device(device)
+        self.max_top_k = int(getattr(kernels, "max_top_k", 64))
+
+    def validate(self, params: SamplingParams) -> None:
+        if params.temperature > 0 and params.top_k > self.max_top_k:
+            raise ValueError(f"top_k must be at most {self.max_top_k} on the device sampler, got {params.top_k}")
+
+    def sample(self, logits: torch.Tensor, params: Sequence[SamplingParams], seeds: Sequence[int],
+               counters: Sequence[int]) -> List[int]:
+        """logits float32 [rows, vocab]; one token id per row, on the host."""
+        rows = logits.shape[0]
+        if rows == 0:
+            return []
+        if all(p.greedy for p in params):
+            return self.kernels.sample(logits).tolist()
+        pinned = self.device.type == "cuda"
+        f = torch.tensor([[p.temperature for p in params], [p.top_p for p in params]], dtype=torch.float32,
+                         pin_memory=pinned).to(self.device, non_blocking=True)
+        i = torch.tensor([[p.top_k for p in params], list(counters)], dtype=torch.int32,
+                         pin_memory=pinned).to(self.device, non_blocking=True)
+        s = torch.tensor([int(x) & 0x7FFFFFFFFFFFFFFF for x in seeds], dtype=torch.int64,
+                         pin_memory=pinned).to(self.device, non_blocking=True)
+        return self.kernels.sample(logits, f[0], i[0], f[1], s, i[1]).tolist()

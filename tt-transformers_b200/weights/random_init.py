@@ -21,22 +21,24 @@ from ..registry import architecture_of, get_architecture
 
 
 def random_tensors(config_dict: dict, seed: int, std: float = 0.02, norm_std: float = 0.0,
-                   dtype: torch.dtype = torch.bfloat16) -> Dict[str, torch.Tensor]:
-    """Matrices ~ N(0, std); vectors (norm weights) 1 + N(0, norm_std)."""
+                   dtype: torch.dtype = torch.bfloat16, device="cpu") -> Dict[str, torch.Tensor]:
+    """Matrices ~ N(0, std); vectors (norm weights) 1 + N(0, norm_std). With a CUDA `device`
+    the numbers are drawn there (other numbers than on the CPU for the same seed): large
+    models for measurements are made in seconds that way."""
     arch = get_architecture(architecture_of(config_dict))
     model = DecoderModel(arch.model_spec(arch.load_config(config_dict)))
-    gen = torch.Generator(device="cpu")
+    gen = torch.Generator(device=device)
     gen.manual_seed(int(seed))
     out = {}
     for spec in model.tensor_specs():
         if spec.kind == "int":
             raise ValueError(f"{spec.name}: random integer tables are not defined")
         if len(spec.shape) == 1:
-            t = torch.ones(spec.shape, dtype=torch.float32)
+            t = torch.ones(spec.shape, dtype=torch.float32, device=device)
             if norm_std:
-                t = t + torch.randn(spec.shape, generator=gen, dtype=torch.float32) * norm_std
+                t = t + torch.randn(spec.shape, generator=gen, dtype=torch.float32, device=device) * norm_std
         else:
-            t = torch.randn(spec.shape, generator=gen, dtype=torch.float32) * std
+            t = torch.randn(spec.shape, generator=gen, dtype=torch.float32, device=device) * std
         out[spec.name] = t.to(dtype).contiguous()
     return out
 
