@@ -42,6 +42,24 @@ TINY_C = {
 }
 
 
+# Head sizes that the tensor-core attention kernel takes: 64 with groups of four, 128 with groups of three.
+TINY_D = {
+    "architectures": ["LlamaForCausalLM"],
+    "hidden_size": 128, "num_hidden_layers": 2, "num_attention_heads": 8, "num_key_value_heads": 2,
+    "head_dim": 64, "intermediate_size": 256, "vocab_size": 512, "rms_norm_eps": 1e-5,
+    "max_position_embeddings": 4096, "rope_theta": 500000.0,
+    "rope_scaling": {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                     "original_max_position_embeddings": 256},
+    "tie_word_embeddings": True,
+}
+TINY_E = {
+    "architectures": ["LlamaForCausalLM"],
+    "hidden_size": 72, "num_hidden_layers": 2, "num_attention_heads": 3, "num_key_value_heads": 1,
+    "head_dim": 128, "intermediate_size": 136, "vocab_size": 300, "rms_norm_eps": 1e-6,
+    "max_position_embeddings": 1024, "rope_theta": 10000.0, "tie_word_embeddings": False,
+}
+
+
 @pytest.fixture(scope="session")
 def tiny_folders(tmp_path_factory):
     """Model folders of the tiny configurations with random weights, made once per session
@@ -52,7 +70,8 @@ def tiny_folders(tmp_path_factory):
 
     root = tmp_path_factory.mktemp("models")
     out = {}
-    for name, cfg, seed, norm_std in (("A", TINY_A, 0, 0.0), ("B", TINY_B, 1, 0.1), ("C", TINY_C, 2, 0.1)):
-        out[name] = write_model_folder(str(root / name), cfg, seed=seed, std=0.02 if name != "C" else 0.05,
+    for name, cfg, seed, norm_std in (("A", TINY_A, 0, 0.0), ("B", TINY_B, 1, 0.1), ("C", TINY_C, 2, 0.1),
+                                      ("D", TINY_D, 3, 0.1), ("E", TINY_E, 4, 0.0)):
+        out[name] = write_model_folder(str(root / name), cfg, seed=seed, std=0.02 if name in "AB" else 0.05,
                                        norm_std=norm_std, dtype=torch.float32)
     return out

@@ -4,11 +4,11 @@ import pytest
 import torch
 
 import helpers
-from conftest import TINY_A, TINY_B, TINY_C
+from conftest import TINY_A, TINY_B, TINY_C, TINY_D, TINY_E
 
 pytestmark = pytest.mark.gpu
 
-CONFIGS = {"A": TINY_A, "B": TINY_B, "C": TINY_C}
+CONFIGS = {"A": TINY_A, "B": TINY_B, "C": TINY_C, "D": TINY_D, "E": TINY_E}
 TOL = {"float32": 1e-4, "bfloat16": 4e-2}
 
 
@@ -34,7 +34,8 @@ def check(got, ref, dtype):
 
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
-@pytest.mark.parametrize("name,lengths,page", [("A", (7, 13, 70), 4), ("B", (5, 17, 33, 90), 8), ("C", (150, 40), 16)])
+@pytest.mark.parametrize("name,lengths,page", [("A", (7, 13, 70), 4), ("B", (5, 17, 33, 90), 8), ("C", (150, 40), 16),
+                                               ("D", (300, 45, 130, 70, 64), 16), ("E", (100, 37, 65), 8)])
 @pytest.mark.parametrize("cut", ["whole", "tail", "portions", "mixed"])
 def test_cuttings_match_plain(tiny_folders, dtype, name, lengths, page, cut):
     requests = requests_for(name, lengths)

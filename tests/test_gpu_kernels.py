@@ -103,11 +103,12 @@ def test_linear(kernels, dtype, M, N, K):
           scale=None if dtype == torch.float32 else 0.05)
 
 
-def make_paged_case(dtype, heads, kv_heads, head_dim, page_size, segments, window=None, seed=0, num_pages=64):
+def make_paged_case(dtype, heads, kv_heads, head_dim, page_size, segments, window=None, seed=0, num_pages=None):
     """Random qkv for the new tokens of several segments and a cache that already holds
     each segment's earlier keys and values on shuffled pages."""
     g = torch.Generator(device="cuda").manual_seed(seed)
     T = sum(n for _, n in segments)
+    num_pages = num_pages or sum(-(-(p + n) // page_size) for p, n in segments) + 3
     qkv = torch.randn(T, (heads + 2 * kv_heads) * head_dim, device="cuda", generator=g).to(dtype)
     keys = torch.randn(num_pages + 1, kv_heads, page_size, head_dim, device="cuda", generator=g).to(dtype)
     values = torch.randn(num_pages + 1, kv_heads, page_size, head_dim, device="cuda", generator=g).to(dtype)
@@ -119,8 +120,15 @@ def make_paged_case(dtype, heads, kv_heads, head_dim, page_size, segments, windo
             table[r, i] = perm.pop()
     positions = torch.tensor([p + i for p, n in segments for i in range(n)], dtype=torch.int32, device="cuda")
     seg_of = torch.tensor([r for r, (p, n) in enumerate(segments) for _ in range(n)], dtype=torch.int32, device="cuda")
+    cu = [0]
+    for _, n in segments:
+        cu.append(cu[-1] + n)
     batch = SimpleNamespace(positions=positions, seg_of_token=seg_of, seg_lens=[n for _, n in segments],
-                            seg_pos0_list=[p for p, _ in segments])
+                            seg_pos0_list=[p for p, _ in segments], num_segments=len(segments),
+                            cu_seqlens=torch.tensor(cu, dtype=torch.int32, device="cuda"),
+                            seg_pos0=torch.tensor([p for p, _ in segments], dtype=torch.int32, device="cuda"),
+                            max_seg_len=max(n for _, n in segments), max_context=max(p + n for p, n in segments),
+                            extras={})
     view = SimpleNamespace(keys=keys, values=values, block_table=table.cuda(), page_size=page_size, window=window)
     return qkv, batch, view
 
@@ -134,6 +142,16 @@ ATTN_CASES = [
     (2, 1, 128, 16, [(100, 5)], None),
     (4, 2, 16, 4, [(0, 40), (37, 1), (20, 9)], 11),
     (6, 3, 80, 8, [(9, 30)], 16),
+    # head sizes of the tensor-core kernel: 64-row tiles, 16-row tiles, key splits, windows, odd group sizes
+    (8, 2, 64, 16, [(0, 200), (70, 33), (500, 1)], None),
+    (8, 2, 64, 16, [(900, 1), (17, 1), (0, 1), (333, 1)], None),
+    (4, 1, 64, 8, [(1000, 3)], None),
+    (3, 1, 128, 16, [(0, 100), (129, 40)], None),
+    (6, 2, 128, 16, [(700, 1), (63, 1), (64, 1)], None),
+    (8, 8, 64, 4, [(0, 130), (300, 2)], None),
+    (8, 2, 64, 16, [(0, 150), (400, 1), (90, 20)], 100),
+    (32, 8, 64, 16, [(2000, 1)], None),
+    (10, 2, 64, 16, [(50, 70)], None),
 ]
 
 

@@ -1,0 +1,404 @@
+// Paged causal flash attention on the tensor cores (bfloat16 operands, float32 scores,
+// running maximum, sum and output in float32), for head sizes 64 and 128.
+//
+// A query tile holds 16 * WM rows; a row is one (token, query head of the KV group) pair,
+// token-major, so the heads that share a KV head share every key and value that is loaded.
+// Keys and values stream from the cache pages in tiles of 64 keys through a two-stage
+// cp.async pipeline into swizzled shared memory. Two shapes of the same code:
+//   prefill:  WM = 4, WN = 1   four warps, 16 rows each, every warp sees all 64 keys of a tile
+//   decode:   WM = 1, WN = 4   one 16-row tile (a single token's heads), the four warps take
+//                              16 keys each of every tile and merge at the end
+// With num_splits > 1 the keys of a tile's range are cut into num_splits chunks, one block
+// each; the blocks write unnormalised partial results to scratch memory and a second kernel
+// merges them (flash decoding).
+//
+// Query t of segment r sits at position seg_pos0[r] + (t - cu_seqlens[r]) and sees the keys at
+// positions <= its own (and > its own - window, with a window).
+#include "common.cuh"
+
+#define AM_BN 64
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Byte offset of 16-byte chunk `chunk` of row `row` in a tile whose rows hold HD bfloat16 values.
+template <int HD> __device__ __forceinline__ uint32_t tile_offset(int row, int chunk) {
+    return (uint32_t)(row * HD * 2 + ((chunk ^ (row & 7)) << 4));
+}
+
+template <int HD, int WM, int WN>
+__global__ void __launch_bounds__(WM * WN * 32)
+attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __nv_bfloat16* __restrict__ out,
+                     const int* __restrict__ cu_seqlens, const int* __restrict__ seg_pos0,
+                     const __nv_bfloat16* __restrict__ key_pages, const __nv_bfloat16* __restrict__ value_pages,
+                     const int* __restrict__ block_table, int table_width, int page_size,
+                     const int* __restrict__ qtile_seg, const int* __restrict__ qtile_tok0,
+                     int heads, int kv_heads, float scale_log2, int window, int num_splits,
+                     float* __restrict__ partial_o, float* __restrict__ partial_ml) {
+    constexpr int BM = 16 * WM;
+    constexpr int THREADS = WM * WN * 32;
+    constexpr int CHUNKS = HD / 8;              // 16-byte chunks per row
+    constexpr int WARP_KEYS = AM_BN / WN;       // keys of a tile that one warp handles
+    constexpr int NB = WARP_KEYS / 8;           // score n-blocks per warp
+    constexpr int KS = HD / 16;                 // k-steps of Q K^T
+    constexpr int OB = HD / 8;                  // output n-blocks
+    constexpr int TILE_BYTES = AM_BN * HD * 2;
+
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char* q_tile = smem;                               // [BM][HD]
+    unsigned char* k_stage = smem + BM * HD * 2;                // [2][BN][HD]
+    unsigned char* v_stage = k_stage + 2 * TILE_BYTES;          // [2][BN][HD]
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int warp_m = warp / WN, warp_n = warp % WN;
+    const int qt = blockIdx.x, g = blockIdx.y, split = blockIdx.z;
+    const int rep = heads / kv_heads;
+    const int seg = qtile_seg ? qtile_seg[qt] : qt;
+    const int tok0 = qtile_tok0 ? qtile_tok0[qt] : 0;
+    const int seg_start = cu_seqlens[seg];
+    const int seg_tokens = cu_seqlens[seg + 1] - seg_start;
+    if (tok0 >= seg_tokens) return;                             // a padded tile of a captured step
+    const int pos0 = seg_pos0[seg];
+    const int tokens_per_tile = BM / rep;
+    const int tile_tokens = min(tokens_per_tile, seg_tokens - tok0);
+    const int valid_rows = tile_tokens * rep;
+    const int q_first = pos0 + tok0, q_last = q_first + tile_tokens - 1;
+    const int lo = (window > 0 && q_first - window + 1 > 0) ? q_first - window + 1 : 0;
+    const int total = q_last - lo + 1;
+    const int chunk = ((total + num_splits - 1) / num_splits + AM_BN - 1) / AM_BN * AM_BN;
+    const int k_begin = lo + split * chunk;
+    const int k_end = min(q_last + 1, k_begin + chunk);
+    const int* table = block_table + (size_t)seg * table_width;
+
+    // the two rows of the score fragment that this thread holds
+    const int r0 = warp_m * 16 + (lane >> 2), r1 = r0 + 8;
+    const int qpos0 = q_first + r0 / rep, qpos1 = q_first + r1 / rep;
+
+    float o_acc[OB][4];
+#pragma unroll
+    for (int i = 0; i < OB; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o_acc[i][j] = 0.f;
+    float row_max[2] = {-INFINITY, -INFINITY}, row_sum[2] = {0.f, 0.f};
+
+    if (k_begin < k_end) {
+        // ---- load the query tile (rows beyond valid_rows are zero)
+        for (int idx = tid; idx < BM * CHUNKS; idx += THREADS) {
+            const int r = idx / CHUNKS, c = idx % CHUNKS;
+            const bool ok = r < valid_rows;
+            const int token = tok0 + (ok ? r / rep : 0), head = g * rep + (ok ? r % rep : 0);
+            const __nv_bfloat16* src = qkv + (size_t)(seg_start + token) * q_row_stride + (size_t)head * HD + c * 8;
+            cp_async16(smem_u32(q_tile + tile_offset<HD>(r, c)), src, ok ? 16 : 0);
+        }
+        auto load_tile = [&](int tile, int stage) {
+            const int kb = k_begin + tile * AM_BN;
+            for (int idx = tid; idx < AM_BN * CHUNKS; idx += THREADS) {
+                const int r = idx / CHUNKS, c = idx % CHUNKS;
+                const int key = kb + r;
+                const bool ok = key < k_end;
+                size_t off = 0;
+                if (ok) {
+                    const int page = table[key / page_size];
+                    off = (((size_t)page * kv_heads + g) * page_size + (key % page_size)) * HD + c * 8;
+                }
+                const uint32_t dst = tile_offset<HD>(r, c) + stage * TILE_BYTES;
+                cp_async16(smem_u32(k_stage + dst), key_pages + off, ok ? 16 : 0);
+                cp_async16(smem_u32(v_stage + dst), value_pages + off, ok ? 16 : 0);
+            }
+        };
+        const int num_tiles = (k_end - k_begin + AM_BN - 1) / AM_BN;
+        load_tile(0, 0);
+        cp_async_commit();
+
+        uint32_t q_frag[KS][4];
+        for (int tile = 0; tile < num_tiles; ++tile) {
+            const int stage = tile & 1;
+            if (tile + 1 < num_tiles) load_tile(tile + 1, stage ^ 1);
+            cp_async_commit();
+            cp_async_wait<1>();
+            __syncthreads();
+            if (tile == 0) {
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks)
+                    ldmatrix_x4(q_frag[ks], smem_u32(q_tile + tile_offset<HD>(warp_m * 16 + (lane & 15), ks * 2 + (lane >> 4))));
+            }
+            const unsigned char* k_tile = k_stage + stage * TILE_BYTES;
+            const unsigned char* v_tile = v_stage + stage * TILE_BYTES;
+            const int key_base = k_begin + tile * AM_BN + warp_n * WARP_KEYS;   // first key of this warp's part
+
+            // ---- scores: S = Q K^T for this warp's keys
+            float s[NB][4];
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) s[nb][j] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+                for (int nb = 0; nb < NB; nb += 2) {
+                    uint32_t b[4];
+                    const int key_row = warp_n * WARP_KEYS + nb * 8 + (lane & 7) + ((lane >> 4) << 3);
+                    ldmatrix_x4(b, smem_u32(k_tile + tile_offset<HD>(key_row, ks * 2 + ((lane >> 3) & 1))));
+                    mma_bf16(s[nb], q_frag[ks], b[0], b[1]);
+                    mma_bf16(s[nb + 1], q_frag[ks], b[2], b[3]);
+                }
+            }
+            // ---- mask, running maximum and sum
+            float tile_max[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int key = key_base + nb * 8 + ((lane & 3) << 1) + (j & 1);
+                    const int qpos = (j < 2) ? qpos0 : qpos1;
+                    const bool visible = key < k_end && key <= qpos && (window <= 0 || key > qpos - window);
+                    const float v = visible ? s[nb][j] * scale_log2 : -INFINITY;
+                    s[nb][j] = v;
+                    tile_max[j >> 1] = fmaxf(tile_max[j >> 1], v);
+                }
+            }
+            float alpha[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                tile_max[h] = fmaxf(tile_max[h], __shfl_xor_sync(0xffffffffu, tile_max[h], 1));
+                tile_max[h] = fmaxf(tile_max[h], __shfl_xor_sync(0xffffffffu, tile_max[h], 2));
+                const float new_max = fmaxf(row_max[h], tile_max[h]);
+                alpha[h] = (row_max[h] == -INFINITY) ? 0.f : exp2f(row_max[h] - new_max);
+                row_max[h] = new_max;
+                row_sum[h] *= alpha[h];
+            }
+            const float m0 = (row_max[0] == -INFINITY) ? 0.f : row_max[0];
+            const float m1 = (row_max[1] == -INFINITY) ? 0.f : row_max[1];
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) {
+                s[nb][0] = exp2f(s[nb][0] - m0);
+                s[nb][1] = exp2f(s[nb][1] - m0);
+                s[nb][2] = exp2f(s[nb][2] - m1);
+                s[nb][3] = exp2f(s[nb][3] - m1);
+                row_sum[0] += s[nb][0] + s[nb][1];
+                row_sum[1] += s[nb][2] + s[nb][3];
+            }
+#pragma unroll
+            for (int ob = 0; ob < OB; ++ob) {
+                o_acc[ob][0] *= alpha[0];
+                o_acc[ob][1] *= alpha[0];
+                o_acc[ob][2] *= alpha[1];
+                o_acc[ob][3] *= alpha[1];
+            }
+            // ---- output: O += P V
+#pragma unroll
+            for (int kk = 0; kk < WARP_KEYS / 16; ++kk) {
+                uint32_t p[4];
+                p[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+                p[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+                p[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+                p[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+                for (int ob = 0; ob < OB; ob += 2) {
+                    uint32_t b[4];
+                    const int key_row = warp_n * WARP_KEYS + kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+                    ldmatrix_x4_trans(b, smem_u32(v_tile + tile_offset<HD>(key_row, ob + (lane >> 4))));
+                    mma_bf16(o_acc[ob], p, b[0], b[1]);
+                    mma_bf16(o_acc[ob + 1], p, b[2], b[3]);
+                }
+            }
+            __syncthreads();     // the stage is free for the load after next
+        }
+        cp_async_wait<0>();
+    }
+
+    // ---- row sums over the four lanes of a quad
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        row_sum[h] += __shfl_xor_sync(0xffffffffu, row_sum[h], 1);
+        row_sum[h] += __shfl_xor_sync(0xffffffffu, row_sum[h], 2);
+    }
+
+    // ---- the warps of one row tile merge what they saw of the keys
+    if constexpr (WN > 1) {
+        __syncthreads();
+        float* merge_o = reinterpret_cast<float*>(k_stage);                     // [WN][16][HD]
+        float* merge_ml = merge_o + WN * 16 * HD;                               // [WN][16][2]
+        const int lr0 = lane >> 2, lr1 = lr0 + 8;
+        if ((lane & 3) == 0) {
+            merge_ml[(warp_n * 16 + lr0) * 2] = row_max[0];
+            merge_ml[(warp_n * 16 + lr0) * 2 + 1] = row_sum[0];
+            merge_ml[(warp_n * 16 + lr1) * 2] = row_max[1];
+            merge_ml[(warp_n * 16 + lr1) * 2 + 1] = row_sum[1];
+        }
+#pragma unroll
+        for (int ob = 0; ob < OB; ++ob) {
+            const int col = ob * 8 + ((lane & 3) << 1);
+            float* a = merge_o + ((size_t)(warp_n * 16 + lr0)) * HD + col;
+            float* b = merge_o + ((size_t)(warp_n * 16 + lr1)) * HD + col;
+            a[0] = o_acc[ob][0]; a[1] = o_acc[ob][1];
+            b[0] = o_acc[ob][2]; b[1] = o_acc[ob][3];
+        }
+        __syncthreads();
+        // every thread now owns elements of the merged tile: 16 rows x HD columns over WM*WN*32 threads
+        for (int idx = tid; idx < 16 * HD; idx += THREADS) {
+            const int r = idx / HD, c = idx % HD;
+            float m = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < WN; ++w) m = fmaxf(m, merge_ml[(w * 16 + r) * 2]);
+            float sum = 0.f, o = 0.f;
+#pragma unroll
+            for (int w = 0; w < WN; ++w) {
+                const float mw = merge_ml[(w * 16 + r) * 2];
+                const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - m);
+                sum += f * merge_ml[(w * 16 + r) * 2 + 1];
+                o += f * merge_o[((size_t)(w * 16 + r)) * HD + c];
+            }
+            if (r >= valid_rows) continue;
+            const int token = tok0 + r / rep, head = g * rep + r % rep;
+            if (num_splits > 1) {
+                const size_t slot = ((size_t)(seg_start + token) * heads + head) * num_splits + split;
+                partial_o[slot * HD + c] = o;
+                if (c == 0) { partial_ml[slot * 2] = m; partial_ml[slot * 2 + 1] = sum; }
+            } else {
+                out[((size_t)(seg_start + token) * heads + head) * HD + c] = __float2bfloat16_rn(sum > 0.f ? o / sum : 0.f);
+            }
+        }
+    } else {
+    // ---- WN == 1: every warp writes its own 16 rows
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int r = h == 0 ? r0 : r1;
+        if (r >= valid_rows) continue;
+        const int token = tok0 + r / rep, head = g * rep + r % rep;
+        const size_t row_index = (size_t)(seg_start + token) * heads + head;
+        if (num_splits > 1) {
+            const size_t slot = row_index * num_splits + split;
+#pragma unroll
+            for (int ob = 0; ob < OB; ++ob) {
+                const int col = ob * 8 + ((lane & 3) << 1);
+                *reinterpret_cast<float2*>(partial_o + slot * HD + col) = make_float2(o_acc[ob][2 * h], o_acc[ob][2 * h + 1]);
+            }
+            if ((lane & 3) == 0) { partial_ml[slot * 2] = row_max[h]; partial_ml[slot * 2 + 1] = row_sum[h]; }
+        } else {
+            const float inv = row_sum[h] > 0.f ? 1.f / row_sum[h] : 0.f;
+#pragma unroll
+            for (int ob = 0; ob < OB; ++ob) {
+                const int col = ob * 8 + ((lane & 3) << 1);
+                *reinterpret_cast<uint32_t*>(out + row_index * HD + col) = pack_bf16(o_acc[ob][2 * h] * inv, o_acc[ob][2 * h + 1] * inv);
+            }
+        }
+    }
+    }
+}
+
+// out[row, :] = sum_s w_s O_s / sum_s w_s l_s with w_s = 2^(m_s - max m); one warp per (token, head) row.
+template <int HD>
+__global__ void attention_merge_kernel(const float* __restrict__ partial_o, const float* __restrict__ partial_ml,
+                                       __nv_bfloat16* __restrict__ out, int rows, int num_splits) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* ml = partial_ml + (size_t)row * num_splits * 2;
+    float m = -INFINITY;
+    for (int s = 0; s < num_splits; ++s) m = fmaxf(m, ml[2 * s]);
+    float acc[HD / 32];
+#pragma unroll
+    for (int i = 0; i < HD / 32; ++i) acc[i] = 0.f;
+    float sum = 0.f;
+    for (int s = 0; s < num_splits; ++s) {
+        const float ms = ml[2 * s];
+        if (ms == -INFINITY) continue;
+        const float f = exp2f(ms - m);
+        sum += f * ml[2 * s + 1];
+        const float* o = partial_o + ((size_t)row * num_splits + s) * HD;
+#pragma unroll
+        for (int i = 0; i < HD / 32; ++i) acc[i] += f * o[lane + 32 * i];
+    }
+    const float inv = sum > 0.f ? 1.f / sum : 0.f;
+#pragma unroll
+    for (int i = 0; i < HD / 32; ++i) out[(size_t)row * HD + lane + 32 * i] = __float2bfloat16_rn(acc[i] * inv);
+}
+
+template <int HD, int WM, int WN>
+static int launch_attention(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens, const int* seg_pos0,
+                            const void* key_pages, const void* value_pages, const int* block_table, int table_width,
+                            int page_size, const int* qtile_seg, const int* qtile_tok0, int n_qtiles, int tokens,
+                            int heads, int kv_heads, float scale, int window, int num_splits, float* partial_o,
+                            float* partial_ml, cudaStream_t stream) {
+    constexpr int BM = 16 * WM;
+    const size_t stage_bytes = (size_t)BM * HD * 2 + 4 * (size_t)AM_BN * HD * 2;
+    const size_t merge_bytes = (size_t)BM * HD * 2 + (size_t)WN * 16 * (HD + 2) * sizeof(float);
+    const size_t smem = stage_bytes > merge_bytes ? stage_bytes : merge_bytes;
+    auto kernel = attention_mma_kernel<HD, WM, WN>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return (int)e;
+        configured = true;
+    }
+    dim3 grid(n_qtiles, kv_heads, num_splits);
+    const float scale_log2 = scale * 1.4426950408889634f;
+    kernel<<<grid, WM * WN * 32, smem, stream>>>(
+        (const __nv_bfloat16*)qkv, q_row_stride, (__nv_bfloat16*)out, cu_seqlens, seg_pos0,
+        (const __nv_bfloat16*)key_pages, (const __nv_bfloat16*)value_pages, block_table, table_width, page_size,
+        qtile_seg, qtile_tok0, heads, kv_heads, scale_log2, window, num_splits, partial_o, partial_ml);
+    int status = ttb_launch_status();
+    if (status != TTB_OK || num_splits == 1) return status;
+    const int rows = tokens * heads;
+    attention_merge_kernel<HD><<<(rows + 3) / 4, 128, 0, stream>>>(partial_o, partial_ml, (__nv_bfloat16*)out, rows, num_splits);
+    return ttb_launch_status();
+}
+
+// Rows of a query tile in each shape: the host cuts segments into tiles of rows / (heads / kv_heads) tokens.
+TTB_EXPORT int ttb_attention_mma_tile_rows(int decode_shape) { return decode_shape ? 16 : 64; }
+
+// Whether this kernel takes the geometry at all.
+TTB_EXPORT int ttb_attention_mma_supports(int heads, int kv_heads, int head_dim) {
+    if (head_dim != 64 && head_dim != 128) return 0;
+    if (kv_heads < 1 || heads % kv_heads) return 0;
+    return heads / kv_heads <= 16;
+}
+
+// decode_shape: 1 when every tile holds the heads of one token (16 rows), 0 for 64-row tiles.
+// qtile_seg / qtile_tok0 may be null: tile i is then token 0 of segment i.
+// With num_splits > 1, partial_o holds tokens * heads * num_splits * head_dim floats and partial_ml
+// tokens * heads * num_splits * 2 floats of scratch memory.
+TTB_EXPORT int ttb_paged_attention_mma(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens,
+                                       const int* seg_pos0, const void* key_pages, const void* value_pages,
+                                       const int* block_table, int table_width, int page_size, const int* qtile_seg,
+                                       const int* qtile_tok0, int n_qtiles, int tokens, int heads, int kv_heads,
+                                       int head_dim, float scale, int window, int decode_shape, int num_splits,
+                                       float* partial_o, float* partial_ml, cudaStream_t stream) {
+    if (n_qtiles == 0 || tokens == 0) return TTB_OK;
+    if (!qkv || !out || !cu_seqlens || !seg_pos0 || !key_pages || !value_pages || !block_table) return TTB_ERR_ARGUMENT;
+    if (!ttb_attention_mma_supports(heads, kv_heads, head_dim)) return TTB_ERR_UNSUPPORTED;
+    if (num_splits < 1 || num_splits > 65535 || kv_heads > 65535) return TTB_ERR_UNSUPPORTED;
+    if (num_splits > 1 && (!partial_o || !partial_ml)) return TTB_ERR_ARGUMENT;
+    if ((q_row_stride & 7) || !aligned16(qkv) || !aligned16(key_pages) || !aligned16(value_pages) || !aligned16(out))
+        return TTB_ERR_ARGUMENT;
+    if (decode_shape && heads / kv_heads > 16) return TTB_ERR_UNSUPPORTED;
+#define AM_ARGS qkv, q_row_stride, out, cu_seqlens, seg_pos0, key_pages, value_pages, block_table, table_width, page_size, \
+                qtile_seg, qtile_tok0, n_qtiles, tokens, heads, kv_heads, scale, window, num_splits, partial_o, partial_ml, stream
+    if (head_dim == 64) return decode_shape ? launch_attention<64, 1, 4>(AM_ARGS) : launch_attention<64, 4, 1>(AM_ARGS);
+    return decode_shape ? launch_attention<128, 1, 4>(AM_ARGS) : launch_attention<128, 4, 1>(AM_ARGS);
+#undef AM_ARGS
+}

@@ -64,7 +64,8 @@ class CudaKernels:
             raise KernelError(f"the CUDA kernel library {path} could not be loaded: {e}") from e
         self.library_path = path
         for name in ("ttb_embedding", "ttb_add_rmsnorm", "ttb_swiglu", "ttb_gather_rows", "ttb_rope_kv_write",
-                     "ttb_paged_attention_generic", "ttb_gemm_simt", "ttb_gemv", "ttb_sample"):
+                     "ttb_paged_attention_generic", "ttb_gemm_simt", "ttb_gemv", "ttb_sample",
+                     "ttb_paged_attention_mma", "ttb_attention_mma_tile_rows", "ttb_attention_mma_supports"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -73,6 +74,8 @@ class CudaKernels:
         with torch.cuda.device(self.device):
             self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.launches = 0     # how many of our kernels were launched (counted for reports)
+        self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.use_mma_attention = True
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
@@ -184,12 +187,61 @@ class CudaKernels:
         out = torch.empty(tokens, heads * head_dim, dtype=qkv.dtype, device=self.device)
         if view.keys.dtype != qkv.dtype:
             raise KernelError("paged_attention: cache pages and queries differ in dtype")
+        if (self.use_mma_attention and qkv.dtype == torch.bfloat16
+                and self.lib.ttb_attention_mma_supports(heads, kv_heads, head_dim)):
+            self._attention_mma(qkv, out, batch, heads, kv_heads, head_dim, scale, view)
+            return out
         self._check(self.lib.ttb_paged_attention_generic(
             self._p(qkv), qkv.stride(0), self._p(out), _dtype_code(qkv.dtype), self._p(batch.positions),
             self._p(batch.seg_of_token), self._p(view.keys), self._p(view.values), self._p(view.block_table),
             view.block_table.shape[1], view.page_size, tokens, heads, kv_heads, head_dim, ctypes.c_float(scale),
             int(view.window or 0), self._stream()), "paged_attention")
         return out
+
+    def _attention_plan(self, batch, rep: int, kv_heads: int):
+        """How the step's segments are cut into query tiles, and into how many key splits:
+        derived once per step and geometry, reused by every layer."""
+        key = ("attention_plan", rep, kv_heads)
+        plan = batch.extras.get(key)
+        if plan is not None:
+            return plan
+        decode_shape = batch.max_seg_len * rep <= 16
+        rows = int(self.lib.ttb_attention_mma_tile_rows(1 if decode_shape else 0))
+        tokens_per_tile = max(1, rows // rep)
+        if decode_shape:
+            seg, tok0, n_tiles = None, None, batch.num_segments
+        else:
+            seg_list, tok_list = [], []
+            for r, n in enumerate(batch.seg_lens):
+                for t in range(0, n, tokens_per_tile):
+                    seg_list.append(r)
+                    tok_list.append(t)
+            n_tiles = len(seg_list)
+            both = torch.tensor([seg_list, tok_list], dtype=torch.int32, pin_memory=True).to(self.device, non_blocking=True)
+            seg, tok0 = both[0], both[1]
+        blocks = n_tiles * kv_heads
+        splits = 1
+        if blocks < 2 * self.sm_count:
+            splits = max(1, min(-(-4 * self.sm_count // blocks), batch.max_context // 256))
+        plan = (decode_shape, seg, tok0, n_tiles, splits)
+        batch.extras[key] = plan
+        return plan
+
+    def _attention_mma(self, qkv, out, batch, heads, kv_heads, head_dim, scale, view):
+        tokens = qkv.shape[0]
+        decode_shape, seg, tok0, n_tiles, splits = self._attention_plan(batch, heads // kv_heads, kv_heads)
+        partial_o = partial_ml = None
+        if splits > 1:
+            partial_o = torch.empty(tokens * heads * splits * head_dim, dtype=torch.float32, device=self.device)
+            partial_ml = torch.empty(tokens * heads * splits * 2, dtype=torch.float32, device=self.device)
+        self._check(self.lib.ttb_paged_attention_mma(
+            self._p(qkv), qkv.stride(0), self._p(out), self._p(batch.cu_seqlens), self._p(batch.seg_pos0),
+            self._p(view.keys), self._p(view.values), self._p(view.block_table), view.block_table.shape[1],
+            view.page_size, self._p(seg), self._p(tok0), n_tiles, tokens, heads, kv_heads, head_dim,
+            ctypes.c_float(scale), int(view.window or 0), 1 if decode_shape else 0, splits,
+            self._p(partial_o), self._p(partial_ml), self._stream()), "paged_attention_mma")
+        if splits > 1:
+            self.launches += 1
 
     # ------------------------------------------------------------------ sampling
     def sample(self, logits, temperature=None, top_k=None, top_p=None, seeds=None, counters=None) -> torch.Tensor:

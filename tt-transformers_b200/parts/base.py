@@ -106,6 +106,7 @@ class StepBatch:
     max_seg_len: int = 1
     max_context: int = 1          # the largest pos0 + len over the segments
     block_tables: Dict[int, torch.Tensor] = field(default_factory=dict)  # group index -> [R, W]
+    extras: dict = field(default_factory=dict)   # per-step tables that kernels derive once and reuse in every layer
 
 
 class Part:
