@@ -114,6 +114,8 @@ def main(argv=None) -> int:
     parser.add_argument("--context", type=int, default=8192)
     parser.add_argument("--layers", type=int, default=FULL_LAYERS)
     parser.add_argument("--points", default="1,64", help="other decode batch sizes to report, comma separated")
+    parser.add_argument("--skip-prefill", action="store_true", help="leave the prefill measurement out (for profiling decode)")
+    parser.add_argument("--skip-e2e", action="store_true", help="leave the end-to-end measurement out (for profiling)")
     parser.add_argument("--fill", default="prefill", choices=("prefill", "synthetic"),
                         help="how the cache gets its context before decoding: through the engine's own prefill, "
                              "or filled with random numbers (faster; decode time does not depend on the values)")
@@ -173,9 +175,11 @@ def main(argv=None) -> int:
         engine.step([StepEntry("p", pre_tokens, [PREFILL_TOKENS - 1])])
         engine.finish("p")
 
-    for _ in range(3):
-        prefill_once()
-    prefill_ms = timed(prefill_once, 5)
+    prefill_ms = float("nan")
+    if not args.skip_prefill:
+        for _ in range(3):
+            prefill_once()
+        prefill_ms = timed(prefill_once, 5)
     flops = prefill_flops(cfg, args.layers, PREFILL_TOKENS)
     prefill = {"value": round(PREFILL_TOKENS / prefill_ms * 1e3, 1), "tokens": PREFILL_TOKENS,
                "ms": round(prefill_ms, 3), "frac": round(flops / (prefill_ms * 1e-3) / (pk["bf16_tflops"] * 1e12), 4)}
@@ -229,7 +233,9 @@ def main(argv=None) -> int:
     # ------------------------------------------------------------------ end to end through the Python entry point
     params = SamplingParams(temperature=0.0, max_new_tokens=1 << 30, ignore_eos=True)
     length = args.context - args.steps - warmup - 2
-    if args.fill == "synthetic":
+    if args.skip_e2e:
+        e2e = None
+    elif args.fill == "synthetic":
         reqs = []
         for i in range(args.batch):       # the prompts' last token goes through the engine; the rest is filled
             r = llm.add_request(prompt(length), params)
@@ -247,17 +253,18 @@ def main(argv=None) -> int:
             llm.add_request(prompt(length), params)
         while any(r.num_computed < len(r.prompt) for r in llm._scheduler.running) or llm._scheduler.waiting:
             llm.step()
-    for _ in range(warmup):
+    if not args.skip_e2e:
+      for _ in range(warmup):
         llm.step()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
+      torch.cuda.synchronize()
+      t0 = time.perf_counter()
+      for _ in range(args.steps):
         llm.step()
-    torch.cuda.synchronize()
-    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
-    e2e = {"value": round(args.batch / e2e_ms * 1e3, 1), "unit": "tokens/s",
-           "h2d_bytes_per_step": 4 * (3 * 4 * max(1, args.batch // 4 + (args.batch % 4 > 0)) + 16 + args.batch * pages_per_request),
-           "d2h_bytes_per_step": 4 * args.batch}
+      torch.cuda.synchronize()
+      e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+      e2e = {"value": round(args.batch / e2e_ms * 1e3, 1), "unit": "tokens/s",
+             "h2d_bytes_per_step": 4 * (3 * 4 * max(1, args.batch // 4 + (args.batch % 4 > 0)) + 16 + args.batch * pages_per_request),
+             "d2h_bytes_per_step": 4 * args.batch}
 
     line = {
         "metric": "decode tokens/s, Llama 3.2 1B sizes, batch 8", "value": round(value, 1), "unit": "tokens/s",

@@ -90,7 +90,9 @@ def test_gather_rows(kernels, dtype, width):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("M,N,K", [(1, 384, 96), (3, 100, 320), (8, 3072, 2048), (5, 77, 41), (9, 96, 64),
-                                   (50, 320, 96), (130, 200, 80), (64, 257, 1000), (200, 2048, 512)])
+                                   (50, 320, 96), (130, 200, 80), (64, 257, 1000), (200, 2048, 512),
+                                   (2, 2048, 8192), (16, 1000, 72), (17, 33, 8), (32, 2048, 2048), (64, 3072, 2048),
+                                   (7, 128256, 256), (40, 50, 1000)])
 def test_linear(kernels, dtype, M, N, K):
     g = torch.Generator(device="cuda").manual_seed(3)
     x = torch.randn(M, K, device="cuda", generator=g).to(dtype)
@@ -101,6 +103,17 @@ def test_linear(kernels, dtype, M, N, K):
     assert got32.dtype == torch.float32
     close(got32, ref, torch.float32 if dtype == torch.float32 else torch.bfloat16,
           scale=None if dtype == torch.float32 else 0.05)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("M,inter,K", [(1, 320, 96), (8, 8192, 2048), (5, 200, 80), (20, 136, 72), (33, 1000, 256),
+                                       (64, 512, 128), (70, 320, 96), (3, 77, 41)])
+def test_linear_swiglu(kernels, twin, dtype, M, inter, K):
+    g = torch.Generator(device="cuda").manual_seed(6)
+    x = torch.randn(M, K, device="cuda", generator=g).to(dtype)
+    w = (torch.randn(2 * inter, K, device="cuda", generator=g) / math.sqrt(K) * 2).to(dtype)
+    ref = twin.linear_swiglu(x.double(), w.double())
+    close(kernels.linear_swiglu(x, w), ref, dtype)
 
 
 def make_paged_case(dtype, heads, kv_heads, head_dim, page_size, segments, window=None, seed=0, num_pages=None):

@@ -44,6 +44,9 @@ class TorchKernels:
     def linear(self, x, w, out_dtype=None):
         return (x.float() @ w.float().t()).to(out_dtype or x.dtype)
 
+    def linear_swiglu(self, x, w_gate_up):
+        return self.swiglu(self.linear(x, w_gate_up))
+
     # ------------------------------------------------------------------ attention
     def rope_kv_write(self, qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True):
         T = qkv.shape[0]

@@ -1,0 +1,207 @@
+// Weight-streaming matrix product for decoding on the tensor cores:
+//   out[m, n] = sum_k x[m, k] * w[n, k]     for M <= 64 rows of x (one per decoded token).
+// The weight matrix is the 16-row operand of mma.m16n8k16 and the activations the 8-column one,
+// so a handful of tokens costs no more tensor work than one. Every weight is read from HBM
+// once, with 16-byte loads that go straight into the fragment registers: within a block of 32
+// k, lane t of a quad holds k = 8t .. 8t+7 for both operands, which is a permutation of k that
+// the sum does not see. The eight warps of a block share the same weight rows and take the
+// k-blocks in turn; their partial sums meet in shared memory.
+//
+// Row modes of a 16-row fragment:
+//   FULL  rows n0 .. n0+15 of w
+//   HALF  rows n0 .. n0+7 of w, upper half zero (more blocks for matrices with few rows)
+//   PAIR  rows n0 .. n0+7 of w (gate) and of w + pair_offset rows (up); the epilogue writes
+//         silu(gate) * up, so the SwiGLU product never round-trips through memory
+#include "common.cuh"
+
+#define GM_WARPS 8
+#define GM_THREADS (GM_WARPS * 32)
+#define GM_FULL 0
+#define GM_HALF 1
+#define GM_PAIR 2
+
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint4 ldg_cached(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int NB, int RG, int MODE, typename TO>
+__global__ void __launch_bounds__(GM_THREADS)
+gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w, TO* __restrict__ out,
+                int M, int N, int K, int ldx, int ldw, int ldo, int pair_offset) {
+    constexpr int ROWS_PER_GROUP = (MODE == GM_FULL) ? 16 : 8;
+    extern __shared__ float4 partial[];          // [GM_WARPS][RG * NB * 32]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int n0 = blockIdx.x * ROWS_PER_GROUP * RG;
+
+    // row pointers of this thread: [rg][half]
+    const __nv_bfloat16* wrow[RG][2];
+#pragma unroll
+    for (int rg = 0; rg < RG; ++rg) {
+        int lower = n0 + rg * ROWS_PER_GROUP + g;
+        if (lower > N - 1) lower = N - 1;                       // clamped rows are computed and not written
+        wrow[rg][0] = w + (size_t)lower * ldw;
+        if (MODE == GM_FULL) {
+            int upper = n0 + rg * 16 + 8 + g;
+            if (upper > N - 1) upper = N - 1;
+            wrow[rg][1] = w + (size_t)upper * ldw;
+        } else if (MODE == GM_PAIR) {
+            wrow[rg][1] = w + (size_t)(lower + pair_offset) * ldw;
+        } else {
+            wrow[rg][1] = nullptr;
+        }
+    }
+    const __nv_bfloat16* xrow[NB];
+    bool xok[NB];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+        const int m = nb * 8 + g;
+        xok[nb] = m < M;
+        xrow[nb] = x + (size_t)(xok[nb] ? m : 0) * ldx;
+    }
+
+    float acc[RG][NB][4];
+#pragma unroll
+    for (int rg = 0; rg < RG; ++rg)
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[rg][nb][c] = 0.f;
+
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    constexpr int UNROLL = (RG * NB >= 8) ? 2 : 4;
+    // warp `warp` takes the k-blocks warp, warp + 8, ... ; UNROLL of them are in flight at a time
+    for (int kb0 = warp * 32; kb0 < K; kb0 += GM_WARPS * 32 * UNROLL) {
+        uint4 wv[UNROLL][RG][2];
+        uint4 xv[UNROLL][NB];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int k = kb0 + u * GM_WARPS * 32 + t * 8;
+            const bool in = k < K;
+#pragma unroll
+            for (int rg = 0; rg < RG; ++rg) {
+                wv[u][rg][0] = in ? ldg_stream(wrow[rg][0] + k) : zero;
+                wv[u][rg][1] = (in && MODE != GM_HALF) ? ldg_stream(wrow[rg][1] + k) : zero;
+            }
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) xv[u][nb] = (in && xok[nb]) ? ldg_cached(xrow[nb] + k) : zero;
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u)
+#pragma unroll
+            for (int rg = 0; rg < RG; ++rg)
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    mma16816(acc[rg][nb], wv[u][rg][0].x, wv[u][rg][1].x, wv[u][rg][0].y, wv[u][rg][1].y,
+                             xv[u][nb].x, xv[u][nb].y);
+                    mma16816(acc[rg][nb], wv[u][rg][0].z, wv[u][rg][1].z, wv[u][rg][0].w, wv[u][rg][1].w,
+                             xv[u][nb].z, xv[u][nb].w);
+                }
+    }
+
+    // ---- the eight warps add up
+    constexpr int PER_WARP = RG * NB * 32;
+#pragma unroll
+    for (int rg = 0; rg < RG; ++rg)
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+            partial[warp * PER_WARP + (rg * NB + nb) * 32 + lane] =
+                make_float4(acc[rg][nb][0], acc[rg][nb][1], acc[rg][nb][2], acc[rg][nb][3]);
+    __syncthreads();
+    for (int e = threadIdx.x; e < PER_WARP; e += GM_THREADS) {
+        float4 s = partial[e];
+#pragma unroll
+        for (int wp = 1; wp < GM_WARPS; ++wp) {
+            const float4 p = partial[wp * PER_WARP + e];
+            s.x += p.x; s.y += p.y; s.z += p.z; s.w += p.w;
+        }
+        const int el = e & 31, nb = (e >> 5) % NB, rg = (e >> 5) / NB;
+        const int eg = el >> 2, et = el & 3;
+        const int m0 = nb * 8 + 2 * et, m1 = m0 + 1;
+        const int lower = n0 + rg * ROWS_PER_GROUP + eg;
+        if (MODE == GM_PAIR) {
+            if (lower < N) {
+                if (m0 < M) out[(size_t)m0 * ldo + lower] = from_float<TO>(s.x / (1.f + __expf(-s.x)) * s.z);
+                if (m1 < M) out[(size_t)m1 * ldo + lower] = from_float<TO>(s.y / (1.f + __expf(-s.y)) * s.w);
+            }
+        } else {
+            if (lower < N) {
+                if (m0 < M) out[(size_t)m0 * ldo + lower] = from_float<TO>(s.x);
+                if (m1 < M) out[(size_t)m1 * ldo + lower] = from_float<TO>(s.y);
+            }
+            if (MODE == GM_FULL) {
+                const int upper = n0 + rg * 16 + 8 + eg;
+                if (upper < N) {
+                    if (m0 < M) out[(size_t)m0 * ldo + upper] = from_float<TO>(s.z);
+                    if (m1 < M) out[(size_t)m1 * ldo + upper] = from_float<TO>(s.w);
+                }
+            }
+        }
+    }
+}
+
+template <int NB, int RG, int MODE, typename TO>
+static int gemv_mma_launch(const void* x, const void* w, void* out, int M, int N, int K, int ldx, int ldw, int ldo,
+                           int pair_offset, cudaStream_t stream) {
+    constexpr int rows = ((MODE == GM_FULL) ? 16 : 8) * RG;
+    const size_t smem = (size_t)GM_WARPS * RG * NB * 32 * sizeof(float4);
+    auto kernel = gemv_mma_kernel<NB, RG, MODE, TO>;
+    static bool configured = false;
+    if (!configured && smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return (int)e;
+    }
+    configured = true;
+    kernel<<<(N + rows - 1) / rows, GM_THREADS, smem, stream>>>(
+        (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (TO*)out, M, N, K, ldx, ldw, ldo, pair_offset);
+    return ttb_launch_status();
+}
+
+template <int MODE, typename TO>
+static int gemv_mma_by_rows(const void* x, const void* w, void* out, int M, int N, int K, int ldx, int ldw, int ldo,
+                            int pair_offset, cudaStream_t stream) {
+#define GM_GO(NB, RG) return gemv_mma_launch<NB, RG, MODE, TO>(x, w, out, M, N, K, ldx, ldw, ldo, pair_offset, stream)
+    if (M <= 8) GM_GO(1, 1);
+    if (M <= 16) GM_GO(2, 1);
+    if (M <= 32) GM_GO(4, 1);
+    GM_GO(8, 2);
+#undef GM_GO
+}
+
+// x [M, K] bfloat16, w [N, K] bfloat16, out [M, N] bfloat16 or float32; M <= 64, K a multiple of 8.
+// pair_rows > 0: w holds N gate rows followed (pair_rows rows further down) by N up rows, and
+// out[m, n] = silu(x . gate_n) * (x . up_n).
+TTB_EXPORT int ttb_gemv_mma(const void* x, const void* w, void* out, int out_dtype, int M, int N, int K, int ldx,
+                            int ldw, int ldo, int pair_rows, cudaStream_t stream) {
+    if (M == 0 || N == 0) return TTB_OK;
+    if (!x || !w || !out) return TTB_ERR_ARGUMENT;
+    if (M > 64 || K < 8 || (K & 7) || (ldx & 7) || (ldw & 7) || !aligned16(x) || !aligned16(w)) return TTB_ERR_UNSUPPORTED;
+    const bool f32 = out_dtype == TTB_DTYPE_F32;
+    if (!f32 && out_dtype != TTB_DTYPE_BF16) return TTB_ERR_UNSUPPORTED;
+    if (pair_rows > 0) {
+        return f32 ? gemv_mma_by_rows<GM_PAIR, float>(x, w, out, M, N, K, ldx, ldw, ldo, pair_rows, stream)
+                   : gemv_mma_by_rows<GM_PAIR, __nv_bfloat16>(x, w, out, M, N, K, ldx, ldw, ldo, pair_rows, stream);
+    }
+    // matrices with few rows get 8-row fragments, so that there are blocks enough for every SM
+    const bool half = (N / 16) < 2 * 148 && M <= 32;
+    if (half)
+        return f32 ? gemv_mma_by_rows<GM_HALF, float>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream)
+                   : gemv_mma_by_rows<GM_HALF, __nv_bfloat16>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream);
+    return f32 ? gemv_mma_by_rows<GM_FULL, float>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream)
+               : gemv_mma_by_rows<GM_FULL, __nv_bfloat16>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream);
+}

@@ -54,6 +54,10 @@ class Engine:
         self._staging_events = [None, None]
         self._staging_turn = 0
         self.steps_run = 0
+        self.graphs = None
+        if config.cuda_graph and runtime.device.type == "cuda" and model.graph_safe():
+            from .graph import DecodeGraphs
+            self.graphs = DecodeGraphs(self)
 
     # ------------------------------------------------------------------ requests
     def admit(self, request_id) -> None:
@@ -77,22 +81,31 @@ class Engine:
             self._staging[i] = torch.empty(max(count, 4096), dtype=torch.int32, pin_memory=self._pinned)
         return self._staging[i][:count]
 
+    def _record_staging(self) -> None:
+        """Mark the point after which the host buffer handed out last may be written again."""
+        if self._staging_events[self._staging_turn] is None:
+            self._staging_events[self._staging_turn] = torch.cuda.Event()
+        self._staging_events[self._staging_turn].record()
+
     def _to_device(self, host: torch.Tensor) -> torch.Tensor:
         if not self._pinned:
             return host.clone()
         dev = host.to(self.runtime.device, non_blocking=True)
-        if self._staging_events[self._staging_turn] is None:
-            self._staging_events[self._staging_turn] = torch.cuda.Event()
-        self._staging_events[self._staging_turn].record()
+        self._record_staging()
         return dev
 
-    def build_batch(self, entries: List[StepEntry], table_width: Optional[int] = None) -> StepBatch:
-        """Host lists -> one packed int32 buffer -> one copy to the device -> StepBatch."""
+    def _fill_host(self, entries: List[StepEntry], pad_to: int = 0, table_width: Optional[int] = None,
+                   want_all: bool = False):
+        """The step's metadata as one packed int32 host buffer. With pad_to, segments of one
+        token at position 0 on the scratch page are appended until there are pad_to segments
+        (a captured decode step has a fixed number of rows). Returns (host, layout, lists)."""
         cache = self.cache
         seg_lens = [len(e.tokens) for e in entries]
         seg_pos0 = [cache.length(e.request_id) for e in entries]
         seg_slot = [cache.slot(e.request_id) for e in entries]
-        T, R = sum(seg_lens), len(entries)
+        real = len(entries)
+        pad = max(0, pad_to - real)
+        T, R = sum(seg_lens) + pad, real + pad
         want_rows, base = [], 0
         for e, n in zip(entries, seg_lens):
             for w in e.want:
@@ -100,6 +113,8 @@ class Engine:
                     raise ValueError(f"request {e.request_id!r}: wanted place {w} is outside its {n} tokens")
                 want_rows.append(base + w)
             base += n
+        if want_all:
+            want_rows = list(range(T))
         N = len(want_rows)
         max_context = max(p + n for p, n in zip(seg_pos0, seg_lens))
         groups = cache.paged_groups()
@@ -114,37 +129,55 @@ class Engine:
         total = o_tab + len(groups) * _round4(R * W)
         host = self._stage(total)
         buf = host.numpy()
-        tokens = np.fromiter((t for e in entries for t in e.tokens), dtype=np.int64, count=T)
-        if T and (tokens.min() < 0 or tokens.max() >= self.vocab_size):
+        tokens = np.fromiter((t for e in entries for t in e.tokens), dtype=np.int64, count=T - pad)
+        if tokens.size and (tokens.min() < 0 or tokens.max() >= self.vocab_size):
             raise ValueError(f"a token id lies outside the vocabulary of {self.vocab_size}")
-        buf[o_tok:o_tok + T] = tokens
-        lens = np.asarray(seg_lens, dtype=np.int32)
+        seg_lens_all = seg_lens + [1] * pad
+        pos0_all = seg_pos0 + [0] * pad
+        slot_all = seg_slot + [0] * pad
+        buf[o_tok:o_tok + T - pad] = tokens
+        buf[o_tok + T - pad:o_tok + T] = 0
+        lens = np.asarray(seg_lens_all, dtype=np.int32)
         cu = np.zeros(R + 1, dtype=np.int32)
         np.cumsum(lens, out=cu[1:])
         seg_ids = np.repeat(np.arange(R, dtype=np.int32), lens)
-        pos0 = np.asarray(seg_pos0, dtype=np.int32)
+        pos0 = np.asarray(pos0_all, dtype=np.int32)
         buf[o_seg:o_seg + T] = seg_ids
         buf[o_pos:o_pos + T] = np.arange(T, dtype=np.int32) - cu[:-1][seg_ids] + pos0[seg_ids]
         buf[o_cu:o_cu + R + 1] = cu
         buf[o_p0:o_p0 + R] = pos0
-        buf[o_slot:o_slot + R] = seg_slot
+        buf[o_slot:o_slot + R] = slot_all
         buf[o_want:o_want + N] = want_rows
         for i, g in enumerate(groups):
             start = o_tab + i * _round4(R * W)
-            buf[start:start + R * W] = cache.table_rows(g, seg_slot, W).reshape(-1)
-        dev = self._to_device(host)
+            buf[start:start + real * W] = cache.table_rows(g, seg_slot, W).reshape(-1)
+            buf[start + real * W:start + R * W] = 0
+        layout = dict(T=T, R=R, N=N, W=W, o_tok=o_tok, o_pos=o_pos, o_seg=o_seg, o_cu=o_cu, o_p0=o_p0, o_slot=o_slot,
+                      o_want=o_want, o_tab=o_tab, total=total, groups=groups)
+        lists = dict(seg_lens=seg_lens_all, seg_pos0=pos0_all, seg_slot=slot_all, max_context=max_context)
+        return host, layout, lists
+
+    def _batch_from(self, dev: torch.Tensor, layout: dict, lists: dict) -> StepBatch:
+        L = layout
+        T, R, N, W = L["T"], L["R"], L["N"], L["W"]
         batch = StepBatch(
             num_tokens=T, num_segments=R,
-            token_ids=dev[o_tok:o_tok + T], positions=dev[o_pos:o_pos + T], seg_of_token=dev[o_seg:o_seg + T],
-            cu_seqlens=dev[o_cu:o_cu + R + 1], seg_pos0=dev[o_p0:o_p0 + R], seg_slot=dev[o_slot:o_slot + R],
-            want_rows=dev[o_want:o_want + N], num_wanted=N,
-            seg_lens=seg_lens, seg_pos0_list=seg_pos0, seg_slot_list=seg_slot,
-            max_seg_len=max(seg_lens), max_context=max_context,
+            token_ids=dev[L["o_tok"]:L["o_tok"] + T], positions=dev[L["o_pos"]:L["o_pos"] + T],
+            seg_of_token=dev[L["o_seg"]:L["o_seg"] + T], cu_seqlens=dev[L["o_cu"]:L["o_cu"] + R + 1],
+            seg_pos0=dev[L["o_p0"]:L["o_p0"] + R], seg_slot=dev[L["o_slot"]:L["o_slot"] + R],
+            want_rows=dev[L["o_want"]:L["o_want"] + N], num_wanted=N,
+            seg_lens=lists["seg_lens"], seg_pos0_list=lists["seg_pos0"], seg_slot_list=lists["seg_slot"],
+            max_seg_len=max(lists["seg_lens"]), max_context=lists["max_context"],
         )
-        for i, g in enumerate(groups):
-            start = o_tab + i * _round4(R * W)
+        for i, g in enumerate(L["groups"]):
+            start = L["o_tab"] + i * _round4(R * W)
             batch.block_tables[g] = dev[start:start + R * W].view(R, W)
         return batch
+
+    def build_batch(self, entries: List[StepEntry], table_width: Optional[int] = None) -> StepBatch:
+        """Host lists -> one packed int32 buffer -> one copy to the device -> StepBatch."""
+        host, layout, lists = self._fill_host(entries, table_width=table_width)
+        return self._batch_from(self._to_device(host), layout, lists)
 
     # ------------------------------------------------------------------ the step
     def step(self, entries: List[StepEntry]) -> torch.Tensor:
@@ -177,8 +210,11 @@ class Engine:
                 elif self.cache.is_live(e.request_id):
                     self.cache.trim(e.request_id)
             raise
-        batch = self.build_batch(entries)
-        logits = self.model.forward(batch, self.cache)
+        if self.graphs is not None and total == len(entries):
+            logits = self.graphs.run(entries)              # one token per request: replay a captured step
+        else:
+            batch = self.build_batch(entries)
+            logits = self.model.forward(batch, self.cache)
         for e in entries:
             self.cache.commit(e.request_id, self.cache.length(e.request_id) + len(e.tokens))
         self.steps_run += 1

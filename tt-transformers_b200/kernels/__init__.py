@@ -49,6 +49,9 @@ class CudaKernels:
     # bfloat16 products with more rows than this go to the library; fewer rows stream the
     # weights through the hand-written skinny kernel.
     SKINNY_ROWS = 8
+    # bfloat16 products with up to this many rows stream the weights through the tensor-core
+    # skinny kernel (K a multiple of 8)
+    TENSOR_SKINNY_ROWS = 64
 
     def __init__(self, device: torch.device):
         if not torch.cuda.is_available():
@@ -65,7 +68,8 @@ class CudaKernels:
         self.library_path = path
         for name in ("ttb_embedding", "ttb_add_rmsnorm", "ttb_swiglu", "ttb_gather_rows", "ttb_rope_kv_write",
                      "ttb_paged_attention_generic", "ttb_gemm_simt", "ttb_gemv", "ttb_sample",
-                     "ttb_paged_attention_mma", "ttb_attention_mma_tile_rows", "ttb_attention_mma_supports"):
+                     "ttb_paged_attention_mma", "ttb_attention_mma_tile_rows", "ttb_attention_mma_supports",
+                     "ttb_gemv_mma"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -150,6 +154,12 @@ class CudaKernels:
             raise KernelError(f"linear: x {tuple(x.shape)} {x.dtype} does not match w {tuple(w.shape)} {w.dtype}")
         if x.stride(1) != 1 or w.stride(1) != 1:
             raise KernelError("linear: operands must be contiguous along K")
+        if (x.dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS and K % 8 == 0 and x.stride(0) % 8 == 0
+                and w.stride(0) % 8 == 0):
+            out = torch.empty(M, N, dtype=out_dtype, device=self.device)
+            self._check(self.lib.ttb_gemv_mma(self._p(x), self._p(w), self._p(out), _dtype_code(out_dtype), M, N, K,
+                                              x.stride(0), w.stride(0), N, 0, self._stream()), "gemv_mma")
+            return out
         if M <= self.SKINNY_ROWS:
             out = torch.empty(M, N, dtype=out_dtype, device=self.device)
             self._check(self.lib.ttb_gemv(self._p(x), self._p(w), self._p(out), _dtype_code(x.dtype),
@@ -166,6 +176,19 @@ class CudaKernels:
                                            _dtype_code(out_dtype), M, N, K, x.stride(0), w.stride(0), N,
                                            self._stream()), "gemm_simt")
         return out
+
+    def linear_swiglu(self, x: torch.Tensor, w_gate_up: torch.Tensor) -> torch.Tensor:
+        """silu(x Wg^T) * (x Wu^T) for w_gate_up = [Wg; Wu] stacked along the rows -> [M, rows / 2]."""
+        M, K = x.shape
+        inter = w_gate_up.shape[0] // 2
+        if (x.dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS and K % 8 == 0 and x.stride(0) % 8 == 0
+                and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1 and w_gate_up.stride(1) == 1):
+            out = torch.empty(M, inter, dtype=x.dtype, device=self.device)
+            self._check(self.lib.ttb_gemv_mma(self._p(x), self._p(w_gate_up), self._p(out), _dtype_code(x.dtype), M,
+                                              inter, K, x.stride(0), w_gate_up.stride(0), inter, inter,
+                                              self._stream()), "gemv_mma_swiglu")
+            return out
+        return self.swiglu(self.linear(x, w_gate_up))
 
     # ------------------------------------------------------------------ attention
     def rope_kv_write(self, qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True):

@@ -21,6 +21,8 @@ from .base import Mixer, PagedKV, PositionEncoding, TensorSpec, register_part
 
 
 class Attention(Mixer):
+    graph_safe = True
+
     def __init__(self, width: int, heads: int, kv_heads: int, head_dim: int, prefix: str,
                  position: Optional[PositionEncoding] = None, scale: Optional[float] = None,
                  window: Optional[int] = None):

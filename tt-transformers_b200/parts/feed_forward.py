@@ -12,6 +12,8 @@ from .base import FeedForward, TensorSpec, register_part
 
 
 class SwiGLU(FeedForward):
+    graph_safe = True
+
     def __init__(self, width: int, inter: int, prefix: str):
         self.width, self.inter, self.prefix = int(width), int(inter), prefix
 
@@ -29,7 +31,7 @@ class SwiGLU(FeedForward):
 
     def forward(self, x, batch):
         k = self.runtime.kernels
-        return k.linear(k.swiglu(k.linear(x, self.w_gate_up)), self.w_down)
+        return k.linear(k.linear_swiglu(x, self.w_gate_up), self.w_down)
 
 
 register_part("feed_forward", "swiglu", SwiGLU)

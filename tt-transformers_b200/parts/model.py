@@ -105,6 +105,12 @@ class DecoderModel:
         for part in self.all_parts():
             part.bind(tensors, runtime)
 
+    def graph_safe(self) -> bool:
+        """True if every mixer and feed-forward says that its forward only launches kernels
+        on the current stream with shapes fixed by the batch's shape (no host reads, no
+        per-step host tables), so that a decode step may be captured and replayed."""
+        return all(getattr(p, "graph_safe", False) for b in self.layers for p in (b.mixer, b.feed_forward))
+
     # ------------------------------------------------------------------ cache needs
     def cache_requests(self):
         """For every entry of the layer order: what its cache unit must be (PagedKV,
