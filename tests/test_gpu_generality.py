@@ -1,0 +1,214 @@
+"""The framework takes parts and architectures it has never seen, without a change to its files:
+a toy mixer with a running state of its own, a layer order that names a layer twice and lets a
+layer read another layer's cache, and layers with and without a window side by side."""
+
+from dataclasses import dataclass
+
+import pytest
+import torch
+
+import helpers
+import plain_llama
+from tt_transformers_b200 import register_architecture, register_part
+from tt_transformers_b200.config import EngineConfig
+from tt_transformers_b200.engine.step import build_engine
+from tt_transformers_b200.parts import LayerCall, LayerSpec, Mixer, ModelSpec, PartSpec, SlotState, TensorSpec
+from tt_transformers_b200.weights import write_model_folder
+
+pytestmark = pytest.mark.gpu
+
+
+# ---------------------------------------------------------------------------- a toy mixer with state
+class RunningMeanMixer(Mixer):
+    """y_t = W * mean(x_0 .. x_t). Its state per request: the running sum (width numbers); the
+    count is the position. Defined here, in the test, with plain torch operations."""
+
+    def __init__(self, width, weight_name, position=None):
+        self.width, self.weight_name = width, weight_name
+
+    def tensor_specs(self):
+        return [TensorSpec(self.weight_name, (self.width, self.width))]
+
+    def bind(self, tensors, runtime):
+        super().bind(tensors, runtime)
+        self.weight = runtime.matrix(tensors[self.weight_name])
+
+    def cache_request(self):
+        return SlotState((self.width,))
+
+    def forward(self, x, batch, cache, write_cache=True):
+        out = torch.empty_like(x)
+        start = 0
+        for n, pos0, slot in zip(batch.seg_lens, batch.seg_pos0_list, cache.slot_list):
+            sums = cache.state[slot] + torch.cumsum(x[start:start + n].float(), dim=0)
+            counts = torch.arange(pos0 + 1, pos0 + n + 1, device=x.device, dtype=torch.float32)[:, None]
+            out[start:start + n] = ((sums / counts).to(x.dtype) @ self.weight.t())
+            if write_cache:
+                cache.state[slot] = sums[-1]
+            start += n
+        return out
+
+
+@dataclass(frozen=True)
+class ToyConfig:
+    width: int
+    layers: int
+    vocab: int
+    inter: int
+    eps: float
+
+
+def toy_load_config(d):
+    return ToyConfig(d["width"], d["layers"], d["vocab"], d["inter"], d["eps"])
+
+
+def toy_model_spec(cfg):
+    layers = tuple(LayerSpec(
+        norm1=PartSpec("rmsnorm", dict(width=cfg.width, eps=cfg.eps, weight_name=f"toy.{i}.norm1")),
+        mixer=PartSpec("running_mean", dict(width=cfg.width, weight_name=f"toy.{i}.mix")),
+        norm2=PartSpec("rmsnorm", dict(width=cfg.width, eps=cfg.eps, weight_name=f"toy.{i}.norm2")),
+        feed_forward=PartSpec("swiglu", dict(width=cfg.width, inter=cfg.inter, prefix=f"toy.{i}.ff.")),
+    ) for i in range(cfg.layers))
+    return ModelSpec(vocab_size=cfg.vocab, width=cfg.width, embedding_name="toy.embed", layers=layers,
+                     order=tuple(LayerCall(i) for i in range(cfg.layers)),
+                     final_norm=PartSpec("rmsnorm", dict(width=cfg.width, eps=cfg.eps, weight_name="toy.norm")),
+                     head_name="toy.head")
+
+
+def toy_plain_forward(cfg, w, tokens):
+    x = w["toy.embed"][torch.as_tensor(tokens)]
+    counts = torch.arange(1, len(tokens) + 1, dtype=torch.float32)[:, None]
+    for i in range(cfg["layers"]):
+        h = plain_llama.rms_norm(x, w[f"toy.{i}.norm1"], cfg["eps"])
+        x = x + (torch.cumsum(h, 0) / counts) @ w[f"toy.{i}.mix"].T
+        h = plain_llama.rms_norm(x, w[f"toy.{i}.norm2"], cfg["eps"])
+        x = x + plain_llama.swiglu(h, w, f"toy.{i}.ff.")
+    return plain_llama.rms_norm(x, w["toy.norm"], cfg["eps"]) @ w["toy.head"].T
+
+
+def test_a_toy_mixer_with_state_is_registered_built_and_stepped(tmp_path):
+    register_part("mixer", "running_mean", RunningMeanMixer)
+    register_architecture("ToyRunningMeanForTests", toy_load_config, toy_model_spec)
+    cfg = {"architectures": ["ToyRunningMeanForTests"], "width": 48, "layers": 2, "vocab": 100, "inter": 72, "eps": 1e-5}
+    folder = write_model_folder(str(tmp_path / "toy"), cfg, seed=5, std=0.2, norm_std=0.1, dtype=torch.float32)
+    _, w = plain_llama.read_model_folder(folder)
+    requests = {f"r{i}": helpers.random_tokens(100, n, i) for i, n in enumerate((9, 30, 17, 5, 22))}
+    ref = {rid: toy_plain_forward(cfg, w, toks) for rid, toks in requests.items()}
+    for dtype, tol in (("float32", 1e-4), ("bfloat16", 5e-2)):
+        engine = build_engine(folder, EngineConfig(dtype=dtype, max_batch_size=4, max_seq_len=64, device="cuda:0"))
+        assert engine.graphs is None                      # a mixer that reads host lists is never captured
+        assert [type(g.request).__name__ for g in engine.cache.groups] == ["SlotState"]
+        for steps in (helpers.steps_whole(requests), helpers.steps_portions(requests), helpers.steps_mixed(requests)):
+            got = helpers.run_steps(engine, steps)
+            for rid in ref:
+                assert helpers.relative_error(got[rid], ref[rid]) < tol, (dtype, rid)
+        assert engine.cache.free_slots == 4
+        engine.close()
+
+
+# ---------------------------------------------------------------------------- layer order as data; windows
+@dataclass(frozen=True)
+class OrderConfig:
+    width: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    inter: int
+    vocab: int
+    eps: float
+    theta: float
+    windows: tuple          # per layer: None or a window
+    order: tuple            # (layer, cache_of or None)
+
+
+def order_load_config(d):
+    return OrderConfig(d["width"], d["heads"], d["kv_heads"], d["head_dim"], d["inter"], d["vocab"], d["eps"],
+                       d["theta"], tuple(d["windows"]), tuple(tuple(o) for o in d["order"]))
+
+
+def order_model_spec(cfg):
+    rotary = PartSpec("rotary", dict(rotary_dim=cfg.head_dim, theta=cfg.theta, scaling=None))
+    layers = tuple(LayerSpec(
+        norm1=PartSpec("rmsnorm", dict(width=cfg.width, eps=cfg.eps, weight_name=f"l.{i}.n1")),
+        mixer=PartSpec("attention", dict(width=cfg.width, heads=cfg.heads, kv_heads=cfg.kv_heads,
+                                         head_dim=cfg.head_dim, prefix=f"l.{i}.attn.", window=window)),
+        position=rotary,
+        norm2=PartSpec("rmsnorm", dict(width=cfg.width, eps=cfg.eps, weight_name=f"l.{i}.n2")),
+        feed_forward=PartSpec("swiglu", dict(width=cfg.width, inter=cfg.inter, prefix=f"l.{i}.ff.")),
+    ) for i, window in enumerate(cfg.windows))
+    return ModelSpec(vocab_size=cfg.vocab, width=cfg.width, embedding_name="emb", layers=layers,
+                     order=tuple(LayerCall(l, c) for l, c in cfg.order),
+                     final_norm=PartSpec("rmsnorm", dict(width=cfg.width, eps=cfg.eps, weight_name="norm")),
+                     head_name=None)
+
+
+def order_plain_forward(cfg, w, tokens):
+    """Whole sequence, no cache: the layer order run by hand with the plain parts."""
+    T = len(tokens)
+    H, G, hd = cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
+    positions = torch.arange(T)
+    inv_freq = plain_llama.rope_inverse_frequencies(hd, cfg["theta"], None)
+    x = w["emb"][torch.as_tensor(tokens)]
+    kept = {}
+    for entry, (layer, cache_of) in enumerate(cfg["order"]):
+        p = f"l.{layer}."
+        h = plain_llama.rms_norm(x, w[p + "n1"], cfg["eps"])
+        q = plain_llama.rope_rotate((h @ w[p + "attn.q_proj.weight"].T).view(T, H, hd), positions, inv_freq)
+        if cache_of is None:
+            k = plain_llama.rope_rotate((h @ w[p + "attn.k_proj.weight"].T).view(T, G, hd), positions, inv_freq)
+            v = (h @ w[p + "attn.v_proj.weight"].T).view(T, G, hd)
+            kept[entry] = (k, v)
+        else:
+            k, v = kept[cache_of]
+        o = plain_llama.causal_attention(q, k, v, cfg["windows"][layer]).reshape(T, H * hd)
+        x = x + o @ w[p + "attn.o_proj.weight"].T
+        h = plain_llama.rms_norm(x, w[p + "n2"], cfg["eps"])
+        x = x + plain_llama.swiglu(h, w, p + "ff.")
+    return plain_llama.rms_norm(x, w["norm"], cfg["eps"]) @ w["emb"].T
+
+
+@pytest.mark.parametrize("head_dim", [32, 64])
+def test_layer_order_shared_caches_and_windows(tmp_path, head_dim):
+    register_architecture("OrderForTests", order_load_config, order_model_spec)
+    cfg = {"architectures": ["OrderForTests"], "width": 96, "heads": 4, "kv_heads": 2, "head_dim": head_dim,
+           "inter": 160, "vocab": 200, "eps": 1e-5, "theta": 10000.0,
+           "windows": [None, 24, None],
+           # layer 0 runs twice with caches of its own, layer 2 reads the cache of the first entry,
+           # layer 1 keeps a window of 24 keys
+           "order": [[0, None], [1, None], [0, None], [2, 0], [1, None]]}
+    folder = write_model_folder(str(tmp_path / "order"), cfg, seed=9, std=0.08, norm_std=0.1, dtype=torch.float32)
+    _, w = plain_llama.read_model_folder(folder)
+    requests = {f"r{i}": helpers.random_tokens(200, n, 20 + i) for i, n in enumerate((70, 33, 120, 9, 64))}
+    ref = {rid: order_plain_forward(cfg, w, toks) for rid, toks in requests.items()}
+    for dtype, tol in (("float32", 1e-4), ("bfloat16", 5e-2)):
+        for make_steps in (helpers.steps_whole, helpers.steps_decode_tail, helpers.steps_portions, helpers.steps_mixed):
+            steps = make_steps(requests)
+            pages = -(-helpers.max_live_tokens(requests, steps, rounding=8) // 8)
+            engine = build_engine(folder, EngineConfig(dtype=dtype, page_size=8, num_pages=pages, max_batch_size=4,
+                                                       max_seq_len=128, device="cuda:0"))
+            kinds = [(type(g.request).__name__, g.request.window, len(g.units)) for g in engine.cache.groups]
+            assert kinds == [("PagedKV", None, 2), ("PagedKV", 24, 2)]       # entry 3 owns no unit: it reads entry 0's
+            for g in engine.cache.groups:
+                g.storage.fill_(float("nan"))        # a read of a slot that was never written would show
+            got = helpers.run_steps(engine, steps)
+            engine.cache.audit()
+            for rid in ref:
+                assert helpers.relative_error(got[rid], ref[rid]) < tol, (dtype, make_steps.__name__, rid)
+            engine.close()
+
+
+def test_windowed_pages_come_back_while_the_request_lives(tmp_path):
+    register_architecture("OrderForTests", order_load_config, order_model_spec)
+    cfg = {"architectures": ["OrderForTests"], "width": 64, "heads": 2, "kv_heads": 1, "head_dim": 32, "inter": 96,
+           "vocab": 100, "eps": 1e-5, "theta": 10000.0, "windows": [16], "order": [[0, None]]}
+    folder = write_model_folder(str(tmp_path / "win"), cfg, seed=3, std=0.1, dtype=torch.float32)
+    _, w = plain_llama.read_model_folder(folder)
+    tokens = helpers.random_tokens(100, 200, 1)
+    ref = order_plain_forward(cfg, w, tokens)
+    # 200 tokens would need 50 pages of 4; the window of 16 never holds more than 6 (+ the step's own)
+    engine = build_engine(folder, EngineConfig(dtype="float32", page_size=4, num_pages=12, max_batch_size=1,
+                                               max_seq_len=256, device="cuda:0"))
+    steps = helpers.steps_portions({"a": tokens}, sizes=(7, 5, 3, 2, 2, 11, 4, 2, 16, 9))
+    got = helpers.run_steps(engine, steps)
+    assert helpers.relative_error(got["a"], ref) < 1e-4
+    assert engine.cache.free_pages() == 12

@@ -124,6 +124,7 @@ class Scheduler:
     def schedule(self) -> List[PlannedEntry]:
         plan: List[PlannedEntry] = []
         budget = self.max_step_tokens
+        preempted_before = self.preemptions
         for req in list(self.running):
             if req not in self.running or budget == 0:
                 continue
@@ -148,13 +149,17 @@ class Scheduler:
             self.cache.reserve(req.request_id, req.num_computed + count)
             plan.append(PlannedEntry(req, req.num_computed, count, sample=req.num_computed + count == len(req.all_tokens)))
             budget -= count
-        while self.waiting and budget > 0 and self.cache.free_slots > 0:
+        # nobody is admitted in a step in which somebody had to give way
+        while (self.waiting and budget > 0 and self.cache.free_slots > 0
+               and self.preemptions == preempted_before):
             req = self.waiting[0]
             pending = len(req.all_tokens)
             count = min(pending, self.max_chunk_tokens, budget)
             fit = min(count, self.cache.room())
             if fit < 1:
                 break
+            if req.preemptions and self.running and self.cache.room() < pending + 1:
+                break      # one that gave way comes back when all it has fits beside the others, not to give way again
             self.waiting.popleft()
             self.cache.admit(req.request_id)
             self.cache.reserve(req.request_id, fit)

@@ -192,6 +192,11 @@ class Engine:
             if e.request_id in seen:
                 raise ValueError(f"request {e.request_id!r} appears twice in one step")
             seen.add(e.request_id)
+            if min(e.tokens) < 0 or max(e.tokens) >= self.vocab_size:
+                raise ValueError(f"request {e.request_id!r}: a token id lies outside the vocabulary of {self.vocab_size}")
+            for w in e.want:
+                if not 0 <= w < len(e.tokens):
+                    raise ValueError(f"request {e.request_id!r}: wanted place {w} is outside its {len(e.tokens)} tokens")
         total = sum(len(e.tokens) for e in entries)
         if total > self.config.max_step_tokens:
             raise ValueError(f"the step holds {total} tokens; the budget is {self.config.max_step_tokens}")
