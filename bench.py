@@ -104,6 +104,23 @@ def prefill_flops(cfg, layers, tokens):
     return layers * (linear + attention) + 2 * vocab * d            # plus one row of logits
 
 
+def reference_arm() -> dict:
+    """The reference's own generation path needs its vendor's accelerator library (ttnn) and a
+    Tenstorrent device. If the package under baseline/_ref and that library import, its stock
+    loader would be driven here; where they do not, the arm says so in one line."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "tt_transformers")):
+        return {"impl": "reference", "unavailable": "baseline/_ref holds no installed tt_transformers package"}
+    sys.path.insert(0, ref)
+    try:
+        import ttnn  # noqa: F401
+    except Exception as e:            # not installed here: there is no wheel of it offline and no CUDA backend
+        return {"impl": "reference", "unavailable":
+                f"tt_transformers is installed under baseline/_ref (--no-deps), but its accelerator library "
+                f"cannot be imported ({type(e).__name__}: {e}); every forward op of the reference is a call into it"}
+    return {"impl": "reference", "unavailable": "ttnn imported, but no Tenstorrent device is present on a B200 box"}
+
+
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -122,9 +139,7 @@ def main(argv=None) -> int:
     args = parser.parse_args(argv)
 
     if args.impl == "reference":
-        print(json.dumps({"impl": "reference", "unavailable":
-                          "the reference runs only on its vendor's accelerator library (ttnn), which is not "
-                          "installed here and has no CUDA backend"}))
+        print(json.dumps(reference_arm()))
         return 0
     if args.gpus != 1:
         print(f"bench.py: this engine runs on one GPU; --gpus {args.gpus} is not supported")
