@@ -402,3 +402,47 @@ TTB_EXPORT int ttb_paged_attention_mma(const void* qkv, int q_row_stride, void* 
     return decode_shape ? launch_attention<128, 1, 4>(AM_ARGS) : launch_attention<128, 4, 1>(AM_ARGS);
 #undef AM_ARGS
 }
+
+// ---------------------------------------------------------------------------------------------
+// The same decode attention for callers that cannot allocate (see no_alloc.h). The partial
+// results of the key splits go to this array in the library image instead of to memory that
+// the caller or an allocator provides.
+#include "no_alloc.h"
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[TTB_NOALLOC_SCRATCH_BYTES];
+
+#define TTB_NOALLOC_MAX_DEVICES 64
+// In host code `g_noalloc_scratch` is only a handle for the symbol, not a device address; the
+// address of each device's copy is looked up once, with that device current.
+static float* g_noalloc_device_ptr[TTB_NOALLOC_MAX_DEVICES];
+
+TTB_EXPORT unsigned int ttb_noalloc_scratch_bytes(void) { return TTB_NOALLOC_SCRATCH_BYTES; }
+
+TTB_EXPORT int ttb_paged_attention_decode_noalloc(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens,
+                                                  const int* seg_pos0, const void* key_pages, const void* value_pages,
+                                                  const int* block_table, int table_width, int page_size, int segments,
+                                                  int heads, int kv_heads, int head_dim, float scale, int window,
+                                                  int num_splits, cudaStream_t stream) {
+    if (segments == 0) return TTB_OK;
+    if (segments < 0 || num_splits < 1 || heads < 1 || head_dim < 1) return TTB_ERR_ARGUMENT;
+    const size_t rows = (size_t)segments * heads * num_splits;
+    const size_t need = rows * ((size_t)head_dim + 2) * sizeof(float);
+    if (need > TTB_NOALLOC_SCRATCH_BYTES) return TTB_ERR_SCRATCH;
+    int device = -1;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return (int)e;
+    if (device < 0 || device >= TTB_NOALLOC_MAX_DEVICES) return TTB_ERR_UNSUPPORTED;
+    if (g_noalloc_device_ptr[device] == nullptr) {          // set-up, once per device
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess) return (int)e;
+        if (ptr == nullptr) return TTB_ERR_ARGUMENT;
+        g_noalloc_device_ptr[device] = static_cast<float*>(ptr);
+    }
+    float* partial_o = g_noalloc_device_ptr[device];
+    float* partial_ml = partial_o + rows * (size_t)head_dim;
+    return ttb_paged_attention_mma(qkv, q_row_stride, out, cu_seqlens, seg_pos0, key_pages, value_pages, block_table,
+                                   table_width, page_size, nullptr, nullptr, segments, segments, heads, kv_heads,
+                                   head_dim, scale, window, /*decode_shape=*/1, num_splits, partial_o, partial_ml,
+                                   stream);
+}
