@@ -259,3 +259,20 @@ def test_sample_distribution(kernels):
     freq = torch.bincount(got.long().cpu(), minlength=5).float() / 4096
     expect = torch.softmax(logits[0].cpu() / 1.5, 0)
     assert float((freq - expect).abs().max()) < 0.03
+
+
+@pytest.mark.parametrize("dtype,head_dim", [(torch.float32, 32), (torch.bfloat16, 32), (torch.bfloat16, 64)])
+def test_attention_does_not_follow_a_page_id_outside_the_pool(kernels, dtype, head_dim):
+    """A block-table entry that points outside the pool is flagged and its keys are left out;
+    nothing outside the pool is read."""
+    from tt_transformers_b200.kernels import EngineDeviceError
+
+    qkv, batch, view = make_paged_case(dtype, 4, 2, head_dim, 16, [(100, 1), (40, 3)], seed=11)
+    kernels.check_status()
+    view.block_table[0, 2] = view.keys.shape[0] + 5
+    view.block_table[1, 0] = -3
+    out = kernels.paged_attention(qkv, batch, 4, 2, head_dim, 0.2, view)
+    assert not torch.isnan(out.float()).any()
+    with pytest.raises(EngineDeviceError, match="page id"):
+        kernels.check_status()
+    kernels.check_status()

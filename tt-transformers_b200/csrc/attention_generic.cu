@@ -21,7 +21,8 @@ paged_attention_generic_kernel(const T* __restrict__ qkv, int q_row_stride, T* _
                                const int* __restrict__ positions, const int* __restrict__ seg_of_token,
                                const T* __restrict__ key_pages, const T* __restrict__ value_pages,
                                const int* __restrict__ block_table, int table_width, int page_size,
-                               int heads, int kv_heads, int head_dim, float scale, int window) {
+                               int heads, int kv_heads, int head_dim, float scale, int window, int num_pages,
+                               int* __restrict__ status) {
     extern __shared__ float smem[];
     float* q = smem;                                   // [head_dim, padded to an even count]
     float* prob = smem + ((head_dim + 1) & ~1);        // [ATT_TILE]
@@ -50,8 +51,13 @@ paged_attention_generic_kernel(const T* __restrict__ qkv, int q_row_stride, T* _
         __syncthreads();   // q ready (first pass); prob and row_offset free (later passes)
         const int key = tile * ATT_TILE + threadIdx.x;
         float score = -INFINITY;
-        if (key >= lo && key <= pos) {
-            const int page = table[key / page_size];
+        int page = (key >= lo && key <= pos) ? table[key / page_size] : -1;
+        if (key >= lo && key <= pos && (unsigned)page >= (unsigned)num_pages) {
+            atomicExch(status, 0x2000000 + t);     // a page id outside the pool: the key is left out
+            row_offset[threadIdx.x] = 0;
+            page = -1;
+        }
+        if (page >= 0) {
             const size_t off = (((size_t)page * kv_heads + g) * page_size + (key % page_size)) * head_dim;
             row_offset[threadIdx.x] = off;
             const T* k = key_pages + off;
@@ -102,9 +108,9 @@ TTB_EXPORT int ttb_paged_attention_generic(const void* qkv, int q_row_stride, vo
                                            const int* positions, const int* seg_of_token, const void* key_pages,
                                            const void* value_pages, const int* block_table, int table_width,
                                            int page_size, int tokens, int heads, int kv_heads, int head_dim,
-                                           float scale, int window, cudaStream_t stream) {
+                                           float scale, int window, int num_pages, int* status, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
-    if (!qkv || !out || !positions || !seg_of_token || !key_pages || !value_pages || !block_table)
+    if (!qkv || !out || !positions || !seg_of_token || !key_pages || !value_pages || !block_table || !status)
         return TTB_ERR_ARGUMENT;
     if (head_dim < 1 || head_dim > ATT_MAX_ACC * ATT_THREADS) return TTB_ERR_UNSUPPORTED;
     if (kv_heads < 1 || heads % kv_heads != 0) return TTB_ERR_UNSUPPORTED;
@@ -116,12 +122,12 @@ TTB_EXPORT int ttb_paged_attention_generic(const void* qkv, int q_row_stride, vo
         paged_attention_generic_kernel<<<grid, ATT_THREADS, smem, stream>>>(
             (const __nv_bfloat16*)qkv, q_row_stride, (__nv_bfloat16*)out, positions, seg_of_token,
             (const __nv_bfloat16*)key_pages, (const __nv_bfloat16*)value_pages, block_table, table_width, page_size,
-            heads, kv_heads, head_dim, scale, window);
+            heads, kv_heads, head_dim, scale, window, num_pages, status);
     } else if (dtype == TTB_DTYPE_F32) {
         if ((head_dim & 7) == 0 && (!aligned16(key_pages))) return TTB_ERR_ARGUMENT;
         paged_attention_generic_kernel<<<grid, ATT_THREADS, smem, stream>>>(
             (const float*)qkv, q_row_stride, (float*)out, positions, seg_of_token, (const float*)key_pages,
-            (const float*)value_pages, block_table, table_width, page_size, heads, kv_heads, head_dim, scale, window);
+            (const float*)value_pages, block_table, table_width, page_size, heads, kv_heads, head_dim, scale, window, num_pages, status);
     } else {
         return TTB_ERR_UNSUPPORTED;
     }

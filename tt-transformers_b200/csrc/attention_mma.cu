@@ -3,8 +3,9 @@
 //
 // A query tile holds 16 * WM rows; a row is one (token, query head of the KV group) pair,
 // token-major, so the heads that share a KV head share every key and value that is loaded.
-// Keys and values stream from the cache pages in tiles of 64 keys through a two-stage
-// cp.async pipeline into swizzled shared memory. Two shapes of the same code:
+// Keys and values stream from the cache pages in tiles of 64 keys through a cp.async pipeline
+// of STAGES tiles into swizzled shared memory; the block-table entries of the block's key range
+// are copied to shared memory first, so that no load of a tile waits for a load of its page id. Two shapes of the same code:
 //   prefill:  WM = 4, WN = 1   four warps, 16 rows each, every warp sees all 64 keys of a tile
 //   decode:   WM = 1, WN = 4   one 16-row tile (a single token's heads), the four warps take
 //                              16 keys each of every tile and merge at the end
@@ -17,6 +18,7 @@
 #include "common.cuh"
 
 #define AM_BN 64
+#define AM_TABLE_CACHE 1024      // block-table entries kept in shared memory per block
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -49,15 +51,16 @@ template <int HD> __device__ __forceinline__ uint32_t tile_offset(int row, int c
     return (uint32_t)(row * HD * 2 + ((chunk ^ (row & 7)) << 4));
 }
 
-template <int HD, int WM, int WN>
+template <int HD, int WM, int WN, int STAGES>
 __global__ void __launch_bounds__(WM * WN * 32)
 attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __nv_bfloat16* __restrict__ out,
                      const int* __restrict__ cu_seqlens, const int* __restrict__ seg_pos0,
                      const __nv_bfloat16* __restrict__ key_pages, const __nv_bfloat16* __restrict__ value_pages,
-                     const int* __restrict__ block_table, int table_width, int page_size,
+                     const int* __restrict__ block_table, int table_width, int page_size, int page_shift,
                      const int* __restrict__ qtile_seg, const int* __restrict__ qtile_tok0,
                      int heads, int kv_heads, float scale_log2, int window, int num_splits,
-                     float* __restrict__ partial_o, float* __restrict__ partial_ml) {
+                     float* __restrict__ partial_o, float* __restrict__ partial_ml, int num_pages,
+                     int* __restrict__ status) {
     constexpr int BM = 16 * WM;
     constexpr int THREADS = WM * WN * 32;
     constexpr int CHUNKS = HD / 8;              // 16-byte chunks per row
@@ -69,9 +72,11 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
 
     extern __shared__ __align__(128) unsigned char smem[];
     unsigned char* q_tile = smem;                               // [BM][HD]
-    unsigned char* k_stage = smem + BM * HD * 2;                // [2][BN][HD]
-    unsigned char* v_stage = k_stage + 2 * TILE_BYTES;          // [2][BN][HD]
+    unsigned char* k_stage = smem + BM * HD * 2;                // [STAGES][BN][HD]
+    unsigned char* v_stage = k_stage + STAGES * TILE_BYTES;     // [STAGES][BN][HD]
+    int* page_cache = reinterpret_cast<int*>(v_stage + STAGES * TILE_BYTES);   // [AM_TABLE_CACHE]
 
+    pdl_wait();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int warp_m = warp / WN, warp_n = warp % WN;
     const int qt = blockIdx.x, g = blockIdx.y, split = blockIdx.z;
@@ -113,16 +118,41 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
             const __nv_bfloat16* src = qkv + (size_t)(seg_start + token) * q_row_stride + (size_t)head * HD + c * 8;
             cp_async16(smem_u32(q_tile + tile_offset<HD>(r, c)), src, ok ? 16 : 0);
         }
+        // block-table entries of this block's keys, first page index `page_base`
+        const int page_base = (page_shift >= 0) ? (k_begin >> page_shift) : (k_begin / page_size);
+        {
+            const int last_page = (page_shift >= 0) ? ((k_end - 1) >> page_shift) : ((k_end - 1) / page_size);
+            const int count = min(last_page - page_base + 1, AM_TABLE_CACHE);
+            for (int i = tid; i < count; i += THREADS) page_cache[i] = table[page_base + i];
+        }
+        __syncthreads();
         auto load_tile = [&](int tile, int stage) {
             const int kb = k_begin + tile * AM_BN;
-            for (int idx = tid; idx < AM_BN * CHUNKS; idx += THREADS) {
+#pragma unroll
+            for (int it = 0; it < (AM_BN * CHUNKS + THREADS - 1) / THREADS; ++it) {
+                const int idx = tid + it * THREADS;
+                if ((AM_BN * CHUNKS) % THREADS != 0 && idx >= AM_BN * CHUNKS) break;
                 const int r = idx / CHUNKS, c = idx % CHUNKS;
                 const int key = kb + r;
-                const bool ok = key < k_end;
+                bool ok = key < k_end;
                 size_t off = 0;
                 if (ok) {
-                    const int page = table[key / page_size];
-                    off = (((size_t)page * kv_heads + g) * page_size + (key % page_size)) * HD + c * 8;
+                    int page_index, in_page;
+                    if (page_shift >= 0) {
+                        page_index = key >> page_shift;
+                        in_page = key & (page_size - 1);
+                    } else {
+                        page_index = key / page_size;
+                        in_page = key - page_index * page_size;
+                    }
+                    const int rel = page_index - page_base;
+                    const int page = rel < AM_TABLE_CACHE ? page_cache[rel] : table[page_index];
+                    if ((unsigned)page < (unsigned)num_pages) {
+                        off = (((size_t)page * kv_heads + g) * page_size + in_page) * HD + c * 8;
+                    } else {                      // a page id outside the pool: read nothing, say so
+                        if (status != nullptr) atomicExch(status, 0x2000000 + seg);
+                        ok = false;
+                    }
                 }
                 const uint32_t dst = tile_offset<HD>(r, c) + stage * TILE_BYTES;
                 cp_async16(smem_u32(k_stage + dst), key_pages + off, ok ? 16 : 0);
@@ -130,15 +160,18 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
             }
         };
         const int num_tiles = (k_end - k_begin + AM_BN - 1) / AM_BN;
-        load_tile(0, 0);
-        cp_async_commit();
+#pragma unroll
+        for (int st = 0; st < STAGES - 1; ++st) {       // the first group also carries the query tile
+            if (st < num_tiles) load_tile(st, st);
+            cp_async_commit();
+        }
 
         uint32_t q_frag[KS][4];
         for (int tile = 0; tile < num_tiles; ++tile) {
-            const int stage = tile & 1;
-            if (tile + 1 < num_tiles) load_tile(tile + 1, stage ^ 1);
+            const int stage = tile % STAGES;
+            if (tile + STAGES - 1 < num_tiles) load_tile(tile + STAGES - 1, (tile + STAGES - 1) % STAGES);
             cp_async_commit();
-            cp_async_wait<1>();
+            cp_async_wait<STAGES - 1>();
             __syncthreads();
             if (tile == 0) {
 #pragma unroll
@@ -230,6 +263,7 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
         cp_async_wait<0>();
     }
 
+    pdl_launch_dependents();     // the streaming part is over: the next kernel may move in
     // ---- row sums over the four lanes of a quad
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -314,6 +348,8 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
 template <int HD>
 __global__ void attention_merge_kernel(const float* __restrict__ partial_o, const float* __restrict__ partial_ml,
                                        __nv_bfloat16* __restrict__ out, int rows, int num_splits) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -338,17 +374,20 @@ __global__ void attention_merge_kernel(const float* __restrict__ partial_o, cons
     for (int i = 0; i < HD / 32; ++i) out[(size_t)row * HD + lane + 32 * i] = __float2bfloat16_rn(acc[i] * inv);
 }
 
-template <int HD, int WM, int WN>
+template <int HD, int WM, int WN, int STAGES>
 static int launch_attention(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens, const int* seg_pos0,
                             const void* key_pages, const void* value_pages, const int* block_table, int table_width,
                             int page_size, const int* qtile_seg, const int* qtile_tok0, int n_qtiles, int tokens,
                             int heads, int kv_heads, float scale, int window, int num_splits, float* partial_o,
-                            float* partial_ml, cudaStream_t stream) {
+                            float* partial_ml, int num_pages, int* status, cudaStream_t stream) {
     constexpr int BM = 16 * WM;
-    const size_t stage_bytes = (size_t)BM * HD * 2 + 4 * (size_t)AM_BN * HD * 2;
+    const size_t stage_bytes = (size_t)BM * HD * 2 + 2 * (size_t)STAGES * AM_BN * HD * 2 + AM_TABLE_CACHE * sizeof(int);
     const size_t merge_bytes = (size_t)BM * HD * 2 + (size_t)WN * 16 * (HD + 2) * sizeof(float);
     const size_t smem = stage_bytes > merge_bytes ? stage_bytes : merge_bytes;
-    auto kernel = attention_mma_kernel<HD, WM, WN>;
+    auto kernel = attention_mma_kernel<HD, WM, WN, STAGES>;
+    int page_shift = -1;
+    for (int b = 0; b < 31; ++b)
+        if (page_size == (1 << b)) page_shift = b;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -357,19 +396,27 @@ static int launch_attention(const void* qkv, int q_row_stride, void* out, const 
     }
     dim3 grid(n_qtiles, kv_heads, num_splits);
     const float scale_log2 = scale * 1.4426950408889634f;
-    kernel<<<grid, WM * WN * 32, smem, stream>>>(
+    ttb_launch(kernel, grid, dim3(WM * WN * 32), smem, stream,
         (const __nv_bfloat16*)qkv, q_row_stride, (__nv_bfloat16*)out, cu_seqlens, seg_pos0,
         (const __nv_bfloat16*)key_pages, (const __nv_bfloat16*)value_pages, block_table, table_width, page_size,
-        qtile_seg, qtile_tok0, heads, kv_heads, scale_log2, window, num_splits, partial_o, partial_ml);
-    int status = ttb_launch_status();
-    if (status != TTB_OK || num_splits == 1) return status;
+        page_shift, qtile_seg, qtile_tok0, heads, kv_heads, scale_log2, window, num_splits, partial_o, partial_ml,
+        num_pages, status);
+    int launch = ttb_launch_status();
+    if (launch != TTB_OK || num_splits == 1) return launch;
     const int rows = tokens * heads;
-    attention_merge_kernel<HD><<<(rows + 3) / 4, 128, 0, stream>>>(partial_o, partial_ml, (__nv_bfloat16*)out, rows, num_splits);
+    ttb_launch(attention_merge_kernel<HD>, dim3((rows + 3) / 4), dim3(128), 0, stream, (const float*)partial_o,
+               (const float*)partial_ml, (__nv_bfloat16*)out, rows, num_splits);
     return ttb_launch_status();
 }
 
 // Rows of a query tile in each shape: the host cuts segments into tiles of rows / (heads / kv_heads) tokens.
 TTB_EXPORT int ttb_attention_mma_tile_rows(int decode_shape) { return decode_shape ? 16 : 64; }
+
+// Blocks of a shape that fit one SM at a time (by shared memory): what the host sizes key splits by.
+TTB_EXPORT int ttb_attention_mma_blocks_per_sm(int decode_shape, int head_dim) {
+    if (head_dim == 64) return decode_shape ? 3 : 4;
+    return decode_shape ? 2 : 2;
+}
 
 // Whether this kernel takes the geometry at all.
 TTB_EXPORT int ttb_attention_mma_supports(int heads, int kv_heads, int head_dim) {
@@ -382,12 +429,15 @@ TTB_EXPORT int ttb_attention_mma_supports(int heads, int kv_heads, int head_dim)
 // qtile_seg / qtile_tok0 may be null: tile i is then token 0 of segment i.
 // With num_splits > 1, partial_o holds tokens * heads * num_splits * head_dim floats and partial_ml
 // tokens * heads * num_splits * 2 floats of scratch memory.
-TTB_EXPORT int ttb_paged_attention_mma(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens,
-                                       const int* seg_pos0, const void* key_pages, const void* value_pages,
-                                       const int* block_table, int table_width, int page_size, const int* qtile_seg,
-                                       const int* qtile_tok0, int n_qtiles, int tokens, int heads, int kv_heads,
-                                       int head_dim, float scale, int window, int decode_shape, int num_splits,
-                                       float* partial_o, float* partial_ml, cudaStream_t stream) {
+// Pages are [num_pages, kv_heads, page_size, head_dim]; a block-table entry outside 0 .. num_pages-1 is not
+// followed: the keys it stands for are left out and `status` (if not null) is set.
+static int paged_attention_mma_impl(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens,
+                                    const int* seg_pos0, const void* key_pages, const void* value_pages,
+                                    const int* block_table, int table_width, int page_size, const int* qtile_seg,
+                                    const int* qtile_tok0, int n_qtiles, int tokens, int heads, int kv_heads,
+                                    int head_dim, float scale, int window, int decode_shape, int num_splits,
+                                    float* partial_o, float* partial_ml, int num_pages, int* status,
+                                    cudaStream_t stream) {
     if (n_qtiles == 0 || tokens == 0) return TTB_OK;
     if (!qkv || !out || !cu_seqlens || !seg_pos0 || !key_pages || !value_pages || !block_table) return TTB_ERR_ARGUMENT;
     if (!ttb_attention_mma_supports(heads, kv_heads, head_dim)) return TTB_ERR_UNSUPPORTED;
@@ -397,10 +447,37 @@ TTB_EXPORT int ttb_paged_attention_mma(const void* qkv, int q_row_stride, void* 
         return TTB_ERR_ARGUMENT;
     if (decode_shape && heads / kv_heads > 16) return TTB_ERR_UNSUPPORTED;
 #define AM_ARGS qkv, q_row_stride, out, cu_seqlens, seg_pos0, key_pages, value_pages, block_table, table_width, page_size, \
-                qtile_seg, qtile_tok0, n_qtiles, tokens, heads, kv_heads, scale, window, num_splits, partial_o, partial_ml, stream
-    if (head_dim == 64) return decode_shape ? launch_attention<64, 1, 4>(AM_ARGS) : launch_attention<64, 4, 1>(AM_ARGS);
-    return decode_shape ? launch_attention<128, 1, 4>(AM_ARGS) : launch_attention<128, 4, 1>(AM_ARGS);
+                qtile_seg, qtile_tok0, n_qtiles, tokens, heads, kv_heads, scale, window, num_splits, partial_o, partial_ml, \
+                num_pages, status, stream
+    if (head_dim == 64) return decode_shape ? launch_attention<64, 1, 4, 4>(AM_ARGS) : launch_attention<64, 4, 1, 3>(AM_ARGS);
+    return decode_shape ? launch_attention<128, 1, 4, 3>(AM_ARGS) : launch_attention<128, 4, 1, 2>(AM_ARGS);
 #undef AM_ARGS
+}
+
+TTB_EXPORT int ttb_paged_attention_mma(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens,
+                                       const int* seg_pos0, const void* key_pages, const void* value_pages,
+                                       const int* block_table, int table_width, int page_size, const int* qtile_seg,
+                                       const int* qtile_tok0, int n_qtiles, int tokens, int heads, int kv_heads,
+                                       int head_dim, float scale, int window, int decode_shape, int num_splits,
+                                       float* partial_o, float* partial_ml, cudaStream_t stream) {
+    return paged_attention_mma_impl(qkv, q_row_stride, out, cu_seqlens, seg_pos0, key_pages, value_pages, block_table,
+                                    table_width, page_size, qtile_seg, qtile_tok0, n_qtiles, tokens, heads, kv_heads,
+                                    head_dim, scale, window, decode_shape, num_splits, partial_o, partial_ml,
+                                    0x7fffffff, nullptr, stream);
+}
+
+// The same with the pool's size and a status word, as the engine calls it.
+TTB_EXPORT int ttb_paged_attention_mma_checked(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens,
+                                               const int* seg_pos0, const void* key_pages, const void* value_pages,
+                                               const int* block_table, int table_width, int page_size,
+                                               const int* qtile_seg, const int* qtile_tok0, int n_qtiles, int tokens,
+                                               int heads, int kv_heads, int head_dim, float scale, int window,
+                                               int decode_shape, int num_splits, float* partial_o, float* partial_ml,
+                                               int num_pages, int* status, cudaStream_t stream) {
+    return paged_attention_mma_impl(qkv, q_row_stride, out, cu_seqlens, seg_pos0, key_pages, value_pages, block_table,
+                                    table_width, page_size, qtile_seg, qtile_tok0, n_qtiles, tokens, heads, kv_heads,
+                                    head_dim, scale, window, decode_shape, num_splits, partial_o, partial_ml,
+                                    num_pages, status, stream);
 }
 
 // ---------------------------------------------------------------------------------------------

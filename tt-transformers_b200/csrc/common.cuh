@@ -3,6 +3,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #define TTB_OK 0
 #define TTB_ERR_UNSUPPORTED (-2)   // a size or option this kernel does not take
@@ -12,6 +13,42 @@
 #define TTB_DTYPE_BF16 1
 
 #define TTB_EXPORT extern "C" __attribute__((visibility("default")))
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels of one step run back to back on one stream. Launched with the attribute below, a kernel
+// may become resident while its predecessor is still running: everything before pdl_wait() (index
+// arithmetic, prefetching weights, which no kernel of the step writes) overlaps the predecessor's
+// tail; pdl_wait() returns once the predecessor has completed and its writes are visible. Every
+// kernel launched this way calls pdl_launch_dependents() first and pdl_wait() before it reads or
+// writes anything another kernel of the step touches. TTB200_PDL=0 in the environment turns the
+// attribute off (the two device calls are then no-ops).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+static inline int ttb_pdl_enabled() {
+    static int enabled = -1;
+    if (enabled < 0) {
+        const char* e = getenv("TTB200_PDL");
+        enabled = (e && e[0] == '0') ? 0 : 1;
+    }
+    return enabled;
+}
+
+template <typename... KArgs, typename... Args>
+static inline void ttb_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = ttb_pdl_enabled() ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);   // errors surface in ttb_launch_status()
+}
 
 static inline int ttb_launch_status() {
     cudaError_t e = cudaGetLastError();

@@ -4,8 +4,10 @@
 // so a handful of tokens costs no more tensor work than one. Every weight is read from HBM
 // once, with 16-byte loads that go straight into the fragment registers: within a block of 32
 // k, lane t of a quad holds k = 8t .. 8t+7 for both operands, which is a permutation of k that
-// the sum does not see. The eight warps of a block share the same weight rows and take the
-// k-blocks in turn; their partial sums meet in shared memory.
+// the sum does not see. The 8 or 16 warps of a block share the same weight rows and take the
+// k-blocks in turn, several blocks of loads in flight each; their partial sums meet in shared
+// memory. Matrices with few rows and a long K get 16 warps: with few blocks per SM, the bytes in
+// flight per block decide the bandwidth.
 //
 // Row modes of a 16-row fragment:
 //   FULL  rows n0 .. n0+15 of w
@@ -14,8 +16,6 @@
 //         silu(gate) * up, so the SwiGLU product never round-trips through memory
 #include "common.cuh"
 
-#define GM_WARPS 8
-#define GM_THREADS (GM_WARPS * 32)
 #define GM_FULL 0
 #define GM_HALF 1
 #define GM_PAIR 2
@@ -39,11 +39,12 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <int NB, int RG, int MODE, typename TO>
-__global__ void __launch_bounds__(GM_THREADS)
+template <int NB, int RG, int MODE, int GM_WARPS, typename TO>
+__global__ void __launch_bounds__(GM_WARPS * 32)
 gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w, TO* __restrict__ out,
                 int M, int N, int K, int ldx, int ldw, int ldo, int pair_offset) {
     constexpr int ROWS_PER_GROUP = (MODE == GM_FULL) ? 16 : 8;
+    constexpr int GM_THREADS = GM_WARPS * 32;
     extern __shared__ float4 partial[];          // [GM_WARPS][RG * NB * 32]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
@@ -66,6 +67,24 @@ gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
             wrow[rg][1] = nullptr;
         }
     }
+    // The weights do not depend on the kernels before this one: ask L2 for this block's rows now,
+    // then wait for the predecessor (whose output is x).
+    {
+        const int row_bytes = K * 2;
+        const int lines = (row_bytes + 127) / 128;
+        constexpr int HALVES = (MODE == GM_HALF) ? 1 : 2;
+        for (int i = threadIdx.x; i < RG * HALVES * 8 * lines; i += GM_THREADS) {
+            const int line = i % lines, r = i / lines;                 // r: (rg, half, row of eight)
+            const int rg = r / (HALVES * 8), h = (r / 8) % HALVES, gg = r % 8;
+            int lower = n0 + rg * ROWS_PER_GROUP + gg;
+            if (lower > N - 1) lower = N - 1;
+            int row = lower;
+            if (h == 1) row = (MODE == GM_FULL) ? min(n0 + rg * 16 + 8 + gg, N - 1) : lower + pair_offset;
+            const char* p = reinterpret_cast<const char*>(w + (size_t)row * ldw) + (size_t)line * 128;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+        }
+    }
+    pdl_wait();
     const __nv_bfloat16* xrow[NB];
     bool xok[NB];
 #pragma unroll
@@ -84,8 +103,8 @@ gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
             for (int c = 0; c < 4; ++c) acc[rg][nb][c] = 0.f;
 
     const uint4 zero = make_uint4(0, 0, 0, 0);
-    constexpr int UNROLL = (RG * NB >= 8) ? 2 : 4;
-    // warp `warp` takes the k-blocks warp, warp + 8, ... ; UNROLL of them are in flight at a time
+    constexpr int UNROLL = (RG * NB >= 8) ? 2 : (RG * NB >= 2 ? 4 : 8);
+    // warp `warp` takes the k-blocks warp, warp + GM_WARPS, ... ; UNROLL of them are in flight at a time
     for (int kb0 = warp * 32; kb0 < K; kb0 += GM_WARPS * 32 * UNROLL) {
         uint4 wv[UNROLL][RG][2];
         uint4 xv[UNROLL][NB];
@@ -114,7 +133,8 @@ gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
                 }
     }
 
-    // ---- the eight warps add up
+    pdl_launch_dependents();     // what is left needs little of the SM: the next kernel may move in
+    // ---- the warps add up
     constexpr int PER_WARP = RG * NB * 32;
 #pragma unroll
     for (int rg = 0; rg < RG; ++rg)
@@ -155,19 +175,20 @@ gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
     }
 }
 
-template <int NB, int RG, int MODE, typename TO>
+template <int NB, int RG, int MODE, int GM_WARPS, typename TO>
 static int gemv_mma_launch(const void* x, const void* w, void* out, int M, int N, int K, int ldx, int ldw, int ldo,
                            int pair_offset, cudaStream_t stream) {
     constexpr int rows = ((MODE == GM_FULL) ? 16 : 8) * RG;
     const size_t smem = (size_t)GM_WARPS * RG * NB * 32 * sizeof(float4);
-    auto kernel = gemv_mma_kernel<NB, RG, MODE, TO>;
+    auto kernel = gemv_mma_kernel<NB, RG, MODE, GM_WARPS, TO>;
+    constexpr int GM_THREADS = GM_WARPS * 32;
     static bool configured = false;
     if (!configured && smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return (int)e;
     }
     configured = true;
-    kernel<<<(N + rows - 1) / rows, GM_THREADS, smem, stream>>>(
+    ttb_launch(kernel, dim3((N + rows - 1) / rows), dim3(GM_THREADS), smem, stream,
         (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (TO*)out, M, N, K, ldx, ldw, ldo, pair_offset);
     return ttb_launch_status();
 }
@@ -175,7 +196,14 @@ static int gemv_mma_launch(const void* x, const void* w, void* out, int M, int N
 template <int MODE, typename TO>
 static int gemv_mma_by_rows(const void* x, const void* w, void* out, int M, int N, int K, int ldx, int ldw, int ldo,
                             int pair_offset, cudaStream_t stream) {
-#define GM_GO(NB, RG) return gemv_mma_launch<NB, RG, MODE, TO>(x, w, out, M, N, K, ldx, ldw, ldo, pair_offset, stream)
+    // few blocks and a long K: sixteen warps per block keep enough loads in flight
+    constexpr int rows_small = (MODE == GM_FULL) ? 16 : 8;
+    const bool wide = K >= 4096 && (N + rows_small - 1) / rows_small < 4 * 148;
+#define GM_GO(NB, RG)                                                                                                      \
+    do {                                                                                                                   \
+        if (wide) return gemv_mma_launch<NB, RG, MODE, 16, TO>(x, w, out, M, N, K, ldx, ldw, ldo, pair_offset, stream);    \
+        return gemv_mma_launch<NB, RG, MODE, 8, TO>(x, w, out, M, N, K, ldx, ldw, ldo, pair_offset, stream);               \
+    } while (0)
     if (M <= 8) GM_GO(1, 1);
     if (M <= 16) GM_GO(2, 1);
     if (M <= 32) GM_GO(4, 1);

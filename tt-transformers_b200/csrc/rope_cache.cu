@@ -16,6 +16,8 @@ __global__ void rope_kv_write_kernel(T* __restrict__ qkv, const int* __restrict_
                                      const int* __restrict__ block_table, int table_width, int page_size,
                                      int num_pages, int write_kv, int* __restrict__ status) {
     extern __shared__ float trig[];  // cos[rotary_dim/2], sin[rotary_dim/2]
+    pdl_wait();
+    pdl_launch_dependents();
     const int t = blockIdx.x;
     const int pos = positions[t];
     const int half_rot = rotary_dim / 2;
@@ -97,12 +99,12 @@ TTB_EXPORT int ttb_rope_kv_write(void* qkv, int dtype, const int* positions, con
     const int threads = 256;
     const size_t smem = (size_t)(rotary_dim > 0 ? rotary_dim : 2) * sizeof(float);
     if (dtype == TTB_DTYPE_BF16)
-        rope_kv_write_kernel<<<tokens, threads, smem, stream>>>(
+        ttb_launch(rope_kv_write_kernel<__nv_bfloat16>, tokens, threads, smem, stream,
             (__nv_bfloat16*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
             (__nv_bfloat16*)key_pages, (__nv_bfloat16*)value_pages, block_table, table_width, page_size, num_pages,
             write_kv, status);
     else if (dtype == TTB_DTYPE_F32)
-        rope_kv_write_kernel<<<tokens, threads, smem, stream>>>(
+        ttb_launch(rope_kv_write_kernel<float>, tokens, threads, smem, stream,
             (float*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
             (float*)key_pages, (float*)value_pages, block_table, table_width, page_size, num_pages, write_kv, status);
     else

@@ -61,6 +61,8 @@ sample_kernel(const float* __restrict__ logits, int ld, int vocab, const float* 
     __shared__ float cand_value[SAMPLE_MAX_K];
     __shared__ int cand_index[SAMPLE_MAX_K];
     __shared__ int result;
+    pdl_wait();
+    pdl_launch_dependents();
     const int row = blockIdx.x;
     const float* l = logits + (size_t)row * ld;
     const int tid = threadIdx.x;
@@ -165,7 +167,7 @@ TTB_EXPORT int ttb_sample(const float* logits, int ld, int rows, int vocab, cons
     if (rows == 0) return TTB_OK;
     if (!logits || !out || vocab < 1) return TTB_ERR_ARGUMENT;
     if (temperature && (!seeds || !counters)) return TTB_ERR_ARGUMENT;
-    sample_kernel<<<rows, SAMPLE_THREADS, 0, stream>>>(logits, ld, vocab, temperature, top_k, top_p, seeds, counters, out);
+    ttb_launch(sample_kernel, rows, SAMPLE_THREADS, 0, stream, logits, ld, vocab, temperature, top_k, top_p, seeds, counters, out);
     return ttb_launch_status();
 }
 

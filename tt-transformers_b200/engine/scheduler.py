@@ -44,6 +44,19 @@ class Request:
         return self.prompt + self.output
 
     @property
+    def num_tokens(self) -> int:
+        return len(self.prompt) + len(self.output)
+
+    def tokens_between(self, start: int, stop: int) -> List[int]:
+        """Tokens start .. stop-1 of prompt + output, without building the whole list."""
+        n = len(self.prompt)
+        if start >= n:
+            return self.output[start - n:stop - n]
+        if stop <= n:
+            return self.prompt[start:stop]
+        return self.prompt[start:] + self.output[:stop - n]
+
+    @property
     def seed(self) -> int:
         return self.params.seed if self.params.seed is not None else 0x5EED + 7919 * self.arrival
 
@@ -61,7 +74,7 @@ class PlannedEntry:
 
     @property
     def tokens(self) -> List[int]:
-        return self.request.all_tokens[self.start:self.start + self.count]
+        return self.request.tokens_between(self.start, self.start + self.count)
 
 
 class Scheduler:
@@ -128,7 +141,7 @@ class Scheduler:
         for req in list(self.running):
             if req not in self.running or budget == 0:
                 continue
-            pending = len(req.all_tokens) - req.num_computed
+            pending = req.num_tokens - req.num_computed
             count = min(pending, self.max_chunk_tokens, budget)
             while True:
                 fit = self._fit(req, count)
@@ -147,13 +160,13 @@ class Scheduler:
             if count == 0:
                 continue
             self.cache.reserve(req.request_id, req.num_computed + count)
-            plan.append(PlannedEntry(req, req.num_computed, count, sample=req.num_computed + count == len(req.all_tokens)))
+            plan.append(PlannedEntry(req, req.num_computed, count, sample=req.num_computed + count == req.num_tokens))
             budget -= count
         # nobody is admitted in a step in which somebody had to give way
         while (self.waiting and budget > 0 and self.cache.free_slots > 0
                and self.preemptions == preempted_before):
             req = self.waiting[0]
-            pending = len(req.all_tokens)
+            pending = req.num_tokens
             count = min(pending, self.max_chunk_tokens, budget)
             fit = min(count, self.cache.room())
             if fit < 1:
@@ -183,7 +196,7 @@ class Scheduler:
             p = req.params
             if not p.ignore_eos and token in p.eos_token_ids:
                 self._finish(req, "stop")
-            elif len(req.output) >= p.max_new_tokens or len(req.all_tokens) >= self.max_seq_len:
+            elif len(req.output) >= p.max_new_tokens or req.num_tokens >= self.max_seq_len:
                 self._finish(req, "length")
             if req.finished:
                 done.append(req)

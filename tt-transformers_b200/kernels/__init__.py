@@ -69,7 +69,7 @@ class CudaKernels:
         for name in ("ttb_embedding", "ttb_add_rmsnorm", "ttb_swiglu", "ttb_gather_rows", "ttb_rope_kv_write",
                      "ttb_paged_attention_generic", "ttb_gemm_simt", "ttb_gemv", "ttb_sample",
                      "ttb_paged_attention_mma", "ttb_attention_mma_tile_rows", "ttb_attention_mma_supports",
-                     "ttb_gemv_mma"):
+                     "ttb_gemv_mma", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -218,13 +218,13 @@ class CudaKernels:
             self._p(qkv), qkv.stride(0), self._p(out), _dtype_code(qkv.dtype), self._p(batch.positions),
             self._p(batch.seg_of_token), self._p(view.keys), self._p(view.values), self._p(view.block_table),
             view.block_table.shape[1], view.page_size, tokens, heads, kv_heads, head_dim, ctypes.c_float(scale),
-            int(view.window or 0), self._stream()), "paged_attention")
+            int(view.window or 0), view.keys.shape[0], self._p(self.status), self._stream()), "paged_attention")
         return out
 
-    def _attention_plan(self, batch, rep: int, kv_heads: int):
+    def _attention_plan(self, batch, rep: int, kv_heads: int, head_dim: int):
         """How the step's segments are cut into query tiles, and into how many key splits:
         derived once per step and geometry, reused by every layer."""
-        key = ("attention_plan", rep, kv_heads)
+        key = ("attention_plan", rep, kv_heads, head_dim)
         plan = batch.extras.get(key)
         if plan is not None:
             return plan
@@ -242,27 +242,32 @@ class CudaKernels:
             n_tiles = len(seg_list)
             both = torch.tensor([seg_list, tok_list], dtype=torch.int32, pin_memory=True).to(self.device, non_blocking=True)
             seg, tok0 = both[0], both[1]
+        # Key splits: with fewer blocks than fit the GPU at once, as many splits as fill it in one
+        # wave (chunks of at least 256 keys); with more, a few waves of chunks of at least 2,048 keys.
         blocks = n_tiles * kv_heads
-        splits = 1
-        if blocks < 2 * self.sm_count:
-            splits = max(1, min(-(-4 * self.sm_count // blocks), batch.max_context // 256))
+        slots = self.sm_count * int(self.lib.ttb_attention_mma_blocks_per_sm(1 if decode_shape else 0, head_dim))
+        if blocks < slots:
+            splits = max(1, min(slots // blocks, batch.max_context // 256))
+        else:
+            splits = max(1, min(batch.max_context // 2048, -(-4 * slots // blocks)))
         plan = (decode_shape, seg, tok0, n_tiles, splits)
         batch.extras[key] = plan
         return plan
 
     def _attention_mma(self, qkv, out, batch, heads, kv_heads, head_dim, scale, view):
         tokens = qkv.shape[0]
-        decode_shape, seg, tok0, n_tiles, splits = self._attention_plan(batch, heads // kv_heads, kv_heads)
+        decode_shape, seg, tok0, n_tiles, splits = self._attention_plan(batch, heads // kv_heads, kv_heads, head_dim)
         partial_o = partial_ml = None
         if splits > 1:
             partial_o = torch.empty(tokens * heads * splits * head_dim, dtype=torch.float32, device=self.device)
             partial_ml = torch.empty(tokens * heads * splits * 2, dtype=torch.float32, device=self.device)
-        self._check(self.lib.ttb_paged_attention_mma(
+        self._check(self.lib.ttb_paged_attention_mma_checked(
             self._p(qkv), qkv.stride(0), self._p(out), self._p(batch.cu_seqlens), self._p(batch.seg_pos0),
             self._p(view.keys), self._p(view.values), self._p(view.block_table), view.block_table.shape[1],
             view.page_size, self._p(seg), self._p(tok0), n_tiles, tokens, heads, kv_heads, head_dim,
             ctypes.c_float(scale), int(view.window or 0), 1 if decode_shape else 0, splits,
-            self._p(partial_o), self._p(partial_ml), self._stream()), "paged_attention_mma")
+            self._p(partial_o), self._p(partial_ml), view.keys.shape[0], self._p(self.status), self._stream()),
+            "paged_attention_mma")
         if splits > 1:
             self.launches += 1
 
