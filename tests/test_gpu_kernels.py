@@ -276,3 +276,40 @@ def test_attention_does_not_follow_a_page_id_outside_the_pool(kernels, dtype, he
     with pytest.raises(EngineDeviceError, match="page id"):
         kernels.check_status()
     kernels.check_status()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (65, 128, 64), (130, 200, 72), (256, 384, 96), (300, 320, 1000),
+                                   (2048, 3072, 2048), (512, 2048, 8192), (100, 1000, 8)])
+def test_tcgen05_product(kernels, M, N, K):
+    """The TMA + tcgen05 matrix product against a float64 product, with tails in every dimension."""
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    ref = x.double() @ w.double().t()
+    before = kernels.use_tcgen05
+    kernels.use_tcgen05 = True
+    try:
+        got = kernels.linear(x, w)
+        got32 = kernels.linear(x, w, out_dtype=torch.float32)
+        kernels.check_status()            # raises if a wait inside the kernel gave up
+    finally:
+        kernels.use_tcgen05 = before
+    close(got, ref, torch.bfloat16)
+    assert got32.dtype == torch.float32
+    close(got32, ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,inter,K", [(128, 128, 64), (200, 320, 96), (70, 136, 72), (1024, 1024, 512)])
+def test_tcgen05_product_with_swiglu(kernels, twin, M, inter, K):
+    g = torch.Generator(device="cuda").manual_seed(8)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(2 * inter, K, device="cuda", generator=g) / math.sqrt(K) * 2).to(torch.bfloat16)
+    ref = twin.linear_swiglu(x.double(), w.double())
+    before = kernels.use_tcgen05
+    kernels.use_tcgen05 = True
+    try:
+        got = kernels.linear_swiglu(x, w)
+        kernels.check_status()
+    finally:
+        kernels.use_tcgen05 = before
+    close(got, ref, torch.bfloat16)

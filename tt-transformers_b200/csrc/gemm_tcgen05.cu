@@ -1,0 +1,326 @@
+// C[M, N] = A[M, K] * W[N, K]^T for prefill on the fifth-generation tensor cores (sm_100a):
+// operands move from global to shared memory by TMA (cp.async.bulk.tensor, 128-byte swizzle),
+// one elected thread issues tcgen05.mma on shared-memory descriptors, the float32 accumulator
+// lives in tensor memory (TMEM) and comes back to registers with tcgen05.ld for the epilogue.
+//
+// One block computes one 128 x 128 tile of C. Six warps:
+//   warp 0      producer: waits for a free stage, arms its mbarrier with the bytes to come, issues the TMA loads
+//   warp 1      allocates TMEM; one thread issues the MMAs of each stage (four k-steps of 16) and commits
+//               them to the stage's "empty" barrier; after the last stage it commits to the "accumulator full" barrier
+//   warps 2-5   epilogue: each reads its quarter of the TMEM lanes (a warp may only touch lanes
+//               32 * (warp % 4) ..), converts and stores rows of C
+// SWIGLU: W holds `up_offset` gate rows followed by as many up rows; the block loads both row
+// tiles, keeps two accumulators and writes silu(gate) * up, so the product's intermediate never
+// goes to memory.
+//
+// No load uses cluster multicast. Every wait on an mbarrier is bounded: after WAIT_LIMIT polls
+// the waiting role records an error code in *error_flag and stops; the block then frees its TMEM
+// and returns (by then every role has either finished or run out of patience, and no copy of its
+// own is in flight). Sizes: any M and N; K a multiple of 8 and row strides of 16 bytes (TMA).
+#include <cuda.h>
+
+#include "common.cuh"
+
+#define TC_BM 128
+#define TC_BN 128
+#define TC_BK 64
+#define TC_THREADS 192
+#define TC_WAIT_LIMIT (1u << 20)
+
+#define TC_ERR_PRODUCER 1
+#define TC_ERR_MMA 2
+#define TC_ERR_EPILOGUE 3
+
+__device__ __forceinline__ uint32_t tc_smem(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// Polls until the barrier's phase `parity` has completed; false after TC_WAIT_LIMIT polls.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < TC_WAIT_LIMIT; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.b32 %0, 1, 0, p;\n\t}"
+            : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_c, uint64_t desc_a, uint64_t desc_b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_c), "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate) : "memory");
+}
+// 32 consecutive columns of this thread's TMEM lane.
+__device__ __forceinline__ void tc_load32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory operand descriptor: K-major tile of rows x 64 bfloat16 as TMA lays it out with the
+// 128-byte swizzle; groups of eight rows are 1,024 bytes apart. `addr` is the shared address of
+// the first element of the k-step (the tile base plus 32 bytes per k-step of 16).
+__device__ __forceinline__ uint64_t tc_smem_desc(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr & 0x3FFFF) >> 4);          // start address, 16-byte units
+    d |= (uint64_t)0 << 16;                          // leading-dimension offset: not used by swizzled K-major tiles
+    d |= (uint64_t)(1024 >> 4) << 32;                // stride between groups of eight rows
+    d |= (uint64_t)1 << 46;                          // descriptor version of this architecture
+    d |= (uint64_t)2 << 61;                          // 128-byte swizzle
+    return d;
+}
+
+template <bool SWIGLU, int STAGES_> struct TcConfig {
+    static constexpr int STAGES = STAGES_;
+    static constexpr int A_BYTES = TC_BM * TC_BK * 2;
+    static constexpr int B_BYTES = TC_BN * TC_BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + (SWIGLU ? 2 : 1) * B_BYTES;
+    static constexpr int TMEM_COLS = SWIGLU ? 2 * TC_BN : TC_BN;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
+};
+
+template <bool SWIGLU, int STAGES_, typename TO>
+__global__ void __launch_bounds__(TC_THREADS)
+gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                    TO* __restrict__ out, int M, int N, int K, int ldc, int up_offset, int* __restrict__ error_flag) {
+    using Cfg = TcConfig<SWIGLU, STAGES_>;
+    extern __shared__ unsigned char tc_raw[];
+    // tiles need 1,024-byte alignment for the 128-byte swizzle
+    unsigned char* tiles = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + Cfg::STAGES * Cfg::STAGE_BYTES);
+    // bars[0 .. STAGES): full; bars[STAGES .. 2 STAGES): empty; bars[2 STAGES]: accumulator full
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * Cfg::STAGES + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * TC_BN;
+    const int k_blocks = (K + TC_BK - 1) / TC_BK;
+    const uint32_t full0 = tc_smem(bars), empty0 = tc_smem(bars + Cfg::STAGES), acc_full = tc_smem(bars + 2 * Cfg::STAGES);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        mbar_init(acc_full, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(tc_smem(tmem_slot)), "r"((uint32_t)Cfg::TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();                       // A is the output of the kernel before this one
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int kb = 0; kb < k_blocks; ++kb) {
+                const int s = kb % Cfg::STAGES;
+                const uint32_t round = kb / Cfg::STAGES;
+                if (round > 0 && !mbar_wait(empty0 + 8 * s, (round - 1) & 1)) {
+                    atomicExch(error_flag, TC_ERR_PRODUCER);
+                    break;
+                }
+                const uint32_t bar = full0 + 8 * s;
+                mbar_expect_tx(bar, Cfg::STAGE_BYTES);
+                unsigned char* stage = tiles + s * Cfg::STAGE_BYTES;
+                tma_load_2d(tc_smem(stage), &map_a, kb * TC_BK, m0, bar);
+                tma_load_2d(tc_smem(stage + Cfg::A_BYTES), &map_w, kb * TC_BK, n0, bar);
+                if (SWIGLU) tma_load_2d(tc_smem(stage + Cfg::A_BYTES + Cfg::B_BYTES), &map_w, kb * TC_BK, up_offset + n0, bar);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // instruction descriptor: float32 accumulator, bfloat16 operands, both K-major, M = 128, N = 128;
+            // with SWIGLU the gate and up tiles lie back to back in the stage and form one operand of
+            // 256 rows: one instruction with N = 256 fills both accumulators (columns 0-127 and 128-255)
+            constexpr uint32_t mma_n = SWIGLU ? 2 * TC_BN : TC_BN;
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((mma_n >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+            bool ok = true;
+            for (int kb = 0; kb < k_blocks && ok; ++kb) {
+                const int s = kb % Cfg::STAGES;
+                if (!mbar_wait(full0 + 8 * s, (kb / Cfg::STAGES) & 1)) {
+                    atomicExch(error_flag, TC_ERR_MMA);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_addr = tc_smem(tiles + s * Cfg::STAGE_BYTES);
+                const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+#pragma unroll
+                for (int k = 0; k < TC_BK / 16; ++k) {
+                    const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                    tc_mma(tmem_base, tc_smem_desc(a_addr + k * 32), tc_smem_desc(b_addr + k * 32), idesc, acc);
+                }
+                tc_commit(empty0 + 8 * s);         // the stage is free once these MMAs have read it
+            }
+            if (ok) tc_commit(acc_full);
+        }
+    } else {
+        // epilogue: TMEM lane quarter of this warp
+        pdl_launch_dependents();
+        const int quarter = warp & 3;
+        const int row = m0 + quarter * 32 + lane;
+        if (!mbar_wait(acc_full, 0)) {
+            if (lane == 0) atomicExch(error_flag, TC_ERR_EPILOGUE);
+        } else {
+            tc_fence_after();
+            const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+            const bool vec = (ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+#pragma unroll 1
+            for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+                uint32_t acc[32];
+                tc_load32(lane_addr + c0, acc);
+                float v[32];
+                if (SWIGLU) {
+                    uint32_t up[32];
+                    tc_load32(lane_addr + TC_BN + c0, up);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float g = __uint_as_float(acc[j]);
+                        v[j] = g / (1.f + __expf(-g)) * __uint_as_float(up[j]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]);
+                }
+                if (row < M) {
+                    TO* dst = out + (size_t)row * ldc + n0 + c0;
+                    if (vec && n0 + c0 + 32 <= N) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            float part[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) part[e] = v[j + e];
+                            store8(dst + j, part);
+                        }
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + c0 + j < N) dst[j] = from_float<TO>(v[j]);
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)Cfg::TMEM_COLS) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------- host side
+typedef CUresult (*TcEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                               const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                               CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static TcEncodeFn tc_encode_fn() {
+    static TcEncodeFn fn = nullptr;
+    static bool looked = false;
+    if (!looked) {
+        looked = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<TcEncodeFn>(p);
+    }
+    return fn;
+}
+
+// A row-major [rows, cols] bfloat16 matrix with row stride ld (elements), fetched in boxes of box_rows x 64.
+static bool tc_make_map(CUtensorMap* map, const void* base, int rows, int cols, int ld, int box_rows) {
+    TcEncodeFn encode = tc_encode_fn();
+    if (!encode) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {TC_BK, (cuuint32_t)box_rows};
+    cuuint32_t elem[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool SWIGLU, int STAGES_, typename TO>
+static int tc_launch_stages(const CUtensorMap& map_a, const CUtensorMap& map_w, void* C, int M, int N, int K, int ldc,
+                     int up_offset, int* error_flag, cudaStream_t stream) {
+    auto kernel = gemm_tcgen05_kernel<SWIGLU, STAGES_, TO>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TcConfig<SWIGLU, STAGES_>::SMEM_BYTES);
+        if (e != cudaSuccess) return (int)e;
+        configured = true;
+    }
+    dim3 grid((N + TC_BN - 1) / TC_BN, (M + TC_BM - 1) / TC_BM);
+    ttb_launch(kernel, grid, dim3(TC_THREADS), (size_t)TcConfig<SWIGLU, STAGES_>::SMEM_BYTES, stream, map_a, map_w, (TO*)C, M, N, K,
+               ldc, up_offset, error_flag);
+    return ttb_launch_status();
+}
+
+static int tc_stage_choice() {          // TTB200_TC_STAGES=few|many, for experiments; default: few (two blocks per SM)
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("TTB200_TC_STAGES");
+        v = (e && e[0] == 'm') ? 1 : 0;
+    }
+    return v;
+}
+
+template <bool SWIGLU, typename TO>
+static int tc_launch(const CUtensorMap& map_a, const CUtensorMap& map_w, void* C, int M, int N, int K, int ldc,
+                     int up_offset, int* error_flag, cudaStream_t stream) {
+    if (tc_stage_choice())
+        return tc_launch_stages<SWIGLU, SWIGLU ? 4 : 6, TO>(map_a, map_w, C, M, N, K, ldc, up_offset, error_flag, stream);
+    return tc_launch_stages<SWIGLU, SWIGLU ? 2 : 3, TO>(map_a, map_w, C, M, N, K, ldc, up_offset, error_flag, stream);
+}
+
+// A [M, K], W [N, K] (or [2 * swiglu_rows, K] with swiglu_rows = N gate rows then N up rows), bfloat16, K-contiguous.
+// C [M, N] bfloat16 or float32. error_flag: device int that a timed-out wait sets (0 = fine).
+TTB_EXPORT int ttb_gemm_tcgen05(const void* A, const void* W, void* C, int out_dtype, int M, int N, int K, int lda,
+                                int ldw, int ldc, int swiglu_rows, int* error_flag, cudaStream_t stream) {
+    if (M == 0 || N == 0) return TTB_OK;
+    if (!A || !W || !C || !error_flag) return TTB_ERR_ARGUMENT;
+    if (K < 8 || (K & 7) || (lda & 7) || (ldw & 7) || !aligned16(A) || !aligned16(W)) return TTB_ERR_UNSUPPORTED;
+    if ((M + TC_BM - 1) / TC_BM > 65535) return TTB_ERR_UNSUPPORTED;
+    if (swiglu_rows != 0 && swiglu_rows != N) return TTB_ERR_ARGUMENT;
+    CUtensorMap map_a, map_w;
+    if (!tc_make_map(&map_a, A, M, K, lda, TC_BM)) return TTB_ERR_UNSUPPORTED;
+    if (!tc_make_map(&map_w, W, swiglu_rows ? 2 * N : N, K, ldw, TC_BN)) return TTB_ERR_UNSUPPORTED;
+    const bool f32 = out_dtype == TTB_DTYPE_F32;
+    if (!f32 && out_dtype != TTB_DTYPE_BF16) return TTB_ERR_UNSUPPORTED;
+    if (swiglu_rows)
+        return f32 ? tc_launch<true, float>(map_a, map_w, C, M, N, K, ldc, swiglu_rows, error_flag, stream)
+                   : tc_launch<true, __nv_bfloat16>(map_a, map_w, C, M, N, K, ldc, swiglu_rows, error_flag, stream);
+    return f32 ? tc_launch<false, float>(map_a, map_w, C, M, N, K, ldc, 0, error_flag, stream)
+               : tc_launch<false, __nv_bfloat16>(map_a, map_w, C, M, N, K, ldc, 0, error_flag, stream);
+}

@@ -69,7 +69,8 @@ class CudaKernels:
         for name in ("ttb_embedding", "ttb_add_rmsnorm", "ttb_swiglu", "ttb_gather_rows", "ttb_rope_kv_write",
                      "ttb_paged_attention_generic", "ttb_gemm_simt", "ttb_gemv", "ttb_sample",
                      "ttb_paged_attention_mma", "ttb_attention_mma_tile_rows", "ttb_attention_mma_supports",
-                     "ttb_gemv_mma", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm"):
+                     "ttb_gemv_mma", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm",
+                     "ttb_gemm_tcgen05"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -80,6 +81,14 @@ class CudaKernels:
         self.launches = 0     # how many of our kernels were launched (counted for reports)
         self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.use_mma_attention = True
+        # bfloat16 products with more rows than the skinny kernel takes go to the library's product, or,
+        # with this switch (or TTB200_TCGEN05=1 in the environment), to the TMA + tcgen05 kernel of
+        # gemm_tcgen05.cu, which is correct at every size but, with its one-tile-per-block schedule,
+        # reaches 0.6 to 0.8 of the library's throughput at prefill sizes.
+        import os
+        self.use_tcgen05 = os.environ.get("TTB200_TCGEN05", "0") == "1"
+        with torch.cuda.device(self.device):
+            self.tc_error = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
@@ -98,6 +107,11 @@ class CudaKernels:
     def check_status(self):
         """Raise if a kernel flagged an index outside its tables since the last check.
         Synchronises with the device."""
+        tc = int(self.tc_error.item())
+        if tc != 0:
+            self.tc_error.zero_()
+            role = {1: "the TMA producer", 2: "the MMA issuer", 3: "the epilogue"}.get(tc, f"role {tc}")
+            raise EngineDeviceError(f"the tcgen05 matrix product gave up waiting on a barrier ({role}); its result is invalid")
         value = int(self.status.item())
         if value != 0:
             self.status.zero_()
@@ -166,6 +180,13 @@ class CudaKernels:
                                           _dtype_code(out_dtype), M, N, K, x.stride(0), w.stride(0), N,
                                           self._stream()), "gemv")
             return out
+        if (x.dtype == torch.bfloat16 and self.use_tcgen05 and K % 8 == 0 and x.stride(0) % 8 == 0
+                and w.stride(0) % 8 == 0):
+            out = torch.empty(M, N, dtype=out_dtype, device=self.device)
+            self._check(self.lib.ttb_gemm_tcgen05(self._p(x), self._p(w), self._p(out), _dtype_code(out_dtype), M, N, K,
+                                                  x.stride(0), w.stride(0), N, 0, self._p(self.tc_error),
+                                                  self._stream()), "gemm_tcgen05")
+            return out
         if x.dtype == torch.bfloat16:
             # library product (cuBLAS), float32 accumulation
             if out_dtype == torch.bfloat16:
@@ -187,6 +208,13 @@ class CudaKernels:
             self._check(self.lib.ttb_gemv_mma(self._p(x), self._p(w_gate_up), self._p(out), _dtype_code(x.dtype), M,
                                               inter, K, x.stride(0), w_gate_up.stride(0), inter, inter,
                                               self._stream()), "gemv_mma_swiglu")
+            return out
+        if (x.dtype == torch.bfloat16 and self.use_tcgen05 and K % 8 == 0 and x.stride(0) % 8 == 0
+                and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1 and w_gate_up.stride(1) == 1):
+            out = torch.empty(M, inter, dtype=x.dtype, device=self.device)
+            self._check(self.lib.ttb_gemm_tcgen05(self._p(x), self._p(w_gate_up), self._p(out), _dtype_code(x.dtype), M,
+                                                  inter, K, x.stride(0), w_gate_up.stride(0), inter, inter,
+                                                  self._p(self.tc_error), self._stream()), "gemm_tcgen05_swiglu")
             return out
         return self.swiglu(self.linear(x, w_gate_up))
 
