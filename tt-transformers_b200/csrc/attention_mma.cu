@@ -41,6 +41,13 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// 2^x by the special-function unit (two units in the last place are plenty for probabilities
+// that are rounded to bfloat16 next); 2^-inf = 0.
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -101,6 +108,8 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
     // the two rows of the score fragment that this thread holds
     const int r0 = warp_m * 16 + (lane >> 2), r1 = r0 + 8;
     const int qpos0 = q_first + r0 / rep, qpos1 = q_first + r1 / rep;
+    const int warp_qpos_min = q_first + (warp_m * 16) / rep;          // over the 16 rows of this warp
+    const int warp_qpos_max = q_first + (warp_m * 16 + 15) / rep;
 
     float o_acc[OB][4];
 #pragma unroll
@@ -199,47 +208,58 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
                     mma_bf16(s[nb + 1], q_frag[ks], b[2], b[3]);
                 }
             }
-            // ---- mask, running maximum and sum
+            // ---- mask (only in tiles that the causal edge, a window or the end of the range cuts),
+            //      running maximum and sum. Scores stay unscaled; the scale goes into the exponent's
+            //      multiply-add: p = 2^(s * scale_log2 - max * scale_log2).
+            const int last_key = key_base + WARP_KEYS - 1;
+            const bool cut = last_key > warp_qpos_min || last_key >= k_end ||
+                             (window > 0 && key_base <= warp_qpos_max - window);
             float tile_max[2] = {-INFINITY, -INFINITY};
+            if (cut) {
 #pragma unroll
-            for (int nb = 0; nb < NB; ++nb) {
+                for (int nb = 0; nb < NB; ++nb) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int key = key_base + nb * 8 + ((lane & 3) << 1) + (j & 1);
-                    const int qpos = (j < 2) ? qpos0 : qpos1;
-                    const bool visible = key < k_end && key <= qpos && (window <= 0 || key > qpos - window);
-                    const float v = visible ? s[nb][j] * scale_log2 : -INFINITY;
-                    s[nb][j] = v;
-                    tile_max[j >> 1] = fmaxf(tile_max[j >> 1], v);
+                    for (int j = 0; j < 4; ++j) {
+                        const int key = key_base + nb * 8 + ((lane & 3) << 1) + (j & 1);
+                        const int qpos = (j < 2) ? qpos0 : qpos1;
+                        const bool visible = key < k_end && key <= qpos && (window <= 0 || key > qpos - window);
+                        if (!visible) s[nb][j] = -INFINITY;
+                    }
                 }
             }
-            float alpha[2];
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) {
+                tile_max[0] = fmaxf(tile_max[0], fmaxf(s[nb][0], s[nb][1]));
+                tile_max[1] = fmaxf(tile_max[1], fmaxf(s[nb][2], s[nb][3]));
+            }
+            float alpha[2], neg_max_scaled[2];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 tile_max[h] = fmaxf(tile_max[h], __shfl_xor_sync(0xffffffffu, tile_max[h], 1));
                 tile_max[h] = fmaxf(tile_max[h], __shfl_xor_sync(0xffffffffu, tile_max[h], 2));
-                const float new_max = fmaxf(row_max[h], tile_max[h]);
-                alpha[h] = (row_max[h] == -INFINITY) ? 0.f : exp2f(row_max[h] - new_max);
+                const float new_max = fmaxf(row_max[h], tile_max[h]);        // unscaled
+                alpha[h] = (row_max[h] == -INFINITY) ? 0.f : fast_exp2((row_max[h] - new_max) * scale_log2);
                 row_max[h] = new_max;
                 row_sum[h] *= alpha[h];
+                neg_max_scaled[h] = (new_max == -INFINITY) ? 0.f : -new_max * scale_log2;
             }
-            const float m0 = (row_max[0] == -INFINITY) ? 0.f : row_max[0];
-            const float m1 = (row_max[1] == -INFINITY) ? 0.f : row_max[1];
 #pragma unroll
             for (int nb = 0; nb < NB; ++nb) {
-                s[nb][0] = exp2f(s[nb][0] - m0);
-                s[nb][1] = exp2f(s[nb][1] - m0);
-                s[nb][2] = exp2f(s[nb][2] - m1);
-                s[nb][3] = exp2f(s[nb][3] - m1);
+                s[nb][0] = fast_exp2(fmaf(s[nb][0], scale_log2, neg_max_scaled[0]));
+                s[nb][1] = fast_exp2(fmaf(s[nb][1], scale_log2, neg_max_scaled[0]));
+                s[nb][2] = fast_exp2(fmaf(s[nb][2], scale_log2, neg_max_scaled[1]));
+                s[nb][3] = fast_exp2(fmaf(s[nb][3], scale_log2, neg_max_scaled[1]));
                 row_sum[0] += s[nb][0] + s[nb][1];
                 row_sum[1] += s[nb][2] + s[nb][3];
             }
+            if (alpha[0] != 1.f || alpha[1] != 1.f) {       // the maximum moved: rescale what was gathered
 #pragma unroll
-            for (int ob = 0; ob < OB; ++ob) {
-                o_acc[ob][0] *= alpha[0];
-                o_acc[ob][1] *= alpha[0];
-                o_acc[ob][2] *= alpha[1];
-                o_acc[ob][3] *= alpha[1];
+                for (int ob = 0; ob < OB; ++ob) {
+                    o_acc[ob][0] *= alpha[0];
+                    o_acc[ob][1] *= alpha[0];
+                    o_acc[ob][2] *= alpha[1];
+                    o_acc[ob][3] *= alpha[1];
+                }
             }
             // ---- output: O += P V
 #pragma unroll
@@ -264,6 +284,10 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
     }
 
     pdl_launch_dependents();     // the streaming part is over: the next kernel may move in
+    // from here on the running maxima are in the exponent's units (scaled, base 2)
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+        if (row_max[h] != -INFINITY) row_max[h] *= scale_log2;
     // ---- row sums over the four lanes of a quad
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
