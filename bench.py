@@ -247,7 +247,10 @@ def main(argv=None) -> int:
 
     # ------------------------------------------------------------------ end to end through the Python entry point
     params = SamplingParams(temperature=0.0, max_new_tokens=1 << 30, ignore_eos=True)
-    length = args.context - args.steps - warmup - 2
+    # Requests whose prompts are done decode while the others' prompts are still being computed, one
+    # token for every later prompt portion: leave room for that, so that nobody reaches the context
+    # limit (and leaves the batch) inside the timed region.
+    length = args.context - args.steps - warmup - 2 - args.batch * (args.context // PREFILL_TOKENS + 1)
     if args.skip_e2e:
         e2e = None
     elif args.fill == "synthetic":

@@ -15,13 +15,16 @@ def manager(requests, page_size=4, num_pages=10, max_slots=3, max_seq_len=64, st
                         allocate_storage=storage)
 
 
-def test_pool_hands_out_each_page_once_and_reuses_the_last_freed_first():
+def test_pool_hands_out_each_page_once_and_reuses_freed_pages_lowest_first():
     pool = PagePool(5)
     a = pool.allocate(3)
     assert a == [1, 2, 3] and pool.free_count == 2
     assert pool.allocate(3) is None and pool.free_count == 2         # nothing taken
     pool.free([2])
     assert pool.allocate(1) == [2]
+    pool.free([3, 1])
+    assert pool.allocate(2) == [1, 3] and pool.free_count == 2
+    pool.free([3])
     with pytest.raises(PagePoolError):
         pool.free([4])                                               # never handed out
     pool.free([1])
