@@ -220,17 +220,12 @@ def main(argv=None) -> int:
 
     def decode_run(batch, steps, warm):
         ids = fill(batch, args.context - steps - warm - 1)
-        state = {"tokens": [1] * batch}
-
-        def one():
-            logits = engine.step([StepEntry(rid, [t], [0]) for rid, t in zip(ids, state["tokens"])])
-            state["tokens"] = kernels.sample(logits).tolist()
-
-        for _ in range(warm):
-            one()
+        # the engine's decode loop: every step takes its tokens from the sampler's output of the step
+        # before, on the device; the sampled ids reach the host behind the steps
+        tokens = engine.decode_steps(ids, [1] * batch, warm)[-1]
         before = kernels.launches
         with ClockSampler() as clocks:
-            ms = timed(one, steps)
+            ms = timed(lambda: engine.decode_steps(ids, tokens, steps), 1) / steps
         launches = kernels.launches - before
         for rid in ids:
             engine.finish(rid)

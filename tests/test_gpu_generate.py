@@ -51,6 +51,50 @@ def test_temperature_sampling_is_reproducible_and_independent_of_the_batch(tiny_
     assert torch.equal(out, again) and out.shape == (1, 10)
 
 
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_decoding_ahead_of_the_host_gives_the_same_tokens(tiny_folders, dtype):
+    """The step that is launched while the host still waits for the one before (tokens fed back on
+    the device) must produce what the plain one-step-at-a-time loop produces; so must the engine's
+    decode loop, and a step ahead that is taken back (a request ends early) must leave no trace."""
+    from tt_transformers_b200 import SamplingParams, from_pretrained
+    from tt_transformers_b200.engine.step import StepEntry
+
+    llm = from_pretrained(tiny_folders["D"], dtype=dtype, page_size=16, max_batch_size=4, max_seq_len=256)
+    prompts = [helpers.random_tokens(512, n, 70 + n) for n in (9, 30, 17)]
+    params = [SamplingParams(temperature=0.7 if i else 0.0, seed=5 + i, max_new_tokens=n) for i, n in enumerate((40, 25, 33))]
+    llm.look_ahead = False
+    plain = [r.output for r in llm.generate_requests(prompts, params)]
+    llm.look_ahead = True
+    ahead = [r.output for r in llm.generate_requests(prompts, params)]
+    assert ahead == plain and [len(o) for o in ahead] == [40, 25, 33]
+    stop = plain[0][7]                                       # ends the first request early: a step ahead is taken back
+    early = [SamplingParams(temperature=0.0, max_new_tokens=40, eos_token_ids=(stop,)), params[1], params[2]]
+    llm.look_ahead = False
+    plain_early = [r.output for r in llm.generate_requests(prompts, early)]
+    llm.look_ahead = True
+    assert [r.output for r in llm.generate_requests(prompts, early)] == plain_early
+    assert plain_early[0] == plain[0][:plain[0].index(stop) + 1] and plain_early[1:] == plain[1:]
+    llm.engine.cache.audit()
+    assert llm.engine.cache.free_pages() == llm.engine.cache.num_pages
+
+    engine = llm.engine
+    one_by_one, fed_back = [], None
+    for mode in ("host", "device"):
+        for i, p in enumerate(prompts):
+            engine.step([StepEntry(i, p, [])])
+        first = [3, 4, 5]
+        if mode == "host":
+            cur = first
+            for _ in range(20):
+                cur = engine.kernels.sample(engine.step([StepEntry(i, [t], [0]) for i, t in enumerate(cur)])).tolist()
+                one_by_one.append(cur)
+        else:
+            fed_back = engine.decode_steps([0, 1, 2], first, 20)
+        for i in range(3):
+            engine.finish(i)
+    assert fed_back == one_by_one
+
+
 @pytest.mark.parametrize("dtype,tol", [("float32", 1e-4), ("bfloat16", 4e-2)])
 def test_long_decoding(tiny_folders, dtype, tol):
     """A short prompt, then hundreds of tokens one by one (captured steps), across many pages."""

@@ -217,6 +217,21 @@ class CacheManager:
                     row[i] = 0
                 g.table[live.slot, :dead] = 0
 
+    def has_windows(self) -> bool:
+        return any(g.pool is not None and g.request.window is not None for g in self.groups)
+
+    def rollback(self, request_id, length: int) -> None:
+        """Take back a step that was committed ahead of time and then not used: the request holds
+        `length` tokens again, pages beyond are given back. Not possible once a window has freed
+        pages on the way (has_windows())."""
+        live = self._live[request_id]
+        if length > live.length:
+            raise ValueError("rollback goes backwards only")
+        if self.has_windows():
+            raise RuntimeError("a cache with windowed groups cannot roll back")
+        live.length = length
+        self.trim(request_id)
+
     def release(self, request_id) -> None:
         """The request ended: its pages and its slot are given back."""
         live = self._live.pop(request_id)

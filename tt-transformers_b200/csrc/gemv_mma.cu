@@ -69,6 +69,7 @@ gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
     }
     // The weights do not depend on the kernels before this one: ask L2 for this block's rows now,
     // then wait for the predecessor (whose output is x).
+    pdl_launch_dependents();
     {
         const int row_bytes = K * 2;
         const int lines = (row_bytes + 127) / 128;
@@ -133,7 +134,6 @@ gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
                 }
     }
 
-    pdl_launch_dependents();     // what is left needs little of the SM: the next kernel may move in
     // ---- the warps add up
     constexpr int PER_WARP = RG * NB * 32;
 #pragma unroll

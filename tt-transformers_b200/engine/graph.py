@@ -60,7 +60,10 @@ class DecodeGraphs:
         kernels_in_graph = eng.kernels.launches - before
         return graph, static, layout, logits, kernels_in_graph
 
-    def run(self, entries: List) -> torch.Tensor:
+    def run(self, entries: List, token_feedback: torch.Tensor = None) -> torch.Tensor:
+        """Replay the captured step for these entries. With token_feedback (int32 on the device, one
+        token per entry, typically what the sampler wrote for the step before) the token ids come
+        from there instead of from the entries, so the host need not have seen them yet."""
         eng = self.engine
         rows = len(entries)
         size = self._bucket(rows)
@@ -71,6 +74,8 @@ class DecodeGraphs:
         assert new_layout["total"] == layout["total"]
         static.copy_(host, non_blocking=True)
         eng._record_staging()
+        if token_feedback is not None:
+            static[layout["o_tok"]:layout["o_tok"] + rows].copy_(token_feedback[:rows])
         graph.replay()
         eng.kernels.launches += kernels_in_graph
         self.replays += 1

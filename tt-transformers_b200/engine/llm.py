@@ -22,6 +22,20 @@ from ..sampling.sampler import Sampler
 from .scheduler import Request, Scheduler
 from .step import Engine, StepEntry, build_engine
 
+class _Flight:
+    """A step that has been launched: which requests its rows belong to, where the sampled ids
+    will arrive on the host, and what every request held before it (to take it back)."""
+
+    def __init__(self, ids, tokens_dev, tokens_host, event, lengths_before):
+        self.ids, self.tokens_dev, self.tokens_host = ids, tokens_dev, tokens_host
+        self.event, self.lengths_before = event, lengths_before
+
+    def result(self) -> List[int]:
+        if self.event is not None:
+            self.event.synchronize()
+        return self.tokens_host.tolist()
+
+
 _UNSET = object()
 # what the reference falls back to when neither the call nor the checkpoint says otherwise
 # (src/tt_transformers/models/hf_generation.py:26,277)
@@ -38,6 +52,8 @@ class LLM:
         self.pad_token_id = pad_token_id
         self.tokenizer = tokenizer
         self._busy = False
+        self._ahead: Optional[_Flight] = None
+        self.look_ahead = True            # launch the next decode step while the host waits for this one's ids
         self._scheduler: Optional[Scheduler] = None
         self._next_id = 0
         self.steps = 0
@@ -123,22 +139,80 @@ class LLM:
     def step(self) -> List[Request]:
         """One step of the engine over what the scheduler picks: token ids go to the device,
         sampled token ids come back and are appended to their requests. Returns the requests
-        that finished with this step."""
+        that finished with this step.
+
+        While the host waits for a decode step's ids, the next decode step is already running:
+        it is launched right behind, with its tokens fed from the sampler's output on the device
+        (the reference's traced decode does the same, src/tt_transformers/llm_runtime/decode.py:1137-1140).
+        If the next call finds that the scheduler wants exactly that step, its result is simply
+        picked up; if not (somebody finished or joined), it is taken back."""
         sched = self._scheduler
         if sched is None or not sched.has_work():
             return []
         plan = sched.schedule()
+        ahead, self._ahead = self._ahead, None
         if not plan:
+            if ahead is not None:
+                self._take_back(ahead)
             if sched.has_work() and not sched.running:
                 raise RuntimeError("the scheduler can make no progress: a waiting request fits no page")
             return []
-        entries = [StepEntry(e.request.request_id, e.tokens, [e.count - 1] if e.sample else []) for e in plan]
-        logits = self.engine.step(entries)
-        wanted = [e.request for e in plan if e.sample]
-        tokens = self.sampler.sample(logits, [r.params for r in wanted], [r.seed for r in wanted],
-                                     [len(r.output) for r in wanted])
+        ids = tuple(e.request.request_id for e in plan)
+        all_decode = all(e.sample and e.count == 1 for e in plan)
+        if ahead is not None and all_decode and ahead.ids == ids:
+            flight = ahead                                   # this very step is running already
+        else:
+            if ahead is not None:
+                self._take_back(ahead)
+            flight = self._launch(plan, [StepEntry(e.request.request_id, e.tokens, [e.count - 1] if e.sample else [])
+                                         for e in plan], None, 0)
+        if self._may_look_ahead(plan):
+            entries = [StepEntry(e.request.request_id, [0], [0]) for e in plan]     # ids come from the device
+            self._ahead = self._launch(plan, entries, flight.tokens_dev, 1)
+        tokens = flight.result()
         self.steps += 1
-        return sched.update(plan, tokens)
+        done = sched.update(plan, tokens)
+        if done and self._ahead is not None:                 # the batch changed: the step ahead is not the next one
+            self._take_back(self._ahead)
+            self._ahead = None
+        return done
+
+    def _launch(self, plan, entries, feedback, ahead_by: int) -> _Flight:
+        cache = self.engine.cache
+        lengths = {e.request_id: (cache.length(e.request_id) if cache.is_live(e.request_id) else 0) for e in entries}
+        logits = self.engine.step(entries, token_feedback=feedback)
+        wanted = [e.request for e in plan if e.sample]
+        if not wanted:
+            return _Flight(tuple(e.request_id for e in entries), None, torch.empty(0, dtype=torch.int32), None, lengths)
+        tokens_dev = self.sampler.sample_device(logits, [r.params for r in wanted], [r.seed for r in wanted],
+                                                [len(r.output) + ahead_by for r in wanted])
+        if self.engine.runtime.device.type != "cuda":
+            return _Flight(tuple(e.request_id for e in entries), tokens_dev, tokens_dev.cpu(), None, lengths)
+        host = torch.empty(len(wanted), dtype=torch.int32, pin_memory=True)
+        host.copy_(tokens_dev, non_blocking=True)
+        event = torch.cuda.Event()
+        event.record()
+        return _Flight(tuple(e.request_id for e in entries), tokens_dev, host, event, lengths)
+
+    def _may_look_ahead(self, plan) -> bool:
+        """After this step every request of the plan decodes, nobody can join, nobody ends by
+        length, and pages are plentiful: the next step is known but for its token ids."""
+        engine, sched = self.engine, self._scheduler
+        if not (self.look_ahead and engine.can_feed_back()) or engine.cache.has_windows() or sched.waiting:
+            return False
+        if len(plan) != len(sched.running) or not all(e.sample for e in plan):
+            return False
+        for e in plan:
+            r = e.request
+            if len(r.output) + 1 >= r.params.max_new_tokens or r.num_tokens + 2 >= engine.max_seq_len:
+                return False
+        return engine.cache.free_pages() >= 2 * len(plan)
+
+    def _take_back(self, flight: _Flight) -> None:
+        cache = self.engine.cache
+        for rid in flight.ids:
+            if cache.is_live(rid):
+                cache.rollback(rid, flight.lengths_before[rid])
 
     def generate_requests(self, prompts: List[List[int]], params: List[SamplingParams]) -> List[Request]:
         """Run until every prompt is finished; the requests in input order."""
@@ -159,6 +233,9 @@ class LLM:
             self.last_stats = {"steps": self.steps - first, "preemptions": self._scheduler.preemptions if self._scheduler else 0}
             return requests
         finally:
+            if self._ahead is not None:
+                self._take_back(self._ahead)
+                self._ahead = None
             if self._scheduler is not None and self._scheduler.has_work():   # a failure must not leave pages taken
                 for rid in self.engine.cache.live_requests():
                     self.engine.cache.release(rid)

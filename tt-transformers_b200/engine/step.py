@@ -180,9 +180,12 @@ class Engine:
         return self._batch_from(self._to_device(host), layout, lists)
 
     # ------------------------------------------------------------------ the step
-    def step(self, entries: List[StepEntry]) -> torch.Tensor:
+    def step(self, entries: List[StepEntry], token_feedback: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Run the entries' tokens as one batch. Returns float32 logits [wanted, vocab] on
-        the device. Raises OutOfPages (nothing was taken or run) if the pages do not suffice."""
+        the device. Raises OutOfPages (nothing was taken or run) if the pages do not suffice.
+        token_feedback: for a step in which every request brings one token, an int32 device tensor
+        with those tokens (what the sampler produced for the step before); the ids in the entries
+        are then placeholders and the host need not wait for the sampler."""
         if not entries:
             return torch.empty(0, self.vocab_size, dtype=torch.float32, device=self.runtime.device)
         seen = set()
@@ -215,8 +218,12 @@ class Engine:
                 elif self.cache.is_live(e.request_id):
                     self.cache.trim(e.request_id)
             raise
+        if token_feedback is not None and not (self.graphs is not None and total == len(entries)):
+            for e in entries:
+                self.cache.trim(e.request_id)
+            raise ValueError("token_feedback needs a captured decode step: one token per request, cuda_graph on")
         if self.graphs is not None and total == len(entries):
-            logits = self.graphs.run(entries)              # one token per request: replay a captured step
+            logits = self.graphs.run(entries, token_feedback)   # one token per request: replay a captured step
         else:
             batch = self.build_batch(entries)
             logits = self.model.forward(batch, self.cache)
@@ -224,6 +231,36 @@ class Engine:
             self.cache.commit(e.request_id, self.cache.length(e.request_id) + len(e.tokens))
         self.steps_run += 1
         return logits
+
+    def can_feed_back(self) -> bool:
+        """Whether decode steps can take their tokens from the device (captured steps are on)."""
+        return self.graphs is not None
+
+    def decode_steps(self, request_ids: List, tokens: List[int], steps: int) -> List[List[int]]:
+        """`steps` greedy decode steps for live requests without the host in between: every step
+        takes its tokens from the sampler's output of the step before, on the device, and the
+        sampled ids travel to pinned host memory behind the steps. Returns tokens[step][request].
+        The reference's traced decode feeds tokens and positions back on the device in the same
+        way (src/tt_transformers/llm_runtime/decode.py:1137-1140)."""
+        rows = len(request_ids)
+        if steps <= 0 or rows == 0:
+            return []
+        if not self.can_feed_back():
+            out, cur = [], list(tokens)
+            for _ in range(steps):
+                logits = self.step([StepEntry(r, [t], [0]) for r, t in zip(request_ids, cur)])
+                cur = self.kernels.sample(logits).tolist()
+                out.append(cur)
+            return out
+        host = torch.empty(steps, rows, dtype=torch.int32, pin_memory=True)
+        feedback, cur = None, list(tokens)
+        for s in range(steps):
+            logits = self.step([StepEntry(r, [t], [0]) for r, t in zip(request_ids, cur)], token_feedback=feedback)
+            feedback = self.kernels.sample(logits)
+            host[s].copy_(feedback, non_blocking=True)
+            cur = [0] * rows                      # placeholders: the device feeds the real ids
+        torch.cuda.current_stream(self.runtime.device).synchronize()
+        return host.tolist()
 
     def close(self) -> None:
         for rid in self.cache.live_requests():

@@ -28,11 +28,15 @@ class Sampler:
     def sample(self, logits: torch.Tensor, params: Sequence[SamplingParams], seeds: Sequence[int],
                counters: Sequence[int]) -> List[int]:
         """logits float32 [rows, vocab]; one token id per row, on the host."""
-        rows = logits.shape[0]
-        if rows == 0:
+        if logits.shape[0] == 0:
             return []
+        return self.sample_device(logits, params, seeds, counters).tolist()
+
+    def sample_device(self, logits: torch.Tensor, params: Sequence[SamplingParams], seeds: Sequence[int],
+                      counters: Sequence[int]) -> torch.Tensor:
+        """The same, but the ids stay on the device (int32 [rows]): nothing waits for the GPU."""
         if all(p.greedy for p in params):
-            return self.kernels.sample(logits).tolist()
+            return self.kernels.sample(logits)
         pinned = self.device.type == "cuda"
         f = torch.tensor([[p.temperature for p in params], [p.top_p for p in params]], dtype=torch.float32,
                          pin_memory=pinned).to(self.device, non_blocking=True)
@@ -40,4 +44,4 @@ class Sampler:
                          pin_memory=pinned).to(self.device, non_blocking=True)
         s = torch.tensor([int(x) & 0x7FFFFFFFFFFFFFFF for x in seeds], dtype=torch.int64,
                          pin_memory=pinned).to(self.device, non_blocking=True)
-        return self.kernels.sample(logits, f[0], i[0], f[1], s, i[1]).tolist()
+        return self.kernels.sample(logits, f[0], i[0], f[1], s, i[1])
