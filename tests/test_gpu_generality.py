@@ -212,3 +212,115 @@ def test_windowed_pages_come_back_while_the_request_lives(tmp_path):
     got = helpers.run_steps(engine, steps)
     assert helpers.relative_error(got["a"], ref) < 1e-4
     assert engine.cache.free_pages() == 12
+
+
+# ---------------------------------------------------------------------------- a routed feed-forward and a learned position encoding
+class ToyRoutedFF:
+    """Top-1 routing over small SwiGLU experts: router logits and their softmax in float32, the chosen
+    expert's output scaled by its probability. Plain torch operations, defined in the test."""
+
+    def __init__(self, width, inter, experts, prefix):
+        self.width, self.inter, self.experts, self.prefix = width, inter, experts, prefix
+
+    def tensor_specs(self):
+        p = self.prefix
+        return ([TensorSpec(p + "router", (self.experts, self.width))]
+                + [TensorSpec(f"{p}{e}.{n}", s) for e in range(self.experts)
+                   for n, s in (("gate", (self.inter, self.width)), ("up", (self.inter, self.width)),
+                                ("down", (self.width, self.inter)))])
+
+    def bind(self, tensors, runtime):
+        self.runtime = runtime
+        p = self.prefix
+        self.router = tensors[p + "router"].to(runtime.device, torch.float32)
+        self.w = [{n: runtime.matrix(tensors[f"{p}{e}.{n}"]) for n in ("gate", "up", "down")} for e in range(self.experts)]
+
+    def forward(self, x, batch):
+        probs = torch.softmax(x.float() @ self.router.t(), dim=-1)
+        weight, choice = probs.max(dim=-1)
+        out = torch.zeros_like(x)
+        k = self.runtime.kernels
+        for e in range(self.experts):
+            rows = (choice == e).nonzero().flatten()
+            if rows.numel():
+                xe = x[rows].contiguous()
+                gate_up = torch.cat([self.w[e]["gate"], self.w[e]["up"]], 0)
+                ye = k.linear(k.linear_swiglu(xe, gate_up), self.w[e]["down"])     # the engine's own kernels per expert
+                out[rows] = (ye.float() * weight[rows, None]).to(x.dtype)
+        return out
+
+
+class LearnedPositions:
+    """An absolute encoding: a learned table row is added to every embedded token; nothing is rotated."""
+
+    def __init__(self, width, max_positions, weight_name):
+        self.width, self.max_positions, self.weight_name = width, max_positions, weight_name
+
+    def tensor_specs(self):
+        return [TensorSpec(self.weight_name, (self.max_positions, self.width))]
+
+    def bind(self, tensors, runtime):
+        self.table = tensors[self.weight_name].to(runtime.device, torch.float32)
+
+    def embed(self, x, batch):
+        return x + self.table[batch.positions.long()]
+
+    def rotation(self):
+        return None
+
+
+def routed_model_spec(cfg):
+    layers = tuple(LayerSpec(
+        norm1=PartSpec("rmsnorm", dict(width=cfg["width"], eps=1e-5, weight_name=f"m.{i}.n1")),
+        mixer=PartSpec("attention", dict(width=cfg["width"], heads=2, kv_heads=1, head_dim=32, prefix=f"m.{i}.attn.")),
+        norm2=PartSpec("rmsnorm", dict(width=cfg["width"], eps=1e-5, weight_name=f"m.{i}.n2")),
+        feed_forward=PartSpec("toy_routed", dict(width=cfg["width"], inter=cfg["inter"], experts=cfg["experts"],
+                                                 prefix=f"m.{i}.moe.")),
+    ) for i in range(cfg["layers"]))
+    return ModelSpec(vocab_size=cfg["vocab"], width=cfg["width"], embedding_name="emb", layers=layers,
+                     order=tuple(LayerCall(i) for i in range(cfg["layers"])),
+                     final_norm=PartSpec("rmsnorm", dict(width=cfg["width"], eps=1e-5, weight_name="norm")),
+                     head_name="head",
+                     input_position=PartSpec("toy_learned", dict(width=cfg["width"], max_positions=cfg["positions"],
+                                                                 weight_name="pos")))
+
+
+def routed_plain_forward(cfg, w, tokens):
+    T = len(tokens)
+    x = w["emb"][torch.as_tensor(tokens)] + w["pos"][:T]
+    for i in range(cfg["layers"]):
+        p = f"m.{i}."
+        h = plain_llama.rms_norm(x, w[p + "n1"], 1e-5)
+        q = (h @ w[p + "attn.q_proj.weight"].T).view(T, 2, 32)            # no rotation: order comes from the table
+        k = (h @ w[p + "attn.k_proj.weight"].T).view(T, 1, 32)
+        v = (h @ w[p + "attn.v_proj.weight"].T).view(T, 1, 32)
+        x = x + plain_llama.causal_attention(q, k, v).reshape(T, 64) @ w[p + "attn.o_proj.weight"].T
+        h = plain_llama.rms_norm(x, w[p + "n2"], 1e-5)
+        probs = torch.softmax(h @ w[p + "moe.router"].T, dim=-1)
+        weight, choice = probs.max(dim=-1)
+        out = torch.zeros_like(h)
+        for t in range(T):
+            e = int(choice[t])
+            ws = {"gate_proj.weight": w[f"{p}moe.{e}.gate"], "up_proj.weight": w[f"{p}moe.{e}.up"],
+                  "down_proj.weight": w[f"{p}moe.{e}.down"]}
+            out[t] = plain_llama.swiglu(h[t:t + 1], ws, "")[0] * weight[t]
+        x = x + out
+    return plain_llama.rms_norm(x, w["norm"], 1e-5) @ w["head"].T
+
+
+def test_a_routed_feed_forward_and_a_learned_position_encoding(tmp_path):
+    register_part("feed_forward", "toy_routed", ToyRoutedFF)
+    register_part("position", "toy_learned", LearnedPositions)
+    register_architecture("ToyRoutedForTests", lambda d: d, routed_model_spec)
+    cfg = {"architectures": ["ToyRoutedForTests"], "width": 64, "layers": 2, "vocab": 120, "inter": 96, "experts": 3,
+           "positions": 128}
+    folder = write_model_folder(str(tmp_path / "routed"), cfg, seed=11, std=0.15, norm_std=0.1, dtype=torch.float32)
+    _, w = plain_llama.read_model_folder(folder)
+    requests = {f"r{i}": helpers.random_tokens(120, n, 40 + i) for i, n in enumerate((50, 21, 37, 8))}
+    ref = {rid: routed_plain_forward(cfg, w, toks) for rid, toks in requests.items()}
+    engine = build_engine(folder, EngineConfig(dtype="float32", page_size=8, max_batch_size=4, max_seq_len=128, device="cuda:0"))
+    assert engine.graphs is None                           # a part that does not declare itself safe to capture
+    for steps in (helpers.steps_whole(requests), helpers.steps_decode_tail(requests, 8), helpers.steps_mixed(requests)):
+        got = helpers.run_steps(engine, steps)
+        for rid in ref:
+            assert helpers.relative_error(got[rid], ref[rid]) < 1e-4, rid
