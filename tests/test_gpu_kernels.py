@@ -313,3 +313,22 @@ def test_tcgen05_product_with_swiglu(kernels, twin, M, inter, K):
     finally:
         kernels.use_tcgen05 = before
     close(got, ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K", [(17, 320, 96), (32, 2048, 2048), (40, 100, 1000), (64, 3072, 2048), (64, 2048, 8192)])
+def test_skinny_tensor_core_product_at_all_its_row_counts(kernels, twin, M, N, K):
+    """The weight-streaming kernel takes up to 64 rows, although the engine hands it 16 at most."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    before = kernels.TENSOR_SKINNY_ROWS
+    kernels.TENSOR_SKINNY_ROWS = 64
+    try:
+        got = kernels.linear(x, w)
+        if N % 2 == 0:
+            fused = kernels.linear_swiglu(x, w)
+    finally:
+        kernels.TENSOR_SKINNY_ROWS = before
+    close(got, x.double() @ w.double().t(), torch.bfloat16)
+    if N % 2 == 0:
+        close(fused, twin.linear_swiglu(x.double(), w.double()), torch.bfloat16)
