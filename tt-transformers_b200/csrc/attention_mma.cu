@@ -433,6 +433,22 @@ static int launch_attention(const void* qkv, int q_row_stride, void* out, const 
     return ttb_launch_status();
 }
 
+// Merge of split partial results by itself (the tcgen05 attention kernel writes the same format).
+TTB_EXPORT int ttb_attention_merge(const float* partial_o, const float* partial_ml, void* out, int rows, int num_splits,
+                                   int head_dim, cudaStream_t stream) {
+    if (rows == 0) return TTB_OK;
+    if (!partial_o || !partial_ml || !out || num_splits < 1) return TTB_ERR_ARGUMENT;
+    if (head_dim == 64)
+        ttb_launch(attention_merge_kernel<64>, dim3((rows + 3) / 4), dim3(128), 0, stream, partial_o, partial_ml,
+                   (__nv_bfloat16*)out, rows, num_splits);
+    else if (head_dim == 128)
+        ttb_launch(attention_merge_kernel<128>, dim3((rows + 3) / 4), dim3(128), 0, stream, partial_o, partial_ml,
+                   (__nv_bfloat16*)out, rows, num_splits);
+    else
+        return TTB_ERR_UNSUPPORTED;
+    return ttb_launch_status();
+}
+
 // Rows of a query tile in each shape: the host cuts segments into tiles of rows / (heads / kv_heads) tokens.
 TTB_EXPORT int ttb_attention_mma_tile_rows(int decode_shape) { return decode_shape ? 16 : 64; }
 

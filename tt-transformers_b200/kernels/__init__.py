@@ -14,6 +14,7 @@ src/tt_transformers/modules/mlp/mlp_1d.py:240-294). Everything else is ours.
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Optional
 
 import torch
@@ -72,7 +73,8 @@ class CudaKernels:
                      "ttb_paged_attention_generic", "ttb_gemm_simt", "ttb_gemv", "ttb_sample",
                      "ttb_paged_attention_mma", "ttb_attention_mma_tile_rows", "ttb_attention_mma_supports",
                      "ttb_gemv_mma", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm",
-                     "ttb_gemm_tcgen05"):
+                     "ttb_gemm_tcgen05", "ttb_paged_attention_tcgen05", "ttb_attention_tcgen05_supports",
+                     "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -83,11 +85,12 @@ class CudaKernels:
         self.launches = 0     # how many of our kernels were launched (counted for reports)
         self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.use_mma_attention = True
+        # prompt portions at head size 64: the TMA + tcgen05 attention kernel (False: the mma.sync one)
+        self.use_tcgen05_attention = os.environ.get("TTB200_TCGEN05_ATTENTION", "1") == "1"
         # bfloat16 products with more rows than the skinny kernel takes go to the library's product, or,
         # with this switch (or TTB200_TCGEN05=1 in the environment), to the TMA + tcgen05 kernel of
         # gemm_tcgen05.cu, which is correct at every size but, with its one-tile-per-block schedule,
         # reaches 0.6 to 0.8 of the library's throughput at prefill sizes.
-        import os
         self.use_tcgen05 = os.environ.get("TTB200_TCGEN05", "0") == "1"
         with torch.cuda.device(self.device):
             self.tc_error = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -112,8 +115,11 @@ class CudaKernels:
         tc = int(self.tc_error.item())
         if tc != 0:
             self.tc_error.zero_()
-            role = {1: "the TMA producer", 2: "the MMA issuer", 3: "the epilogue"}.get(tc, f"role {tc}")
-            raise EngineDeviceError(f"the tcgen05 matrix product gave up waiting on a barrier ({role}); its result is invalid")
+            role = {1: "the product's TMA producer", 2: "the product's MMA issuer", 3: "the product's epilogue",
+                    11: "attention's TMA producer", 12: "attention's MMA issuer waiting for the queries",
+                    13: "attention's MMA issuer waiting for keys", 14: "attention's MMA issuer waiting for P",
+                    15: "attention's softmax warps", 16: "attention's epilogue"}.get(tc, f"role {tc}")
+            raise EngineDeviceError(f"a tcgen05 kernel gave up waiting on a barrier ({role}); its result is invalid")
         value = int(self.status.item())
         if value != 0:
             self.status.zero_()
@@ -251,15 +257,17 @@ class CudaKernels:
             int(view.window or 0), view.keys.shape[0], self._p(self.status), self._stream()), "paged_attention")
         return out
 
-    def _attention_plan(self, batch, rep: int, kv_heads: int, head_dim: int):
+    def _attention_plan(self, batch, rep: int, kv_heads: int, head_dim: int, big_tiles: bool = False):
         """How the step's segments are cut into query tiles, and into how many key splits:
-        derived once per step and geometry, reused by every layer."""
-        key = ("attention_plan", rep, kv_heads, head_dim)
+        derived once per step and geometry, reused by every layer. big_tiles: the 128-row
+        tiles of the tcgen05 kernel."""
+        key = ("attention_plan", rep, kv_heads, head_dim, big_tiles)
         plan = batch.extras.get(key)
         if plan is not None:
             return plan
-        decode_shape = batch.max_seg_len * rep <= 16
-        rows = int(self.lib.ttb_attention_mma_tile_rows(1 if decode_shape else 0))
+        decode_shape = batch.max_seg_len * rep <= 16 and not big_tiles
+        rows = (int(self.lib.ttb_attention_tcgen05_tile_rows()) if big_tiles
+                else int(self.lib.ttb_attention_mma_tile_rows(1 if decode_shape else 0)))
         tokens_per_tile = max(1, rows // rep)
         if decode_shape:
             seg, tok0, n_tiles = None, None, batch.num_segments
@@ -275,7 +283,8 @@ class CudaKernels:
         # Key splits: with fewer blocks than fit the GPU at once, as many splits as fill it in one
         # wave (chunks of at least 256 keys); with more, a few waves of chunks of at least 2,048 keys.
         blocks = n_tiles * kv_heads
-        slots = self.sm_count * int(self.lib.ttb_attention_mma_blocks_per_sm(1 if decode_shape else 0, head_dim))
+        slots = self.sm_count * (2 if big_tiles else
+                                 int(self.lib.ttb_attention_mma_blocks_per_sm(1 if decode_shape else 0, head_dim)))
         if blocks < slots:
             splits = max(1, min(slots // blocks, batch.max_context // 256))
         else:
@@ -284,8 +293,29 @@ class CudaKernels:
         batch.extras[key] = plan
         return plan
 
+    def _attention_tcgen05(self, qkv, out, batch, heads, kv_heads, head_dim, scale, view):
+        tokens = qkv.shape[0]
+        _, seg, tok0, n_tiles, splits = self._attention_plan(batch, heads // kv_heads, kv_heads, head_dim, big_tiles=True)
+        partial_o = partial_ml = None
+        if splits > 1:
+            partial_o = torch.empty(tokens * heads * splits * head_dim, dtype=torch.float32, device=self.device)
+            partial_ml = torch.empty(tokens * heads * splits * 2, dtype=torch.float32, device=self.device)
+        self._check(self.lib.ttb_paged_attention_tcgen05(
+            self._p(qkv), qkv.stride(0), self._p(out), self._p(batch.cu_seqlens), self._p(batch.seg_pos0),
+            self._p(view.keys), self._p(view.values), self._p(view.block_table), view.block_table.shape[1],
+            view.page_size, self._p(seg), self._p(tok0), n_tiles, tokens, heads, kv_heads, head_dim,
+            ctypes.c_float(scale), splits, self._p(partial_o), self._p(partial_ml), view.keys.shape[0],
+            self._p(self.status), self._p(self.tc_error), self._stream()), "paged_attention_tcgen05")
+        if splits > 1:
+            self._check(self.lib.ttb_attention_merge(self._p(partial_o), self._p(partial_ml), self._p(out),
+                                                     tokens * heads, splits, head_dim, self._stream()), "attention_merge")
+
     def _attention_mma(self, qkv, out, batch, heads, kv_heads, head_dim, scale, view):
         tokens = qkv.shape[0]
+        if (self.use_tcgen05_attention and batch.max_seg_len * (heads // kv_heads) > 16 and view.keys.is_contiguous()
+                and view.values.is_contiguous() and qkv.stride(0) % head_dim == 0
+                and self.lib.ttb_attention_tcgen05_supports(heads, kv_heads, head_dim, view.page_size, int(view.window or 0))):
+            return self._attention_tcgen05(qkv, out, batch, heads, kv_heads, head_dim, scale, view)
         decode_shape, seg, tok0, n_tiles, splits = self._attention_plan(batch, heads // kv_heads, kv_heads, head_dim)
         partial_o = partial_ml = None
         if splits > 1:
