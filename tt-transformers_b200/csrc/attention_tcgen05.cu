@@ -126,7 +126,9 @@ __device__ __forceinline__ uint64_t fa_desc(uint32_t addr) {
 }
 
 struct FaBars {
-    uint64_t q_full, kv_full[FA_STAGES], kv_empty[FA_STAGES], s_full[2], s_empty[2], p_full, pv_done;
+    // p_full[b]: the softmax warps have written P buffer b; p_free[b]: the P V that read buffer b has completed
+    // (so the buffer may be written again, and O holds that product)
+    uint64_t q_full, kv_full[FA_STAGES], kv_empty[FA_STAGES], s_full[2], s_empty[2], p_full[2], p_free[2];
 };
 
 __global__ void __launch_bounds__(FA_THREADS)
@@ -142,14 +144,15 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~(uintptr_t)1023);
     unsigned char* q_tile = base;
     unsigned char* p_tile = base + FA_QP_BYTES;
-    unsigned char* k_stage = p_tile + FA_QP_BYTES;
+    unsigned char* k_stage = p_tile + 2 * FA_QP_BYTES;          // two P buffers
     unsigned char* v_stage = k_stage + FA_STAGES * FA_TILE_BYTES;
     FaBars* bars = reinterpret_cast<FaBars*>(v_stage + FA_STAGES * FA_TILE_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1);
     int* page_cache = reinterpret_cast<int*>(tmem_slot + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qt = blockIdx.x, g = blockIdx.y, split = blockIdx.z;
+    // later tiles of a segment see more keys: they go first, so that the longest blocks do not end the grid
+    const int qt = gridDim.x - 1 - blockIdx.x, g = blockIdx.y, split = blockIdx.z;
     const int rep = heads / kv_heads;
     const int seg = qtile_seg[qt], tok0 = qtile_tok0[qt];
     const int seg_start = cu_seqlens[seg];
@@ -177,8 +180,10 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
             fa_mbar_init(fa_smem(&bars->s_full[b]), 1);
             fa_mbar_init(fa_smem(&bars->s_empty[b]), 4);      // one arrival per softmax warp
         }
-        fa_mbar_init(fa_smem(&bars->p_full), 4);
-        fa_mbar_init(fa_smem(&bars->pv_done), 1);
+        for (int b = 0; b < 2; ++b) {
+            fa_mbar_init(fa_smem(&bars->p_full[b]), 4);
+            fa_mbar_init(fa_smem(&bars->p_free[b]), 1);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fa_fence_async();
     }
@@ -257,15 +262,15 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
             if (ok && !issue_qk(0)) { atomicExch(error_flag, 13); ok = false; }
             for (int j = 0; j < num_tiles && ok; ++j) {
                 if (j + 1 < num_tiles && !issue_qk(j + 1)) { atomicExch(error_flag, 13); ok = false; break; }
-                if (!fa_wait(fa_smem(&bars->p_full), j & 1)) { atomicExch(error_flag, 14); ok = false; break; }
+                if (!fa_wait(fa_smem(&bars->p_full[j & 1]), (j >> 1) & 1)) { atomicExch(error_flag, 14); ok = false; break; }
                 fa_fence_after();
                 const int s = j % FA_STAGES;
-                const uint32_t pa = fa_smem(p_tile), va = fa_smem(v_stage) + s * FA_TILE_BYTES;
+                const uint32_t pa = fa_smem(p_tile) + (j & 1) * FA_QP_BYTES, va = fa_smem(v_stage) + s * FA_TILE_BYTES;
 #pragma unroll
                 for (int k = 0; k < FA_BN / 16; ++k)
                     fa_mma(tmem_o, fa_desc(pa + k * 32), fa_desc(va + k * 16 * FA_HD * 2), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
                 fa_commit(fa_smem(&bars->kv_empty[s]));
-                fa_commit(fa_smem(&bars->pv_done));
+                fa_commit(fa_smem(&bars->p_free[j & 1]));
             }
         }
     } else {
@@ -301,10 +306,16 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
             float tile_max = -INFINITY;
 #pragma unroll
             for (int c = 0; c < 64; ++c) tile_max = fmaxf(tile_max, sc[c]);
+            // The exponent's reference `row_max` follows the true maximum only when that has moved by more
+            // than 2^8: probabilities stay below 256 and O needs rescaling (which has to wait for the P V
+            // before) only then. Sum and O use the same reference, so the result is exact all the same.
+            float alpha = 1.f;
             const float new_max = fmaxf(row_max, tile_max);
-            const float alpha = (row_max == -INFINITY) ? 0.f : fa_exp2((row_max - new_max) * scale_log2);
-            const float neg = (new_max == -INFINITY) ? 0.f : -new_max * scale_log2;
-            row_max = new_max;
+            if (row_max == -INFINITY || (new_max - row_max) * scale_log2 > 8.f) {
+                alpha = (row_max == -INFINITY) ? 0.f : fa_exp2((row_max - new_max) * scale_log2);
+                row_max = new_max;
+            }
+            const float neg = (row_max == -INFINITY) ? 0.f : -row_max * scale_log2;
             float sum = 0.f;
             uint32_t packed[32];
 #pragma unroll
@@ -316,12 +327,14 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                 packed[c >> 1] = *reinterpret_cast<uint32_t*>(&h);
             }
             row_sum = row_sum * alpha + sum;
-            // the P buffer and the O accumulator are ours once the P V of the tile before has completed
-            if (j > 0 && !fa_wait(fa_smem(&bars->pv_done), (j - 1) & 1)) { ok = false; break; }
-            fa_fence_after();
+            // P buffer j & 1 is free once the P V of tile j - 2 has completed
+            if (j >= 2 && !fa_wait(fa_smem(&bars->p_free[j & 1]), ((j >> 1) - 1) & 1)) { ok = false; break; }
             if (j > 0) {
                 const bool moved = alpha != 1.f;
-                if (__any_sync(0xffffffffu, moved)) {          // warp-collective: rows whose maximum stayed scale by 1
+                if (__any_sync(0xffffffffu, moved)) {          // warp-collective: rows whose reference stayed scale by 1
+                    // O must hold the P V of tile j - 1 before it is rescaled
+                    if (!fa_wait(fa_smem(&bars->p_free[(j - 1) & 1]), ((j - 1) >> 1) & 1)) { ok = false; break; }
+                    fa_fence_after();
                     uint32_t o[2][32];
                     fa_ld32(lane_base + 2 * FA_BN, o[0]);
                     fa_ld32(lane_base + 2 * FA_BN + 32, o[1]);
@@ -345,7 +358,7 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                 }
             }
             // P row in the swizzled K-major layout: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
-            unsigned char* p_row = p_tile + row * 128;
+            unsigned char* p_row = p_tile + (j & 1) * FA_QP_BYTES + row * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c)
                 *reinterpret_cast<uint4*>(p_row + ((c ^ (row & 7)) << 4)) =
@@ -353,10 +366,10 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
             fa_fence_async();            // generic-proxy writes become visible to the tensor core's reads
             fa_fence_before();
             __syncwarp();
-            if (lane == 0) fa_arrive(fa_smem(&bars->p_full));
+            if (lane == 0) fa_arrive(fa_smem(&bars->p_full[j & 1]));
         }
         if (!ok && lane == 0) atomicExch(error_flag, 15);
-        if (ok && num_tiles > 0 && !fa_wait(fa_smem(&bars->pv_done), (num_tiles - 1) & 1)) {
+        if (ok && num_tiles > 0 && !fa_wait(fa_smem(&bars->p_free[(num_tiles - 1) & 1]), ((num_tiles - 1) >> 1) & 1)) {
             ok = false;
             if (lane == 0) atomicExch(error_flag, 16);
         }
@@ -482,7 +495,7 @@ TTB_EXPORT int ttb_paged_attention_tcgen05(const void* qkv, int q_row_stride, vo
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return TTB_ERR_UNSUPPORTED;
     }
-    const size_t smem = 1024 + 2 * FA_QP_BYTES + 2 * FA_STAGES * FA_TILE_BYTES + sizeof(FaBars) + 16 + FA_TABLE * sizeof(int);
+    const size_t smem = 1024 + 3 * FA_QP_BYTES + 2 * FA_STAGES * FA_TILE_BYTES + sizeof(FaBars) + 16 + FA_TABLE * sizeof(int);
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
