@@ -303,9 +303,15 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                 for (int c = 0; c < 64; ++c)
                     if (key0 + c > qpos || key0 + c >= k_end) sc[c] = -INFINITY;
             }
-            float tile_max = -INFINITY;
+            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};     // four chains instead of one of 64
 #pragma unroll
-            for (int c = 0; c < 64; ++c) tile_max = fmaxf(tile_max, sc[c]);
+            for (int c = 0; c < 64; c += 4) {
+                m4[0] = fmaxf(m4[0], sc[c]);
+                m4[1] = fmaxf(m4[1], sc[c + 1]);
+                m4[2] = fmaxf(m4[2], sc[c + 2]);
+                m4[3] = fmaxf(m4[3], sc[c + 3]);
+            }
+            const float tile_max = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
             // The exponent's reference `row_max` follows the true maximum only when that has moved by more
             // than 2^8: probabilities stay below 256 and O needs rescaling (which has to wait for the P V
             // before) only then. Sum and O use the same reference, so the result is exact all the same.
@@ -316,17 +322,20 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                 row_max = new_max;
             }
             const float neg = (row_max == -INFINITY) ? 0.f : -row_max * scale_log2;
-            float sum = 0.f;
+            float s4[4] = {0.f, 0.f, 0.f, 0.f};
             uint32_t packed[32];
 #pragma unroll
-            for (int c = 0; c < 64; c += 2) {
+            for (int c = 0; c < 64; c += 4) {
                 const float p0 = fa_exp2(fmaf(sc[c], scale_log2, neg));
                 const float p1 = fa_exp2(fmaf(sc[c + 1], scale_log2, neg));
-                sum += p0 + p1;
-                __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
-                packed[c >> 1] = *reinterpret_cast<uint32_t*>(&h);
+                const float p2 = fa_exp2(fmaf(sc[c + 2], scale_log2, neg));
+                const float p3 = fa_exp2(fmaf(sc[c + 3], scale_log2, neg));
+                s4[0] += p0; s4[1] += p1; s4[2] += p2; s4[3] += p3;
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(p0, p1), h1 = __floats2bfloat162_rn(p2, p3);
+                packed[c >> 1] = *reinterpret_cast<uint32_t*>(&h0);
+                packed[(c >> 1) + 1] = *reinterpret_cast<uint32_t*>(&h1);
             }
-            row_sum = row_sum * alpha + sum;
+            row_sum = row_sum * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
             // P buffer j & 1 is free once the P V of tile j - 2 has completed
             if (j >= 2 && !fa_wait(fa_smem(&bars->p_free[j & 1]), ((j >> 1) - 1) & 1)) { ok = false; break; }
             if (j > 0) {
