@@ -332,3 +332,27 @@ def test_skinny_tensor_core_product_at_all_its_row_counts(kernels, twin, M, N, K
     close(got, x.double() @ w.double().t(), torch.bfloat16)
     if N % 2 == 0:
         close(fused, twin.linear_swiglu(x.double(), w.double()), torch.bfloat16)
+
+
+@pytest.mark.parametrize("heads,kv_heads,head_dim,page_size,segments,width", [
+    (8, 2, 64, 16, [(300, 1), (0, 1), (17, 1)], 128), (32, 8, 64, 16, [(8000, 1)] * 8, 2048),
+    (6, 2, 128, 8, [(63, 1), (64, 1)], 96), (4, 4, 16, 4, [(5, 1), (6, 1), (7, 1), (0, 1), (100, 1)], 72),
+    (3, 1, 32, 8, [(40, 1)], 96)])
+def test_fused_qkv_projection_rotation_and_cache_write(kernels, twin, heads, kv_heads, head_dim, page_size, segments, width):
+    """One kernel for a decode step's QKV product, rotation and cache write against the three steps one by one."""
+    _, batch, view = make_paged_case(torch.bfloat16, heads, kv_heads, head_dim, page_size, segments, seed=21)
+    g = torch.Generator(device="cuda").manual_seed(22)
+    M = len(segments)
+    x = torch.randn(M, width, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn((heads + 2 * kv_heads) * head_dim, width, device="cuda", generator=g) / math.sqrt(width)).to(torch.bfloat16)
+    inv_freq = (1.0 / (500000.0 ** (torch.arange(0, head_dim, 2).float() / head_dim))).cuda()
+    view2 = SimpleNamespace(keys=view.keys.float(), values=view.values.float(), block_table=view.block_table,
+                            page_size=page_size, window=None)
+    q = kernels.fused_qkv_rope(x, w, batch, inv_freq, head_dim, heads, kv_heads, head_dim, view, True)
+    assert q is not None and q.shape == (M, heads * head_dim)
+    qkv = (x.float() @ w.float().t())                     # float32 product, then the twin's rotation and write
+    twin.rope_kv_write(qkv, batch, inv_freq, head_dim, heads, kv_heads, head_dim, view2, True)
+    close(q, qkv[:, :heads * head_dim], torch.bfloat16)
+    close(view.keys, view2.keys, torch.bfloat16)
+    close(view.values, view2.values, torch.bfloat16)
+    kernels.check_status()

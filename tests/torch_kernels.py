@@ -47,6 +47,9 @@ class TorchKernels:
     def linear_swiglu(self, x, w_gate_up):
         return self.swiglu(self.linear(x, w_gate_up))
 
+    def fused_qkv_rope(self, *args, **kwargs):
+        return None          # the twin has no fused form: the caller runs projection, rotation and write one by one
+
     # ------------------------------------------------------------------ attention
     def rope_kv_write(self, qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True):
         T = qkv.shape[0]

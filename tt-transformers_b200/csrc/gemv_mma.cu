@@ -14,11 +14,28 @@
 //   HALF  rows n0 .. n0+7 of w, upper half zero (more blocks for matrices with few rows)
 //   PAIR  rows n0 .. n0+7 of w (gate) and of w + pair_offset rows (up); the epilogue writes
 //         silu(gate) * up, so the SwiGLU product never round-trips through memory
+//   ROPE  the fused QKV projection of a decode step: a block owns rows i .. i+7 of one head and their
+//         rotation partners i + head_dim/2 .., so that the epilogue can rotate query and key pairs by
+//         their positions (float32 angles, accurate sincosf), write the queries out and put keys and
+//         values straight into their cache pages; no rotation kernel and no qkv round trip
 #include "common.cuh"
 
 #define GM_FULL 0
 #define GM_HALF 1
 #define GM_PAIR 2
+#define GM_ROPE 3
+
+// What the fused QKV mode needs beyond the product: positions, rotation frequencies and the cache.
+struct GmRope {
+    const int* positions;        // [M]
+    const int* seg_of_token;     // [M]
+    const float* inv_freq;       // [head_dim / 2]
+    const int* block_table;      // [segments, table_width]
+    __nv_bfloat16* key_pages;    // [num_pages, kv_heads, page_size, head_dim]
+    __nv_bfloat16* value_pages;
+    int* status;
+    int table_width, page_size, num_pages, heads, kv_heads, head_dim, write_kv;
+};
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     uint4 v;
@@ -42,13 +59,17 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
 template <int NB, int RG, int MODE, int GM_WARPS, typename TO>
 __global__ void __launch_bounds__(GM_WARPS * 32)
 gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w, TO* __restrict__ out,
-                int M, int N, int K, int ldx, int ldw, int ldo, int pair_offset) {
+                int M, int N, int K, int ldx, int ldw, int ldo, int pair_offset, GmRope rope) {
     constexpr int ROWS_PER_GROUP = (MODE == GM_FULL) ? 16 : 8;
     constexpr int GM_THREADS = GM_WARPS * 32;
     extern __shared__ float4 partial[];          // [GM_WARPS][RG * NB * 32]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int n0 = blockIdx.x * ROWS_PER_GROUP * RG;
+    int n0 = blockIdx.x * ROWS_PER_GROUP * RG;
+    if (MODE == GM_ROPE) {       // blocks per head: head_dim / 16; eight rows of the first half, pair_offset = head_dim / 2
+        const int per_head = rope.head_dim >> 4;
+        n0 = (blockIdx.x / per_head) * rope.head_dim + (blockIdx.x % per_head) * 8;
+    }
 
     // row pointers of this thread: [rg][half]
     const __nv_bfloat16* wrow[RG][2];
@@ -61,7 +82,7 @@ gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
             int upper = n0 + rg * 16 + 8 + g;
             if (upper > N - 1) upper = N - 1;
             wrow[rg][1] = w + (size_t)upper * ldw;
-        } else if (MODE == GM_PAIR) {
+        } else if (MODE == GM_PAIR || MODE == GM_ROPE) {
             wrow[rg][1] = w + (size_t)(lower + pair_offset) * ldw;
         } else {
             wrow[rg][1] = nullptr;
@@ -154,7 +175,44 @@ gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
         const int eg = el >> 2, et = el & 3;
         const int m0 = nb * 8 + 2 * et, m1 = m0 + 1;
         const int lower = n0 + rg * ROWS_PER_GROUP + eg;
-        if (MODE == GM_PAIR) {
+        if (MODE == GM_ROPE) {
+            const int hd = rope.head_dim, half = hd >> 1;
+            const int head = lower / hd, i = lower - head * hd;             // i < half: index of the rotation pair
+            const bool is_q = head < rope.heads, is_k = !is_q && head < rope.heads + rope.kv_heads;
+            const float freq = (is_q || is_k) ? rope.inv_freq[i] : 0.f;
+#pragma unroll
+            for (int which = 0; which < 2; ++which) {
+                const int m = which ? m1 : m0;
+                if (m >= M) continue;
+                float lo = which ? s.y : s.x, up = which ? s.w : s.z;
+                const int pos = rope.positions[m];
+                if (is_q || is_k) {
+                    float sn, cs;
+                    sincosf((float)pos * freq, &sn, &cs);
+                    const float a = lo, b = up;
+                    lo = a * cs - b * sn;
+                    up = b * cs + a * sn;
+                }
+                if (is_q) {
+                    out[(size_t)m * ldo + lower] = from_float<TO>(lo);
+                    out[(size_t)m * ldo + lower + half] = from_float<TO>(up);
+                } else if (rope.write_kv) {
+                    const int kvh = head - rope.heads - (is_k ? 0 : rope.kv_heads);
+                    const int page_index = pos / rope.page_size;
+                    int page = -1;
+                    if (page_index < rope.table_width)
+                        page = rope.block_table[(size_t)rope.seg_of_token[m] * rope.table_width + page_index];
+                    if ((unsigned)page >= (unsigned)rope.num_pages) {
+                        atomicExch(rope.status, 0x2000000 + m);              // outside the pool: skip the write, say so
+                    } else {
+                        __nv_bfloat16* dst = (is_k ? rope.key_pages : rope.value_pages) +
+                            (((size_t)page * rope.kv_heads + kvh) * rope.page_size + (pos - page_index * rope.page_size)) * hd;
+                        dst[i] = __float2bfloat16_rn(lo);
+                        dst[i + half] = __float2bfloat16_rn(up);
+                    }
+                }
+            }
+        } else if (MODE == GM_PAIR) {
             if (lower < N) {
                 if (m0 < M) out[(size_t)m0 * ldo + lower] = from_float<TO>(s.x / (1.f + __expf(-s.x)) * s.z);
                 if (m1 < M) out[(size_t)m1 * ldo + lower] = from_float<TO>(s.y / (1.f + __expf(-s.y)) * s.w);
@@ -177,7 +235,7 @@ gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
 
 template <int NB, int RG, int MODE, int GM_WARPS, typename TO>
 static int gemv_mma_launch(const void* x, const void* w, void* out, int M, int N, int K, int ldx, int ldw, int ldo,
-                           int pair_offset, cudaStream_t stream) {
+                           int pair_offset, cudaStream_t stream, const GmRope* rope = nullptr) {
     constexpr int rows = ((MODE == GM_FULL) ? 16 : 8) * RG;
     const size_t smem = (size_t)GM_WARPS * RG * NB * 32 * sizeof(float4);
     auto kernel = gemv_mma_kernel<NB, RG, MODE, GM_WARPS, TO>;
@@ -188,8 +246,11 @@ static int gemv_mma_launch(const void* x, const void* w, void* out, int M, int N
         if (e != cudaSuccess) return (int)e;
     }
     configured = true;
-    ttb_launch(kernel, dim3((N + rows - 1) / rows), dim3(GM_THREADS), smem, stream,
-        (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (TO*)out, M, N, K, ldx, ldw, ldo, pair_offset);
+    GmRope none = {};
+    const int blocks = (MODE == GM_ROPE) ? N / 16 : (N + rows - 1) / rows;
+    ttb_launch(kernel, dim3(blocks), dim3(GM_THREADS), smem, stream,
+        (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (TO*)out, M, N, K, ldx, ldw, ldo, pair_offset,
+        rope ? *rope : none);
     return ttb_launch_status();
 }
 
@@ -232,4 +293,26 @@ TTB_EXPORT int ttb_gemv_mma(const void* x, const void* w, void* out, int out_dty
                    : gemv_mma_by_rows<GM_HALF, __nv_bfloat16>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream);
     return f32 ? gemv_mma_by_rows<GM_FULL, float>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream)
                : gemv_mma_by_rows<GM_FULL, __nv_bfloat16>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream);
+}
+
+
+// The QKV projection of a decode step fused with the rotation and the cache write.
+// x [M <= 8, K], w [(heads + 2 kv_heads) * head_dim, K] (queries, keys, values stacked), bfloat16;
+// q_out [M, heads * head_dim] gets the rotated queries; rotated keys and the values go to their
+// pages. head_dim a multiple of 16, full rotary (every pair of a head is rotated).
+TTB_EXPORT int ttb_gemv_qkv_rope(const void* x, const void* w, void* q_out, int M, int K, int ldx, int ldw,
+                                 const int* positions, const int* seg_of_token, const float* inv_freq, int heads,
+                                 int kv_heads, int head_dim, void* key_pages, void* value_pages,
+                                 const int* block_table, int table_width, int page_size, int num_pages, int write_kv,
+                                 int* status, cudaStream_t stream) {
+    if (M == 0) return TTB_OK;
+    if (!x || !w || !q_out || !positions || !inv_freq || !status) return TTB_ERR_ARGUMENT;
+    if (write_kv && (!seg_of_token || !key_pages || !value_pages || !block_table)) return TTB_ERR_ARGUMENT;
+    if (M > 8 || K < 8 || (K & 7) || (ldx & 7) || (ldw & 7) || !aligned16(x) || !aligned16(w)) return TTB_ERR_UNSUPPORTED;
+    if (head_dim < 16 || (head_dim & 15)) return TTB_ERR_UNSUPPORTED;
+    GmRope rope = {positions, seg_of_token, inv_freq, block_table, (__nv_bfloat16*)key_pages, (__nv_bfloat16*)value_pages,
+                   status, table_width, page_size, num_pages, heads, kv_heads, head_dim, write_kv};
+    const int N = (heads + 2 * kv_heads) * head_dim;
+    return gemv_mma_launch<1, 1, GM_ROPE, 8, __nv_bfloat16>(x, w, q_out, M, N, K, ldx, ldw, heads * head_dim,
+                                                            head_dim / 2, stream, &rope);
 }

@@ -74,7 +74,7 @@ class CudaKernels:
                      "ttb_paged_attention_mma", "ttb_attention_mma_tile_rows", "ttb_attention_mma_supports",
                      "ttb_gemv_mma", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm",
                      "ttb_gemm_tcgen05", "ttb_paged_attention_tcgen05", "ttb_attention_tcgen05_supports",
-                     "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge"):
+                     "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge", "ttb_gemv_qkv_rope"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -225,6 +225,24 @@ class CudaKernels:
                                                   self._p(self.tc_error), self._stream()), "gemm_tcgen05_swiglu")
             return out
         return self.swiglu(self.linear(x, w_gate_up))
+
+    def fused_qkv_rope(self, x, w_qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True):
+        """The QKV projection, the rotation and the cache write of a decode step in one kernel.
+        Returns the rotated queries [M, heads * head_dim], or None where the fused kernel does not
+        apply (then the caller runs the three steps one by one)."""
+        M, K = x.shape
+        if not (x.dtype == torch.bfloat16 and M <= 8 and K % 8 == 0 and x.stride(1) == 1 and x.stride(0) % 8 == 0
+                and w_qkv.stride(1) == 1 and w_qkv.stride(0) % 8 == 0 and inv_freq is not None
+                and rotary_dim == head_dim and head_dim % 16 == 0 and view is not None
+                and view.keys.dtype == torch.bfloat16 and view.keys.is_contiguous() and view.values.is_contiguous()):
+            return None
+        q = torch.empty(M, heads * head_dim, dtype=x.dtype, device=self.device)
+        self._check(self.lib.ttb_gemv_qkv_rope(
+            self._p(x), self._p(w_qkv), self._p(q), M, K, x.stride(0), w_qkv.stride(0), self._p(batch.positions),
+            self._p(batch.seg_of_token), self._p(inv_freq), heads, kv_heads, head_dim, self._p(view.keys),
+            self._p(view.values), self._p(view.block_table), view.block_table.shape[1], view.page_size,
+            view.keys.shape[0], 1 if write_kv else 0, self._p(self.status), self._stream()), "gemv_qkv_rope")
+        return q
 
     # ------------------------------------------------------------------ attention
     def rope_kv_write(self, qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True):

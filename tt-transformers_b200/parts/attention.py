@@ -51,10 +51,15 @@ class Attention(Mixer):
 
     def forward(self, x, batch, cache, write_cache=True):
         k = self.runtime.kernels
-        qkv = k.linear(x, self.w_qkv)
         rotation = self.position.rotation() if self.position is not None else None
         inv_freq, rotary_dim = rotation if rotation is not None else (None, 0)
-        k.rope_kv_write(qkv, batch, inv_freq, rotary_dim, self.heads, self.kv_heads, self.head_dim, cache, write_cache)
+        qkv = None
+        if batch.max_seg_len == 1:          # a handful of decoded tokens: projection, rotation and cache write in one kernel
+            qkv = k.fused_qkv_rope(x, self.w_qkv, batch, inv_freq, rotary_dim, self.heads, self.kv_heads, self.head_dim,
+                                   cache, write_cache)
+        if qkv is None:
+            qkv = k.linear(x, self.w_qkv)
+            k.rope_kv_write(qkv, batch, inv_freq, rotary_dim, self.heads, self.kv_heads, self.head_dim, cache, write_cache)
         mixed = k.paged_attention(qkv, batch, self.heads, self.kv_heads, self.head_dim, self.scale, cache)
         return k.linear(mixed, self.w_o)
 
