@@ -1,0 +1,67 @@
+"""Randomly drawn configurations and traces: sizes that are no power of two, every head size in steps
+of 16, any number of heads and groups, with and without frequency scaling, tied and untied heads,
+replayed in a mixed way with few pages, in 32-bit and in bfloat16, against the plain implementation."""
+
+import os
+import random
+
+import pytest
+import torch
+
+import helpers
+
+pytestmark = pytest.mark.gpu
+
+
+def draw_config(rng):
+    head_dim = rng.choice([16, 32, 48, 64, 64, 80, 96, 112, 128, 128])
+    kv_heads = rng.choice([1, 2, 3, 4])
+    rep = rng.choice([1, 2, 3, 4, 5, 8])
+    heads = kv_heads * rep
+    hidden = rng.choice([40, 72, 88, 104, 136, 200])
+    cfg = {
+        "architectures": ["LlamaForCausalLM"], "hidden_size": hidden, "num_hidden_layers": rng.choice([1, 2, 3]),
+        "num_attention_heads": heads, "num_key_value_heads": kv_heads, "head_dim": head_dim,
+        "intermediate_size": rng.choice([56, 120, 136, 264, 328]), "vocab_size": rng.choice([97, 250, 513, 1000]),
+        "rms_norm_eps": rng.choice([1e-5, 1e-6, 3e-4]), "max_position_embeddings": 512,
+        "rope_theta": rng.choice([10000.0, 500000.0, 1000000.0]), "tie_word_embeddings": rng.random() < 0.5,
+    }
+    if rng.random() < 0.6:
+        cfg["rope_scaling"] = {"rope_type": "llama3", "factor": rng.choice([2.0, 8.0, 32.0]),
+                               "low_freq_factor": rng.choice([1.0, 2.0]), "high_freq_factor": rng.choice([4.0, 8.0]),
+                               "original_max_position_embeddings": rng.choice([32, 64, 128])}
+    if rng.random() < 0.3:
+        del cfg["head_dim"]
+        cfg["hidden_size"] = heads * head_dim           # head size derived from the width
+    return cfg
+
+
+@pytest.mark.parametrize("seed", range(int(os.environ.get("TTB200_RANDOM_CONFIGS", "10"))))   # more for a longer hunt
+def test_random_configuration_and_trace(tmp_path, seed):
+    from tt_transformers_b200.config import EngineConfig
+    from tt_transformers_b200.engine.step import build_engine
+    from tt_transformers_b200.weights import write_model_folder
+
+    rng = random.Random(1000 + seed)
+    cfg = draw_config(rng)
+    folder = write_model_folder(str(tmp_path / "m"), cfg, seed=seed, std=0.06, norm_std=0.1,
+                                dtype=torch.float32 if seed % 2 else torch.bfloat16)
+    lengths = [rng.randint(1, 150) for _ in range(rng.randint(2, 6))]
+    requests = {f"r{i}": helpers.random_tokens(cfg["vocab_size"], n, seed * 100 + i) for i, n in enumerate(lengths)}
+    ref = helpers.plain_logits(folder, requests)
+    page = rng.choice([4, 8, 16, 32])
+    for dtype, tol in (("float32", 1e-4), ("bfloat16", 5e-2)):
+        for make in (helpers.steps_mixed, helpers.steps_decode_tail):
+            steps = make(requests, seed=seed) if make is helpers.steps_mixed else make(requests, tail=rng.randint(1, 40))
+            pages = -(-helpers.max_live_tokens(requests, steps, rounding=page) // page)
+            engine = build_engine(folder, EngineConfig(dtype=dtype, page_size=page, num_pages=pages, max_batch_size=4,
+                                                       max_seq_len=256, device="cuda:0"))
+            for g in engine.cache.groups:
+                g.storage.fill_(float("nan"))
+            got = helpers.run_steps(engine, steps)
+            engine.cache.audit()
+            assert engine.cache.free_pages() == engine.cache.num_pages
+            for rid in ref:
+                err = helpers.relative_error(got[rid], ref[rid])
+                assert err < tol, (cfg, dtype, make.__name__, rid, err)
+            engine.close()
