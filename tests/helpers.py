@@ -37,7 +37,8 @@ def steps_decode_tail(requests, tail=32):
     steps = []
     for rid, toks in requests.items():
         head = max(1, len(toks) - tail)
-        steps.append({"entries": [{"id": rid, "tokens": toks[:head], "want": list(range(head))}], "end": []})
+        steps.append({"entries": [{"id": rid, "tokens": toks[:head], "want": list(range(head))}],
+                      "end": [rid] if head == len(toks) else []})
         for i in range(head, len(toks)):
             steps.append({"entries": [{"id": rid, "tokens": [toks[i]], "want": [0]}],
                           "end": [rid] if i == len(toks) - 1 else []})

@@ -44,8 +44,12 @@ def test_random_configuration_and_trace(tmp_path, seed):
 
     rng = random.Random(1000 + seed)
     cfg = draw_config(rng)
-    folder = write_model_folder(str(tmp_path / "m"), cfg, seed=seed, std=0.06, norm_std=0.1,
-                                dtype=torch.float32 if seed % 2 else torch.bfloat16)
+    # Weights are stored in bfloat16, so that the plain implementation and the bfloat16 engine start from
+    # the same numbers, and are scaled with the width: at widths of thousands, weights of 0.06 give
+    # scores so large that bfloat16 arithmetic itself (a plain PyTorch bfloat16 emulation too) is off
+    # by 10 to 20 percent, which says nothing about the kernels.
+    std = min(0.06, 1.2 / cfg["hidden_size"] ** 0.5)
+    folder = write_model_folder(str(tmp_path / "m"), cfg, seed=seed, std=std, norm_std=0.1, dtype=torch.bfloat16)
     lengths = [rng.randint(1, 150) for _ in range(rng.randint(2, 6))]
     requests = {f"r{i}": helpers.random_tokens(cfg["vocab_size"], n, seed * 100 + i) for i, n in enumerate(lengths)}
     ref = helpers.plain_logits(folder, requests)

@@ -11,6 +11,8 @@ live in a buffer that the next replay of the same size overwrites.
 
 from __future__ import annotations
 
+import gc
+import weakref
 from typing import Dict, List
 
 import torch
@@ -18,7 +20,7 @@ import torch
 
 class DecodeGraphs:
     def __init__(self, engine):
-        self.engine = engine
+        self._engine = weakref.ref(engine)       # no cycle with the engine: both go when the last user lets go
         sizes, b = [], 1
         while b < engine.config.max_batch_size:
             sizes.append(b)
@@ -28,6 +30,10 @@ class DecodeGraphs:
         self._graphs: Dict[int, tuple] = {}
         self.replays = 0
         self.pool = None
+
+    @property
+    def engine(self):
+        return self._engine()
 
     def _bucket(self, rows: int) -> int:
         for s in self.sizes:
@@ -53,8 +59,17 @@ class DecodeGraphs:
         graph = torch.cuda.CUDAGraph()
         before = eng.kernels.launches
         batch.extras.clear()
-        with torch.cuda.graph(graph, pool=self.pool):
-            logits = eng.model.forward(batch, eng.cache)
+        # No garbage collection while the stream is capturing: an object that happens to be collected then
+        # (an engine used before, with its pinned buffers, events and graphs) would make CUDA calls that
+        # are not allowed during a capture and invalidate it.
+        gc_was_on = gc.isenabled()
+        gc.disable()                  # (torch.cuda.graph collects once on entry, before the capture begins)
+        try:
+            with torch.cuda.graph(graph, pool=self.pool):
+                logits = eng.model.forward(batch, eng.cache)
+        finally:
+            if gc_was_on:
+                gc.enable()
         if self.pool is None:
             self.pool = graph.pool()
         kernels_in_graph = eng.kernels.launches - before

@@ -267,6 +267,7 @@ class Engine:
             self.cache.release(rid)
         for g in self.cache.groups:
             g.storage = None
+        self.graphs = None
 
 
 def build_engine(model_folder: str = None, engine_config: EngineConfig = None, *, config_dict: dict = None,
