@@ -3,15 +3,17 @@
 // one elected thread issues tcgen05.mma on shared-memory descriptors, the float32 accumulator
 // lives in tensor memory (TMEM) and comes back to registers with tcgen05.ld for the epilogue.
 //
-// One block computes one 128 x 128 tile of C. Six warps:
+// Persistent: one block per SM walks over tiles of 128 rows x 256 accumulator columns. Six warps:
 //   warp 0      producer: waits for a free stage, arms its mbarrier with the bytes to come, issues the TMA loads
-//   warp 1      allocates TMEM; one thread issues the MMAs of each stage (four k-steps of 16) and commits
-//               them to the stage's "empty" barrier; after the last stage it commits to the "accumulator full" barrier
+//   warp 1      allocates TMEM (two accumulators of 256 columns); one thread issues the MMAs of each stage
+//               (four k-steps of 16, N = 256) and commits them to the stage's "empty" barrier; after a tile's
+//               last stage it commits to that accumulator's "full" barrier and goes on with the other one
 //   warps 2-5   epilogue: each reads its quarter of the TMEM lanes (a warp may only touch lanes
-//               32 * (warp % 4) ..), converts and stores rows of C
-// SWIGLU: W holds `up_offset` gate rows followed by as many up rows; the block loads both row
-// tiles, keeps two accumulators and writes silu(gate) * up, so the product's intermediate never
-// goes to memory.
+//               32 * (warp % 4) ..), converts and stores rows of C, then releases the accumulator;
+//               it runs under the products of the next tile
+// SWIGLU: W holds `up_offset` gate rows followed by as many up rows; a stage holds 128 gate rows and
+// their 128 up rows as one 256-row operand, and the epilogue writes silu(gate) * up, so the product's
+// intermediate never goes to memory.
 //
 // No load uses cluster multicast. Every wait on an mbarrier is bounded: after WAIT_LIMIT polls
 // the waiting role records an error code in *error_flag and stops; the block then frees its TMEM
@@ -22,7 +24,6 @@
 #include "common.cuh"
 
 #define TC_BM 128
-#define TC_BN 128
 #define TC_BK 64
 #define TC_THREADS 192
 #define TC_WAIT_LIMIT (1u << 20)
@@ -95,38 +96,64 @@ __device__ __forceinline__ uint64_t tc_smem_desc(uint32_t addr) {
     return d;
 }
 
-template <bool SWIGLU, int STAGES_> struct TcConfig {
-    static constexpr int STAGES = STAGES_;
-    static constexpr int A_BYTES = TC_BM * TC_BK * 2;
-    static constexpr int B_BYTES = TC_BN * TC_BK * 2;
-    static constexpr int STAGE_BYTES = A_BYTES + (SWIGLU ? 2 : 1) * B_BYTES;
-    static constexpr int TMEM_COLS = SWIGLU ? 2 * TC_BN : TC_BN;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
+// 16 bytes of output from consecutive float values.
+template <typename TO> __device__ __forceinline__ uint4 pack_chunk(const float* v);
+template <> __device__ __forceinline__ uint4 pack_chunk<float>(const float* v) {
+    return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+}
+template <> __device__ __forceinline__ uint4 pack_chunk<__nv_bfloat16>(const float* v) {
+    uint4 r;
+    __nv_bfloat162 p;
+    p = __floats2bfloat162_rn(v[0], v[1]); r.x = *reinterpret_cast<uint32_t*>(&p);
+    p = __floats2bfloat162_rn(v[2], v[3]); r.y = *reinterpret_cast<uint32_t*>(&p);
+    p = __floats2bfloat162_rn(v[4], v[5]); r.z = *reinterpret_cast<uint32_t*>(&p);
+    p = __floats2bfloat162_rn(v[6], v[7]); r.w = *reinterpret_cast<uint32_t*>(&p);
+    return r;
+}
+
+// Geometry of one block: it walks over output tiles of 128 rows x TC_BN_ACC accumulator columns.
+// Plain product: 256 columns of C. SWIGLU: 128 gate columns and their 128 up columns (the two W row
+// tiles lie back to back in the stage and form one 256-row operand), giving 128 columns of output.
+struct TcCfg {
+    static constexpr int STAGES = 4;
+    static constexpr int ACC_COLS = 256;                       // accumulator columns per tile = MMA N
+    static constexpr int A_BYTES = TC_BM * TC_BK * 2;          // 16 KB
+    static constexpr int B_BYTES = ACC_COLS * TC_BK * 2;       // 32 KB
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * ACC_COLS;             // two accumulators: the epilogue of a tile runs under the next tile's products
+    static constexpr int STAGING_BYTES = 4 * 32 * 128;         // the epilogue's transposition buffers: 32 rows x 128 bytes per warp
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
 };
 
-template <bool SWIGLU, int STAGES_, typename TO>
+template <bool SWIGLU, typename TO>
 __global__ void __launch_bounds__(TC_THREADS)
 gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
-                    TO* __restrict__ out, int M, int N, int K, int ldc, int up_offset, int* __restrict__ error_flag) {
-    using Cfg = TcConfig<SWIGLU, STAGES_>;
+                    TO* __restrict__ out, int M, int N, int K, int ldc, int up_offset, int m_tiles, int n_tiles,
+                    int* __restrict__ error_flag) {
+    using Cfg = TcCfg;
+    constexpr int OUT_COLS = SWIGLU ? Cfg::ACC_COLS / 2 : Cfg::ACC_COLS;      // columns of C per tile
     extern __shared__ unsigned char tc_raw[];
-    // tiles need 1,024-byte alignment for the 128-byte swizzle
     unsigned char* tiles = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + Cfg::STAGES * Cfg::STAGE_BYTES);
-    // bars[0 .. STAGES): full; bars[STAGES .. 2 STAGES): empty; bars[2 STAGES]: accumulator full
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * Cfg::STAGES + 1);
+    unsigned char* staging = tiles + Cfg::STAGES * Cfg::STAGE_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + Cfg::STAGING_BYTES);
+    // bars: full[STAGES], empty[STAGES], acc_full[2], acc_empty[2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * Cfg::STAGES + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * TC_BN;
     const int k_blocks = (K + TC_BK - 1) / TC_BK;
-    const uint32_t full0 = tc_smem(bars), empty0 = tc_smem(bars + Cfg::STAGES), acc_full = tc_smem(bars + 2 * Cfg::STAGES);
+    const int num_tiles = m_tiles * n_tiles;
+    const uint32_t full0 = tc_smem(bars), empty0 = tc_smem(bars + Cfg::STAGES);
+    const uint32_t acc_full0 = tc_smem(bars + 2 * Cfg::STAGES), acc_empty0 = tc_smem(bars + 2 * Cfg::STAGES + 2);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::STAGES; ++s) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, 1);
         }
-        mbar_init(acc_full, 1);
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(acc_full0 + 8 * a, 1);
+            mbar_init(acc_empty0 + 8 * a, 4);          // one arrival per epilogue warp
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -141,94 +168,138 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     const uint32_t tmem_base = *tmem_slot;
     pdl_wait();                       // A is the output of the kernel before this one
 
+    // Tiles go round the blocks; consecutive tiles share the W column block (m runs fastest), so the
+    // blocks that run side by side read the same weights from L2.
     if (warp == 0) {
         if (lane == 0) {
-            for (int kb = 0; kb < k_blocks; ++kb) {
-                const int s = kb % Cfg::STAGES;
-                const uint32_t round = kb / Cfg::STAGES;
-                if (round > 0 && !mbar_wait(empty0 + 8 * s, (round - 1) & 1)) {
-                    atomicExch(error_flag, TC_ERR_PRODUCER);
-                    break;
+            uint32_t it = 0;                      // k-blocks loaded so far, over all tiles
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                const int m0 = (tile % m_tiles) * TC_BM, n0 = (tile / m_tiles) * OUT_COLS;
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % Cfg::STAGES;
+                    const uint32_t round = it / Cfg::STAGES;
+                    if (round > 0 && !mbar_wait(empty0 + 8 * s, (round - 1) & 1)) {
+                        atomicExch(error_flag, TC_ERR_PRODUCER);
+                        tile = num_tiles;
+                        break;
+                    }
+                    const uint32_t bar = full0 + 8 * s;
+                    mbar_expect_tx(bar, Cfg::STAGE_BYTES);
+                    unsigned char* stage = tiles + s * Cfg::STAGE_BYTES;
+                    tma_load_2d(tc_smem(stage), &map_a, kb * TC_BK, m0, bar);
+                    if (SWIGLU) {
+                        tma_load_2d(tc_smem(stage + Cfg::A_BYTES), &map_w, kb * TC_BK, n0, bar);
+                        tma_load_2d(tc_smem(stage + Cfg::A_BYTES + Cfg::B_BYTES / 2), &map_w, kb * TC_BK, up_offset + n0, bar);
+                    } else {
+                        tma_load_2d(tc_smem(stage + Cfg::A_BYTES), &map_w, kb * TC_BK, n0, bar);
+                    }
                 }
-                const uint32_t bar = full0 + 8 * s;
-                mbar_expect_tx(bar, Cfg::STAGE_BYTES);
-                unsigned char* stage = tiles + s * Cfg::STAGE_BYTES;
-                tma_load_2d(tc_smem(stage), &map_a, kb * TC_BK, m0, bar);
-                tma_load_2d(tc_smem(stage + Cfg::A_BYTES), &map_w, kb * TC_BK, n0, bar);
-                if (SWIGLU) tma_load_2d(tc_smem(stage + Cfg::A_BYTES + Cfg::B_BYTES), &map_w, kb * TC_BK, up_offset + n0, bar);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // instruction descriptor: float32 accumulator, bfloat16 operands, both K-major, M = 128, N = 128;
-            // with SWIGLU the gate and up tiles lie back to back in the stage and form one operand of
-            // 256 rows: one instruction with N = 256 fills both accumulators (columns 0-127 and 128-255)
-            constexpr uint32_t mma_n = SWIGLU ? 2 * TC_BN : TC_BN;
-            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((mma_n >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
-            bool ok = true;
-            for (int kb = 0; kb < k_blocks && ok; ++kb) {
-                const int s = kb % Cfg::STAGES;
-                if (!mbar_wait(full0 + 8 * s, (kb / Cfg::STAGES) & 1)) {
+            // instruction descriptor: float32 accumulator, bfloat16 operands, both K-major, M = 128, N = 256
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(Cfg::ACC_COLS >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+            uint32_t it = 0;
+            int local = 0;                        // tiles this block has started
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+                const int acc = local & 1;
+                if (local >= 2 && !mbar_wait(acc_empty0 + 8 * acc, ((local >> 1) - 1) & 1)) {
                     atomicExch(error_flag, TC_ERR_MMA);
-                    ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a_addr = tc_smem(tiles + s * Cfg::STAGE_BYTES);
-                const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+                bool ok = true;
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % Cfg::STAGES;
+                    if (!mbar_wait(full0 + 8 * s, (it / Cfg::STAGES) & 1)) {
+                        atomicExch(error_flag, TC_ERR_MMA);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = tc_smem(tiles + s * Cfg::STAGE_BYTES);
+                    const uint32_t b_addr = a_addr + Cfg::A_BYTES;
 #pragma unroll
-                for (int k = 0; k < TC_BK / 16; ++k) {
-                    const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-                    tc_mma(tmem_base, tc_smem_desc(a_addr + k * 32), tc_smem_desc(b_addr + k * 32), idesc, acc);
+                    for (int k = 0; k < TC_BK / 16; ++k)
+                        tc_mma(tmem_base + acc * Cfg::ACC_COLS, tc_smem_desc(a_addr + k * 32), tc_smem_desc(b_addr + k * 32),
+                               idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    tc_commit(empty0 + 8 * s);         // the stage is free once these MMAs have read it
                 }
-                tc_commit(empty0 + 8 * s);         // the stage is free once these MMAs have read it
+                if (!ok) break;
+                tc_commit(acc_full0 + 8 * acc);
             }
-            if (ok) tc_commit(acc_full);
         }
     } else {
-        // epilogue: TMEM lane quarter of this warp
-        pdl_launch_dependents();
+        // epilogue: TMEM lane quarter of this warp. A thread holds one row of the accumulator, so
+        // storing from registers would write 16 bytes to each of 32 rows per instruction. Instead the
+        // warp passes 32 rows x 128 bytes through shared memory (16-byte chunks swizzled by row, free
+        // of bank conflicts both ways) and stores whole 128-byte lines, four rows per instruction.
         const int quarter = warp & 3;
-        const int row = m0 + quarter * 32 + lane;
-        if (!mbar_wait(acc_full, 0)) {
-            if (lane == 0) atomicExch(error_flag, TC_ERR_EPILOGUE);
-        } else {
+        constexpr int CHUNK_ELEMS = 16 / (int)sizeof(TO);            // elements in 16 bytes
+        constexpr int LINE_COLS = 8 * CHUNK_ELEMS;                   // columns in 128 bytes of output
+        const bool vec = (ldc % CHUNK_ELEMS == 0) && (N % CHUNK_ELEMS == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+        uint4* stage_rows = reinterpret_cast<uint4*>(staging + quarter * 4096);
+        int local = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const int m0 = (tile % m_tiles) * TC_BM, n0 = (tile / m_tiles) * OUT_COLS;
+            const int row0 = m0 + quarter * 32;
+            if (tile + (int)gridDim.x >= num_tiles) pdl_launch_dependents();      // this block's last tile
+            if (!mbar_wait(acc_full0 + 8 * acc, (local >> 1) & 1)) {
+                if (lane == 0) atomicExch(error_flag, TC_ERR_EPILOGUE);
+                break;
+            }
             tc_fence_after();
-            const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
-            const bool vec = (ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+            const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * Cfg::ACC_COLS;
 #pragma unroll 1
-            for (int c0 = 0; c0 < TC_BN; c0 += 32) {
-                uint32_t acc[32];
-                tc_load32(lane_addr + c0, acc);
-                float v[32];
-                if (SWIGLU) {
-                    uint32_t up[32];
-                    tc_load32(lane_addr + TC_BN + c0, up);
+            for (int c0 = 0; c0 < OUT_COLS; c0 += LINE_COLS) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float g = __uint_as_float(acc[j]);
-                        v[j] = g / (1.f + __expf(-g)) * __uint_as_float(up[j]);
-                    }
-                } else {
+                for (int h = 0; h < LINE_COLS / 32; ++h) {
+                    uint32_t accv[32];
+                    tc_load32(lane_addr + c0 + h * 32, accv);
+                    float v[32];
+                    if (SWIGLU) {
+                        uint32_t up[32];
+                        tc_load32(lane_addr + OUT_COLS + c0 + h * 32, up);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]);
-                }
-                if (row < M) {
-                    TO* dst = out + (size_t)row * ldc + n0 + c0;
-                    if (vec && n0 + c0 + 32 <= N) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 8) {
-                            float part[8];
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) part[e] = v[j + e];
-                            store8(dst + j, part);
+                        for (int j = 0; j < 32; ++j) {
+                            const float g = __uint_as_float(accv[j]);
+                            v[j] = __fdividef(g, 1.f + __expf(-g)) * __uint_as_float(up[j]);
                         }
                     } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(accv[j]);
+                    }
+                    if (vec) {
+#pragma unroll
+                        for (int q = 0; q < 32 / CHUNK_ELEMS; ++q) {
+                            const int chunk = h * (32 / CHUNK_ELEMS) + q;
+                            stage_rows[lane * 8 + (chunk ^ (lane & 7))] = pack_chunk<TO>(v + q * CHUNK_ELEMS);
+                        }
+                    } else if (row0 + lane < M) {
+                        TO* dst = out + (size_t)(row0 + lane) * ldc + n0 + c0 + h * 32;
                         for (int j = 0; j < 32; ++j)
-                            if (n0 + c0 + j < N) dst[j] = from_float<TO>(v[j]);
+                            if (n0 + c0 + h * 32 + j < N) dst[j] = from_float<TO>(v[j]);
                     }
                 }
+                if (vec) {
+                    __syncwarp();
+                    const int chunk = lane & 7, col = n0 + c0 + chunk * CHUNK_ELEMS;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int r = i * 4 + (lane >> 3);
+                        const uint4 value = stage_rows[r * 8 + (chunk ^ (r & 7))];
+                        if (row0 + r < M && col < N)
+                            *reinterpret_cast<uint4*>(out + (size_t)(row0 + r) * ldc + col) = value;
+                    }
+                    __syncwarp();
+                }
             }
+            // the accumulator has been read: the products of the tile after next may overwrite it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acc_empty0 + 8 * acc) : "memory");
         }
         tc_fence_before();
     }
@@ -271,37 +342,33 @@ static bool tc_make_map(CUtensorMap* map, const void* base, int rows, int cols, 
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool SWIGLU, int STAGES_, typename TO>
-static int tc_launch_stages(const CUtensorMap& map_a, const CUtensorMap& map_w, void* C, int M, int N, int K, int ldc,
-                     int up_offset, int* error_flag, cudaStream_t stream) {
-    auto kernel = gemm_tcgen05_kernel<SWIGLU, STAGES_, TO>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TcConfig<SWIGLU, STAGES_>::SMEM_BYTES);
-        if (e != cudaSuccess) return (int)e;
-        configured = true;
+static int tc_sm_count() {
+    static int count = 0;
+    if (count == 0) {
+        int device = 0;
+        cudaGetDevice(&device);
+        cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
+        if (count <= 0) count = 1;
     }
-    dim3 grid((N + TC_BN - 1) / TC_BN, (M + TC_BM - 1) / TC_BM);
-    ttb_launch(kernel, grid, dim3(TC_THREADS), (size_t)TcConfig<SWIGLU, STAGES_>::SMEM_BYTES, stream, map_a, map_w, (TO*)C, M, N, K,
-               ldc, up_offset, error_flag);
-    return ttb_launch_status();
-}
-
-static int tc_stage_choice() {          // TTB200_TC_STAGES=few|many, for experiments; default: few (two blocks per SM)
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("TTB200_TC_STAGES");
-        v = (e && e[0] == 'm') ? 1 : 0;
-    }
-    return v;
+    return count;
 }
 
 template <bool SWIGLU, typename TO>
 static int tc_launch(const CUtensorMap& map_a, const CUtensorMap& map_w, void* C, int M, int N, int K, int ldc,
                      int up_offset, int* error_flag, cudaStream_t stream) {
-    if (tc_stage_choice())
-        return tc_launch_stages<SWIGLU, SWIGLU ? 4 : 6, TO>(map_a, map_w, C, M, N, K, ldc, up_offset, error_flag, stream);
-    return tc_launch_stages<SWIGLU, SWIGLU ? 2 : 3, TO>(map_a, map_w, C, M, N, K, ldc, up_offset, error_flag, stream);
+    auto kernel = gemm_tcgen05_kernel<SWIGLU, TO>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg::SMEM_BYTES);
+        if (e != cudaSuccess) return (int)e;
+        configured = true;
+    }
+    constexpr int out_cols = SWIGLU ? TcCfg::ACC_COLS / 2 : TcCfg::ACC_COLS;
+    const int m_tiles = (M + TC_BM - 1) / TC_BM, n_tiles = (N + out_cols - 1) / out_cols;
+    const int blocks = m_tiles * n_tiles < tc_sm_count() ? m_tiles * n_tiles : tc_sm_count();
+    ttb_launch(kernel, dim3(blocks), dim3(TC_THREADS), (size_t)TcCfg::SMEM_BYTES, stream, map_a, map_w, (TO*)C, M, N, K,
+               ldc, up_offset, m_tiles, n_tiles, error_flag);
+    return ttb_launch_status();
 }
 
 // A [M, K], W [N, K] (or [2 * swiglu_rows, K] with swiglu_rows = N gate rows then N up rows), bfloat16, K-contiguous.
@@ -315,7 +382,7 @@ TTB_EXPORT int ttb_gemm_tcgen05(const void* A, const void* W, void* C, int out_d
     if (swiglu_rows != 0 && swiglu_rows != N) return TTB_ERR_ARGUMENT;
     CUtensorMap map_a, map_w;
     if (!tc_make_map(&map_a, A, M, K, lda, TC_BM)) return TTB_ERR_UNSUPPORTED;
-    if (!tc_make_map(&map_w, W, swiglu_rows ? 2 * N : N, K, ldw, TC_BN)) return TTB_ERR_UNSUPPORTED;
+    if (!tc_make_map(&map_w, W, swiglu_rows ? 2 * N : N, K, ldw, swiglu_rows ? TcCfg::ACC_COLS / 2 : TcCfg::ACC_COLS)) return TTB_ERR_UNSUPPORTED;
     const bool f32 = out_dtype == TTB_DTYPE_F32;
     if (!f32 && out_dtype != TTB_DTYPE_BF16) return TTB_ERR_UNSUPPORTED;
     if (swiglu_rows)

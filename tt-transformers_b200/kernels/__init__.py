@@ -55,6 +55,7 @@ class CudaKernels:
     # activations' traffic through L1 holds it back and the library's product is faster (measured:
     # 13 us against 20 to 42 us for the down projection at 32 to 64 rows).
     TENSOR_SKINNY_ROWS = 16
+    TCGEN05_SWIGLU_ROWS = 128
 
     def __init__(self, device: torch.device):
         if not torch.cuda.is_available():
@@ -87,11 +88,13 @@ class CudaKernels:
         self.use_mma_attention = True
         # prompt portions at head size 64: the TMA + tcgen05 attention kernel (False: the mma.sync one)
         self.use_tcgen05_attention = os.environ.get("TTB200_TCGEN05_ATTENTION", "1") == "1"
-        # bfloat16 products with more rows than the skinny kernel takes go to the library's product, or,
-        # with this switch (or TTB200_TCGEN05=1 in the environment), to the TMA + tcgen05 kernel of
-        # gemm_tcgen05.cu, which is correct at every size but, with its one-tile-per-block schedule,
-        # reaches 0.6 to 0.8 of the library's throughput at prefill sizes.
-        self.use_tcgen05 = os.environ.get("TTB200_TCGEN05", "0") == "1"
+        # bfloat16 products with more rows than the skinny kernel takes: the TMA + tcgen05 kernel of
+        # gemm_tcgen05.cu or the library's product. None (TTB200_TCGEN05 unset or "auto"): the feed-forward's
+        # gate/up product with its fused SwiGLU goes to the tcgen05 kernel from TCGEN05_SWIGLU_ROWS rows on
+        # (measured 1.1 to 1.35 times faster than the library's product followed by the SwiGLU kernel) and
+        # plain products go to the library (the tcgen05 kernel reaches 0.75 to 0.95 of it). True ("1"):
+        # every such product goes to the tcgen05 kernel. False ("0"): none does.
+        self.use_tcgen05 = {"1": True, "0": False}.get(os.environ.get("TTB200_TCGEN05", "auto"))
         with torch.cuda.device(self.device):
             self.tc_error = torch.zeros(1, dtype=torch.int32, device=self.device)
 
@@ -217,7 +220,8 @@ class CudaKernels:
                                               inter, K, x.stride(0), w_gate_up.stride(0), inter, inter,
                                               self._stream()), "gemv_mma_swiglu")
             return out
-        if (x.dtype == torch.bfloat16 and self.use_tcgen05 and K % 8 == 0 and x.stride(0) % 8 == 0
+        fused = self.use_tcgen05 if self.use_tcgen05 is not None else M >= self.TCGEN05_SWIGLU_ROWS
+        if (x.dtype == torch.bfloat16 and fused and K % 8 == 0 and x.stride(0) % 8 == 0
                 and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1 and w_gate_up.stride(1) == 1):
             out = torch.empty(M, inter, dtype=x.dtype, device=self.device)
             self._check(self.lib.ttb_gemm_tcgen05(self._p(x), self._p(w_gate_up), self._p(out), _dtype_code(x.dtype), M,
