@@ -225,6 +225,59 @@ def test_attention_finds_a_far_key(kernels):
                 close(got.view(heads, head_dim)[h], want, dtype)
 
 
+DECODE_CASES = [
+    # heads, kv_heads, head_dim, page_size, segments (cached before, new tokens), window
+    (32, 8, 64, 16, [(8191, 1), (0, 1), (63, 1), (64, 1), (65, 1), (4095, 1)], None),
+    (8, 8, 64, 8, [(100, 1), (7, 1), (8, 2), (511, 5), (1024, 8)], None),          # one head per group, up to 8 tokens
+    (6, 2, 64, 32, [(1000, 1), (31, 2), (32, 1)], None),                           # three heads per group
+    (10, 2, 64, 64, [(700, 1), (63, 3)], None),                                    # five per group: 16-row tiles
+    (16, 1, 64, 128, [(1500, 1), (127, 1), (128, 1)], None),                       # sixteen per group, pages beyond a tile
+    (8, 2, 128, 16, [(3000, 1), (15, 1), (16, 1), (200, 2)], None),
+    (24, 2, 128, 8, [(900, 1), (64, 1)], None),                                    # twelve per group at head size 128
+    (8, 2, 64, 16, [(500, 1), (99, 1), (100, 1), (101, 2), (10, 1)], 100),         # windows
+    (4, 1, 128, 32, [(2000, 1), (300, 3)], 257),
+    (8, 4, 64, 256, [(1000, 1), (255, 1), (256, 1)], 300),
+]
+
+
+@pytest.mark.parametrize("case", DECODE_CASES)
+@pytest.mark.parametrize("tma", [True, False])
+def test_decode_attention(kernels, twin, case, tma):
+    """Both decode kernels (TMA loads with transposed products; the mma.sync kernel's decode shape) against
+    the plain reference, with one split and with several. Every cache slot that no query may see (slots
+    past a segment's end, keys a window has passed, pages of nobody) holds NaN: none may reach the output."""
+    heads, kv_heads, head_dim, page_size, segments, window = case
+    dtype = torch.bfloat16
+    qkv, batch, view = make_paged_case(dtype, heads, kv_heads, head_dim, page_size, segments, window, seed=3)
+    visible = torch.zeros(view.keys.shape[0], page_size, dtype=torch.bool)
+    for r, (p, n) in enumerate(segments):
+        low = max(0, p - window + 1) if window else 0
+        for key in range(low, p + n):
+            visible[int(view.block_table[r, key // page_size]), key % page_size] = True
+    ref = twin.paged_attention(qkv.float(), batch, heads, kv_heads, head_dim, 0.3,
+                               SimpleNamespace(keys=view.keys.float(), values=view.values.float(),
+                                               block_table=view.block_table, page_size=page_size, window=window))
+    hidden = (~visible).cuda()[:, None, :, None].expand_as(view.keys)
+    view.keys[hidden] = float("nan")
+    view.values[hidden] = float("nan")
+    before = kernels.use_tma_decode
+    kernels.use_tma_decode = tma
+    try:
+        for splits in (None, 1, 3):
+            batch.extras.clear()
+            if splits is not None:
+                plan = kernels._attention_plan(batch, heads // kv_heads, kv_heads, head_dim)
+                assert plan[0], "the case is meant for the decode kernels"
+                key = ("attention_plan", heads // kv_heads, kv_heads, head_dim, False)
+                batch.extras[key] = plan[:4] + (splits,)
+            got = kernels.paged_attention(qkv, batch, heads, kv_heads, head_dim, 0.3, view)
+            assert not torch.isnan(got.float()).any()
+            close(got, ref, dtype)
+        kernels.check_status()
+    finally:
+        kernels.use_tma_decode = before
+
+
 @pytest.mark.parametrize("vocab,rows", [(384, 5), (128256, 3), (1000, 64), (33, 2)])
 def test_sample(kernels, twin, vocab, rows):
     g = torch.Generator(device="cuda").manual_seed(4)

@@ -88,6 +88,9 @@ class CudaKernels:
         self.use_mma_attention = True
         # prompt portions at head size 64: the TMA + tcgen05 attention kernel (False: the mma.sync one)
         self.use_tcgen05_attention = os.environ.get("TTB200_TCGEN05_ATTENTION", "1") == "1"
+        # decode steps (up to 16 query rows per segment and KV head): the transposed-product kernel with TMA
+        # loads of attention_decode.cu (False: the decode shape of the mma.sync kernel)
+        self.use_tma_decode = os.environ.get("TTB200_TMA_DECODE", "1") == "1"
         # bfloat16 products with more rows than the skinny kernel takes: the TMA + tcgen05 kernel of
         # gemm_tcgen05.cu or the library's product. None (TTB200_TCGEN05 unset or "auto"): the feed-forward's
         # gate/up product with its fused SwiGLU goes to the tcgen05 kernel from TCGEN05_SWIGLU_ROWS rows on
@@ -121,7 +124,8 @@ class CudaKernels:
             role = {1: "the product's TMA producer", 2: "the product's MMA issuer", 3: "the product's epilogue",
                     11: "attention's TMA producer", 12: "attention's MMA issuer waiting for the queries",
                     13: "attention's MMA issuer waiting for keys", 14: "attention's MMA issuer waiting for P",
-                    15: "attention's softmax warps", 16: "attention's epilogue"}.get(tc, f"role {tc}")
+                    15: "attention's softmax warps", 16: "attention's epilogue",
+                    21: "decode attention's TMA producer", 22: "decode attention's consumer warps"}.get(tc, f"role {tc}")
             raise EngineDeviceError(f"a tcgen05 kernel gave up waiting on a barrier ({role}); its result is invalid")
         value = int(self.status.item())
         if value != 0:
@@ -343,6 +347,20 @@ class CudaKernels:
         if splits > 1:
             partial_o = torch.empty(tokens * heads * splits * head_dim, dtype=torch.float32, device=self.device)
             partial_ml = torch.empty(tokens * heads * splits * 2, dtype=torch.float32, device=self.device)
+        max_rows = batch.max_seg_len * (heads // kv_heads)
+        if (decode_shape and self.use_tma_decode and view.keys.is_contiguous() and view.values.is_contiguous()
+                and self.lib.ttb_attention_decode_supports(heads, kv_heads, head_dim, view.page_size, max_rows)):
+            self._check(self.lib.ttb_paged_attention_decode(
+                self._p(qkv), qkv.stride(0), self._p(out), self._p(batch.cu_seqlens), self._p(batch.seg_pos0),
+                self._p(view.keys), self._p(view.values), self._p(view.block_table), view.block_table.shape[1],
+                view.page_size, batch.num_segments, max_rows, heads, kv_heads, head_dim, ctypes.c_float(scale),
+                int(view.window or 0), splits, self._p(partial_o), self._p(partial_ml), view.keys.shape[0],
+                self._p(self.status), self._p(self.tc_error), self._stream()), "paged_attention_decode")
+            if splits > 1:
+                self._check(self.lib.ttb_attention_merge(self._p(partial_o), self._p(partial_ml), self._p(out),
+                                                         tokens * heads, splits, head_dim, self._stream()),
+                            "attention_merge")
+            return
         self._check(self.lib.ttb_paged_attention_mma_checked(
             self._p(qkv), qkv.stride(0), self._p(out), self._p(batch.cu_seqlens), self._p(batch.seg_pos0),
             self._p(view.keys), self._p(view.values), self._p(view.block_table), view.block_table.shape[1],
