@@ -278,6 +278,35 @@ def test_decode_attention(kernels, twin, case, tma):
         kernels.use_tma_decode = before
 
 
+@pytest.mark.parametrize("case", [
+    (8, 2, 64, 16, [(0, 200), (70, 33), (500, 40)], None),          # the TMA + tcgen05 kernel's geometry
+    (32, 8, 64, 16, [(0, 300), (1000, 37)], None),
+    (8, 2, 64, 16, [(0, 150), (90, 20)], 100),                      # a window: the mma.sync kernel
+    (3, 1, 128, 16, [(0, 100), (129, 40)], None),
+    (6, 3, 80, 8, [(9, 30)], 16),                                   # the kernel for any size
+])
+def test_prompt_attention_ignores_slots_that_hold_nothing(kernels, twin, case):
+    """Prompt portions: cache slots past a segment's end or below its window, and pages of nobody, hold NaN."""
+    heads, kv_heads, head_dim, page_size, segments, window = case
+    dtype = torch.bfloat16
+    qkv, batch, view = make_paged_case(dtype, heads, kv_heads, head_dim, page_size, segments, window, seed=8)
+    visible = torch.zeros(view.keys.shape[0], page_size, dtype=torch.bool)
+    for r, (p, n) in enumerate(segments):
+        low = max(0, p - window + 1) if window else 0
+        for key in range(low, p + n):
+            visible[int(view.block_table[r, key // page_size]), key % page_size] = True
+    ref = twin.paged_attention(qkv.float(), batch, heads, kv_heads, head_dim, 0.3,
+                               SimpleNamespace(keys=view.keys.float(), values=view.values.float(),
+                                               block_table=view.block_table, page_size=page_size, window=window))
+    hidden = (~visible).cuda()[:, None, :, None].expand_as(view.keys)
+    view.keys[hidden] = float("nan")
+    view.values[hidden] = float("nan")
+    got = kernels.paged_attention(qkv, batch, heads, kv_heads, head_dim, 0.3, view)
+    assert not torch.isnan(got.float()).any()
+    close(got, ref, dtype)
+    kernels.check_status()
+
+
 @pytest.mark.parametrize("vocab,rows", [(384, 5), (128256, 3), (1000, 64), (33, 2)])
 def test_sample(kernels, twin, vocab, rows):
     g = torch.Generator(device="cuda").manual_seed(4)
@@ -404,6 +433,114 @@ def test_fused_qkv_projection_rotation_and_cache_write(kernels, twin, heads, kv_
     q = kernels.fused_qkv_rope(x, w, batch, inv_freq, head_dim, heads, kv_heads, head_dim, view, True)
     assert q is not None and q.shape == (M, heads * head_dim)
     qkv = (x.float() @ w.float().t())                     # float32 product, then the twin's rotation and write
+    twin.rope_kv_write(qkv, batch, inv_freq, head_dim, heads, kv_heads, head_dim, view2, True)
+    close(q, qkv[:, :heads * head_dim], torch.bfloat16)
+    close(view.keys, view2.keys, torch.bfloat16)
+    close(view.values, view2.values, torch.bfloat16)
+    kernels.check_status()
+
+
+@pytest.fixture
+def fusing(kernels):
+    """The kernel table with the norm and residual fusions of the skinny products switched on."""
+    before = kernels.fuse_norm, kernels.fuse_add
+    kernels.fuse_norm = kernels.fuse_add = True
+    yield kernels
+    kernels.fuse_norm, kernels.fuse_add = before
+
+
+def _deferred(residual, weight, eps):
+    from tt_transformers_b200.parts.base import DeferredNorm
+
+    def never():
+        raise AssertionError("the norm was meant to be fused into the product")
+
+    return DeferredNorm(residual, weight.float().contiguous(), eps, never)
+
+
+def _rms(residual, weight, eps):
+    r = residual.double()
+    return r * torch.rsqrt((r * r).mean(-1, keepdim=True) + eps) * weight.double()
+
+
+@pytest.mark.parametrize("M,N,K,eps", [(1, 384, 96, 1e-5), (8, 3072, 2048, 1e-5), (5, 77, 72, 1e-6), (16, 2048, 2048, 1e-5),
+                                       (12, 128256, 256, 1e-3), (8, 2048, 8192, 1e-5), (3, 100, 4096, 1e-5)])
+def test_skinny_product_takes_the_norm_before_it_and_the_residual_add_after_it(fusing, twin, M, N, K, eps):
+    kernels = fusing
+    """A deferred RMS norm as the product's input (plain, SwiGLU pair, both output types), and the float32
+    residual stream as its output, against the steps one by one in float64."""
+    from tt_transformers_b200.parts.base import ADDED
+
+    g = torch.Generator(device="cuda").manual_seed(31)
+    residual = torch.randn(M, K, device="cuda", generator=g) * 3.0
+    weight = 1.0 + 0.3 * torch.randn(K, device="cuda", generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    assert kernels.defers_norm(residual, torch.bfloat16)
+    kept = residual.clone()
+    normed = _rms(residual, weight, eps)
+    for out_dtype in (torch.bfloat16, torch.float32):
+        got = kernels.linear(_deferred(residual, weight, eps), w, out_dtype=out_dtype)
+        assert got.dtype == out_dtype
+        close(got, normed @ w.double().t(), torch.bfloat16)
+    if N % 2 == 0:
+        got = kernels.linear_swiglu(_deferred(residual, weight, eps), w)
+        close(got, twin.linear_swiglu(normed, w.double()), torch.bfloat16)
+    assert torch.equal(residual, kept), "a deferred norm leaves the residual stream as it is"
+    # the product added to the stream
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    stream = torch.randn(M, N, device="cuda", generator=g)
+    want = stream.double() + x.double() @ w.double().t()
+    assert kernels.linear(x, w, accumulate=stream) is ADDED
+    close(stream, want, torch.bfloat16)
+    # both at once
+    stream = torch.randn(M, N, device="cuda", generator=g)
+    want = stream.double() + normed @ w.double().t()
+    assert kernels.linear(_deferred(residual, weight, eps), w, accumulate=stream) is ADDED
+    close(stream, want, torch.bfloat16)
+
+
+def test_products_that_cannot_fuse_fall_back_to_the_steps_one_by_one(fusing):
+    kernels = fusing
+    """More rows than the skinny kernel takes, or float32: the deferred norm is materialised and the
+    product comes back for the caller to add."""
+    from tt_transformers_b200.parts.base import DeferredNorm
+
+    g = torch.Generator(device="cuda").manual_seed(32)
+    for dtype, M in ((torch.bfloat16, 40), (torch.float32, 4)):
+        residual = torch.randn(M, 96, device="cuda", generator=g)
+        weight = (1.0 + 0.1 * torch.randn(96, device="cuda", generator=g)).to(dtype)
+        w = (torch.randn(64, 96, device="cuda", generator=g) / 10).to(dtype)
+        calls = []
+
+        def materialize():
+            calls.append(1)
+            return kernels.add_rmsnorm(residual, None, weight, 1e-5, dtype)
+
+        d = DeferredNorm(residual, weight.float(), 1e-5, materialize)
+        got = kernels.linear(d, w)
+        assert calls == [1]
+        close(got, _rms(residual, weight, 1e-5) @ w.double().t(), dtype)
+        stream = torch.zeros(M, 64, device="cuda")
+        out = kernels.linear(got.new_zeros(M, 96) + 1, w, accumulate=stream)
+        assert torch.is_tensor(out) and float(stream.abs().max()) == 0.0
+
+
+def test_fused_qkv_projection_takes_the_norm(fusing, twin):
+    kernels = fusing
+    heads, kv_heads, head_dim, page_size, width = 8, 2, 64, 16, 256
+    segments = [(300, 1), (0, 1), (17, 1), (64, 1)]
+    _, batch, view = make_paged_case(torch.bfloat16, heads, kv_heads, head_dim, page_size, segments, seed=23)
+    g = torch.Generator(device="cuda").manual_seed(24)
+    M = len(segments)
+    residual = torch.randn(M, width, device="cuda", generator=g) * 2
+    weight = 1.0 + 0.2 * torch.randn(width, device="cuda", generator=g)
+    w = (torch.randn((heads + 2 * kv_heads) * head_dim, width, device="cuda", generator=g) / math.sqrt(width)).to(torch.bfloat16)
+    inv_freq = (1.0 / (500000.0 ** (torch.arange(0, head_dim, 2).float() / head_dim))).cuda()
+    view2 = SimpleNamespace(keys=view.keys.float(), values=view.values.float(), block_table=view.block_table,
+                            page_size=page_size, window=None)
+    q = kernels.fused_qkv_rope(_deferred(residual, weight, 1e-5), w, batch, inv_freq, head_dim, heads, kv_heads, head_dim, view, True)
+    assert q is not None
+    qkv = (_rms(residual, weight, 1e-5) @ w.double().t()).float()
     twin.rope_kv_write(qkv, batch, inv_freq, head_dim, heads, kv_heads, head_dim, view2, True)
     close(q, qkv[:, :heads * head_dim], torch.bfloat16)
     close(view.keys, view2.keys, torch.bfloat16)

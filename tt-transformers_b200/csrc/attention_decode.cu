@@ -136,7 +136,10 @@ attention_decode_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    pdl_wait();
+    // The step's metadata (segment bounds, positions, block table) comes from the host, not from the kernel
+    // before this one, and the same holds for every key below the first new token's position: all of that is
+    // read before pdl_wait(), while the preceding kernel may still be running. The queries and the new
+    // tokens' keys and values are that kernel's output and are read after it.
     const int seg_start = cu_seqlens[seg];
     const int seg_tokens = cu_seqlens[seg + 1] - seg_start;
     if (seg_tokens <= 0) return;                                // a padded segment of a captured step
@@ -156,16 +159,7 @@ attention_decode_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_
     const int last_page = num_tiles > 0 ? (k_end - 1) >> page_shift : page_base;
 
     if (num_tiles > 0) {
-        // the query rows (rows beyond valid_rows are zero) and the block-table entries of this block's keys
-        for (int idx = tid; idx < ROWS * CHUNKS; idx += AD_THREADS) {
-            const int r = idx / CHUNKS, c = idx % CHUNKS;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (r < valid_rows) {
-                const int token = r / rep, head = kvh * rep + r % rep;
-                v = *reinterpret_cast<const uint4*>(qkv + (size_t)(seg_start + token) * q_row_stride + (size_t)head * HD + c * 8);
-            }
-            *reinterpret_cast<uint4*>(q_tile + r * HD * 2 + ((c ^ (r & 7)) << 4)) = v;
-        }
+        // the block-table entries of this block's keys
         const int count = min(last_page - page_base + 1, AD_TABLE_CACHE);
         for (int i = tid; i < count; i += AD_THREADS) page_cache[i] = table[page_base + i];
     }
@@ -190,8 +184,13 @@ attention_decode_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_
         const int copies = 2 * boxes * HALVES;                  // <= 32: one lane each
         const int which = lane / (boxes * HALVES);              // 0 keys, 1 values
         const int box = (lane / HALVES) % boxes, half = lane % HALVES;
+        bool waited = false;
         for (int tile = 0; tile < num_tiles; ++tile) {
             const int stage = tile % STAGES, round = tile / STAGES;
+            if (!waited && k_begin + (tile + 1) * AD_BN > q_first) {      // this tile holds keys of the new tokens
+                pdl_wait();
+                waited = true;
+            }
             if (round > 0 && !ad_mbar_wait(empty0 + 8 * stage, (round - 1) & 1)) {
                 if (lane == 0) atomicExch(error_flag, AD_ERR_PRODUCER);
                 break;
@@ -215,8 +214,22 @@ attention_decode_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_
                 ad_tma_2d(dst, which ? &map_v : &map_k, half * 64, row, full0 + 8 * stage);
             }
         }
-    } else if (num_tiles > 0) {
+        if (!waited) pdl_wait();        // this warp takes part in writing the result
+    } else {
         // ------------------------------------------------------------------ consumers
+        pdl_wait();
+      if (num_tiles > 0) {
+        // the query rows (rows beyond valid_rows are zero)
+        for (int idx = tid; idx < ROWS * CHUNKS; idx += AD_CONSUMERS * 32) {
+            const int r = idx / CHUNKS, c = idx % CHUNKS;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r < valid_rows) {
+                const int token = r / rep, head = kvh * rep + r % rep;
+                v = *reinterpret_cast<const uint4*>(qkv + (size_t)(seg_start + token) * q_row_stride + (size_t)head * HD + c * 8);
+            }
+            *reinterpret_cast<uint4*>(q_tile + r * HD * 2 + ((c ^ (r & 7)) << 4)) = v;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(AD_CONSUMERS * 32) : "memory");      // the consumer warps only
         // B fragments of Q^T: ldmatrix of query rows (lane & 7) at four consecutive chunks gives two k-steps
         uint32_t q_frag[NT][KS][2];
 #pragma unroll
@@ -331,6 +344,7 @@ attention_decode_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_
             __syncwarp();
             if (lane == 0) ad_mbar_arrive(empty0 + 8 * stage);
         }
+      }
     }
 
     pdl_launch_dependents();     // the streaming part is over: the next kernel may move in

@@ -161,6 +161,71 @@ sample_kernel(const float* __restrict__ logits, int ld, int vocab, const float* 
     }
 }
 
+// ---- the largest logit of every row, the vocabulary cut into ARGMAX_PARTS slices of one block each
+// (one block per row, as above, is bound by the latency of a single block's loads at a vocabulary of 128 K)
+#define ARGMAX_PARTS 32
+#define ARGMAX_THREADS 256
+
+__global__ void __launch_bounds__(ARGMAX_THREADS)
+argmax_partial_kernel(const float* __restrict__ logits, int ld, int vocab, Best* __restrict__ partial) {
+    __shared__ Best scratch[32];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int row = blockIdx.y, part = blockIdx.x;
+    const float* l = logits + (size_t)row * ld;
+    const int per = ((vocab + ARGMAX_PARTS - 1) / ARGMAX_PARTS + 3) & ~3;       // a multiple of four ids
+    const int begin = part * per, end = min(begin + per, vocab);
+    Best mine{-INFINITY, 0x7fffffff};
+    if ((ld & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0) {
+        const int end4 = begin + ((end - begin) > 0 ? ((end - begin) & ~3) : 0);
+        for (int i = begin + 4 * threadIdx.x; i < end4; i += 4 * ARGMAX_THREADS) {
+            const float4 v = *reinterpret_cast<const float4*>(l + i);
+            mine = better(mine, Best{v.x, i});
+            mine = better(mine, Best{v.y, i + 1});
+            mine = better(mine, Best{v.z, i + 2});
+            mine = better(mine, Best{v.w, i + 3});
+        }
+        for (int i = end4 + threadIdx.x; i < end; i += ARGMAX_THREADS) mine = better(mine, Best{l[i], i});
+    } else {
+        for (int i = begin + threadIdx.x; i < end; i += ARGMAX_THREADS) mine = better(mine, Best{l[i], i});
+    }
+    const Best top = block_best(mine, scratch);
+    if (threadIdx.x == 0) partial[row * ARGMAX_PARTS + part] = top;
+}
+
+// one warp per row
+__global__ void argmax_final_kernel(const Best* __restrict__ partial, int rows, int* __restrict__ out) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    Best v = lane < ARGMAX_PARTS ? partial[row * ARGMAX_PARTS + lane] : Best{-INFINITY, 0x7fffffff};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Best other;
+        other.value = __shfl_xor_sync(0xffffffffu, v.value, o);
+        other.index = __shfl_xor_sync(0xffffffffu, v.index, o);
+        v = better(v, other);
+    }
+    if (lane == 0) out[row] = v.index;
+}
+
+TTB_EXPORT int ttb_argmax_scratch_bytes(int rows) { return rows * ARGMAX_PARTS * (int)sizeof(Best); }
+
+// out[row] = the id of the row's largest logit (the lowest id among equal ones); scratch: ttb_argmax_scratch_bytes(rows).
+TTB_EXPORT int ttb_argmax(const float* logits, int ld, int rows, int vocab, void* scratch, int* out, cudaStream_t stream) {
+    if (rows == 0) return TTB_OK;
+    if (!logits || !out || !scratch || vocab < 1) return TTB_ERR_ARGUMENT;
+    if (rows > 65535) return TTB_ERR_UNSUPPORTED;
+    static_assert(ARGMAX_PARTS <= 32, "the final kernel reads one partial result per lane");
+    ttb_launch(argmax_partial_kernel, dim3(ARGMAX_PARTS, rows), dim3(ARGMAX_THREADS), 0, stream, logits, ld, vocab,
+               (Best*)scratch);
+    int status = ttb_launch_status();
+    if (status != TTB_OK) return status;
+    ttb_launch(argmax_final_kernel, dim3((rows + 3) / 4), dim3(128), 0, stream, (const Best*)scratch, rows, out);
+    return ttb_launch_status();
+}
+
 TTB_EXPORT int ttb_sample(const float* logits, int ld, int rows, int vocab, const float* temperature,
                           const int* top_k, const float* top_p, const long long* seeds, const int* counters,
                           int* out, cudaStream_t stream) {

@@ -49,7 +49,10 @@ class Attention(Mixer):
     def cache_request(self):
         return PagedKV(self.kv_heads, self.head_dim, self.window)
 
-    def forward(self, x, batch, cache, write_cache=True):
+    fuses_norm = True
+    fuses_residual = True
+
+    def forward(self, x, batch, cache, write_cache=True, residual=None):
         k = self.runtime.kernels
         rotation = self.position.rotation() if self.position is not None else None
         inv_freq, rotary_dim = rotation if rotation is not None else (None, 0)
@@ -61,6 +64,8 @@ class Attention(Mixer):
             qkv = k.linear(x, self.w_qkv)
             k.rope_kv_write(qkv, batch, inv_freq, rotary_dim, self.heads, self.kv_heads, self.head_dim, cache, write_cache)
         mixed = k.paged_attention(qkv, batch, self.heads, self.kv_heads, self.head_dim, self.scale, cache)
+        if residual is not None:
+            return k.linear(mixed, self.w_o, accumulate=residual)      # ADDED, or the product where that is not fused
         return k.linear(mixed, self.w_o)
 
 

@@ -109,8 +109,43 @@ class StepBatch:
     extras: dict = field(default_factory=dict)   # per-step tables that kernels derive once and reuse in every layer
 
 
+class DeferredNorm:
+    """A norm that has been asked for but not computed: the float32 residual rows, the norm's
+    float32 weight and eps. A kernel that can take the norm into its own loads (a skinny matrix
+    product reads the residual stream, scales by the weight and divides its sums by the rows'
+    RMS) accepts this in place of the normalised tensor; everything else calls materialize()."""
+
+    __slots__ = ("residual", "weight", "eps", "_materialize")
+
+    def __init__(self, residual, weight, eps, materialize):
+        self.residual, self.weight, self.eps, self._materialize = residual, weight, float(eps), materialize
+
+    @property
+    def shape(self):
+        return self.residual.shape
+
+    def materialize(self):
+        return self._materialize()
+
+
+class _Added:
+    """What a part returns instead of its output when it has already added that output to the
+    residual stream it was given."""
+
+    def __repr__(self):
+        return "ADDED"
+
+
+ADDED = _Added()
+
+
 class Part:
-    """Base of all parts."""
+    """Base of all parts. Two optional capabilities, off unless a part says otherwise:
+    `fuses_norm`: forward() accepts a DeferredNorm in place of x; `fuses_residual`: forward()
+    accepts residual=<float32 stream> and may add its output there and return ADDED."""
+
+    fuses_norm = False
+    fuses_residual = False
 
     def tensor_specs(self) -> List[TensorSpec]:
         return []
@@ -145,7 +180,10 @@ class FeedForward(Part):
 class Norm(Part):
     """forward_add(residual, delta) adds delta (or nothing, if None) into the
     float32 residual stream in place and returns the normalised tensor in the
-    compute dtype."""
+    compute dtype. A norm with `can_defer` also takes defer=True and may then
+    return a DeferredNorm when there is nothing to add."""
+
+    can_defer = False
 
     def forward_add(self, residual, delta):
         raise NotImplementedError

@@ -4,11 +4,25 @@
 (src/tt_transformers/models/llama32_1b/model.py:113-139,141-186). The residual stream x
 is float32. A sub-layer's output is not added at once: it is handed on as `delta` and
 added inside the next norm kernel, which reads and writes x once instead of twice.
+
+Parts that say so fuse further: a sub-layer with `fuses_residual` is given the stream and may
+add its output there itself (its last product's epilogue does it) and return ADDED; a norm with
+`can_defer` before a sub-layer with `fuses_norm` may hand on a DeferredNorm, which that
+sub-layer's first product computes on the way. A decode layer then runs no norm kernel at all.
+Parts without these flags see tensors only, as before.
 """
 
 from __future__ import annotations
 
-from .base import register_part
+from .base import ADDED, register_part
+
+
+def _normed(norm, consumer, x, delta):
+    if delta is ADDED:
+        delta = None
+    if getattr(norm, "can_defer", False) and getattr(consumer, "fuses_norm", False):
+        return norm.forward_add(x, delta, defer=True)
+    return norm.forward_add(x, delta)
 
 
 class PreNormBlock:
@@ -19,11 +33,16 @@ class PreNormBlock:
         return [self.norm1, self.mixer, self.norm2, self.feed_forward]
 
     def forward(self, x, delta, batch, cache, write_cache=True):
-        """x: float32 residual, updated in place; delta: pending sub-layer output or None.
-        Returns (x, delta) for the next block."""
-        h = self.norm1.forward_add(x, delta)
-        mixed = self.mixer.forward(h, batch, cache, write_cache)
-        h = self.norm2.forward_add(x, mixed)
+        """x: float32 residual, updated in place; delta: pending sub-layer output, None, or ADDED
+        (nothing pending). Returns (x, delta) for the next block."""
+        h = _normed(self.norm1, self.mixer, x, delta)
+        if getattr(self.mixer, "fuses_residual", False):
+            mixed = self.mixer.forward(h, batch, cache, write_cache, residual=x)
+        else:
+            mixed = self.mixer.forward(h, batch, cache, write_cache)
+        h = _normed(self.norm2, self.feed_forward, x, mixed)
+        if getattr(self.feed_forward, "fuses_residual", False):
+            return x, self.feed_forward.forward(h, batch, residual=x)
         return x, self.feed_forward.forward(h, batch)
 
 

@@ -31,6 +31,8 @@ class Embedding(Part):
 class Head(Part):
     """`weight_name` None: the head shares the table of `tied_to` (an Embedding)."""
 
+    fuses_norm = True
+
     def __init__(self, vocab: int, width: int, weight_name=None, tied_to: Embedding = None):
         self.vocab, self.width, self.weight_name, self.tied_to = int(vocab), int(width), weight_name, tied_to
         if (weight_name is None) == (tied_to is None):

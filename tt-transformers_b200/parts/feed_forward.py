@@ -29,9 +29,15 @@ class SwiGLU(FeedForward):
         self.w_gate_up = runtime.matrix(torch.cat([tensors[p + "gate_proj.weight"], tensors[p + "up_proj.weight"]], 0))
         self.w_down = runtime.matrix(tensors[p + "down_proj.weight"])
 
-    def forward(self, x, batch):
+    fuses_norm = True
+    fuses_residual = True
+
+    def forward(self, x, batch, residual=None):
         k = self.runtime.kernels
-        return k.linear(k.linear_swiglu(x, self.w_gate_up), self.w_down)
+        h = k.linear_swiglu(x, self.w_gate_up)
+        if residual is not None:
+            return k.linear(h, self.w_down, accumulate=residual)       # ADDED, or the product where that is not fused
+        return k.linear(h, self.w_down)
 
 
 register_part("feed_forward", "swiglu", SwiGLU)

@@ -17,7 +17,7 @@ from typing import Dict, List, Optional
 
 import torch
 
-from .base import PartSpec, Runtime, StepBatch, TensorSpec, build_part
+from .base import ADDED, PartSpec, Runtime, StepBatch, TensorSpec, build_part
 from .embedding import Embedding, Head
 
 
@@ -139,7 +139,12 @@ class DecoderModel:
         if batch.num_wanted == 0:
             return torch.empty(0, self.spec.vocab_size, dtype=torch.float32, device=x.device)
         x = k.gather_rows(x, batch.want_rows)
+        if delta is ADDED:
+            delta = None
         if delta is not None:
             delta = k.gather_rows(delta, batch.want_rows)
-        h = self.final_norm.forward_add(x, delta)
+        if getattr(self.final_norm, "can_defer", False) and getattr(self.head, "fuses_norm", False):
+            h = self.final_norm.forward_add(x, delta, defer=True)
+        else:
+            h = self.final_norm.forward_add(x, delta)
         return self.head.forward(h)
