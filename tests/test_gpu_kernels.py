@@ -449,13 +449,14 @@ def fusing(kernels):
     kernels.fuse_norm, kernels.fuse_add = before
 
 
-def _deferred(residual, weight, eps):
-    from tt_transformers_b200.parts.base import DeferredNorm
+class _Norm:
+    """As much of a norm part as the fused products ask for."""
 
-    def never():
-        raise AssertionError("the norm was meant to be fused into the product")
+    def __init__(self, weight, eps):
+        self.weight, self.eps = weight, eps
 
-    return DeferredNorm(residual, weight.float().contiguous(), eps, never)
+    def fusion_args(self):
+        return self.weight.float().contiguous(), self.eps
 
 
 def _rms(residual, weight, eps):
@@ -463,84 +464,88 @@ def _rms(residual, weight, eps):
     return r * torch.rsqrt((r * r).mean(-1, keepdim=True) + eps) * weight.double()
 
 
-@pytest.mark.parametrize("M,N,K,eps", [(1, 384, 96, 1e-5), (8, 3072, 2048, 1e-5), (5, 77, 72, 1e-6), (16, 2048, 2048, 1e-5),
-                                       (12, 128256, 256, 1e-3), (8, 2048, 8192, 1e-5), (3, 100, 4096, 1e-5)])
-def test_skinny_product_takes_the_norm_before_it_and_the_residual_add_after_it(fusing, twin, M, N, K, eps):
-    kernels = fusing
-    """A deferred RMS norm as the product's input (plain, SwiGLU pair, both output types), and the float32
-    residual stream as its output, against the steps one by one in float64."""
-    from tt_transformers_b200.parts.base import ADDED
+@pytest.mark.parametrize("M,N,K,eps", [(1, 384, 96, 1e-5), (8, 2048, 2048, 1e-5), (5, 72, 80, 1e-6), (16, 2048, 2048, 1e-5),
+                                       (12, 256, 8192, 1e-3), (8, 8192, 2048, 1e-5), (3, 104, 4096, 1e-5)])
+def test_skinny_products_take_the_residual_add_and_the_norm_between_them(fusing, twin, M, N, K, eps):
+    """The product that ends a sub-layer adds to the float32 stream and prepares the norm that follows;
+    the product after it (plain, SwiGLU pair, both output types) finishes that norm. Against the steps
+    one by one in float64."""
+    from tt_transformers_b200.parts.base import ADDED, DeferredNorm
 
+    kernels = fusing
     g = torch.Generator(device="cuda").manual_seed(31)
-    residual = torch.randn(M, K, device="cuda", generator=g) * 3.0
-    weight = 1.0 + 0.3 * torch.randn(K, device="cuda", generator=g)
-    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
-    assert kernels.defers_norm(residual, torch.bfloat16)
-    kept = residual.clone()
-    normed = _rms(residual, weight, eps)
-    for out_dtype in (torch.bfloat16, torch.float32):
-        got = kernels.linear(_deferred(residual, weight, eps), w, out_dtype=out_dtype)
-        assert got.dtype == out_dtype
-        close(got, normed @ w.double().t(), torch.bfloat16)
-    if N % 2 == 0:
-        got = kernels.linear_swiglu(_deferred(residual, weight, eps), w)
-        close(got, twin.linear_swiglu(normed, w.double()), torch.bfloat16)
-    assert torch.equal(residual, kept), "a deferred norm leaves the residual stream as it is"
-    # the product added to the stream
     x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
-    stream = torch.randn(M, N, device="cuda", generator=g)
-    want = stream.double() + x.double() @ w.double().t()
-    assert kernels.linear(x, w, accumulate=stream) is ADDED
-    close(stream, want, torch.bfloat16)
-    # both at once
-    stream = torch.randn(M, N, device="cuda", generator=g)
-    want = stream.double() + normed @ w.double().t()
-    assert kernels.linear(_deferred(residual, weight, eps), w, accumulate=stream) is ADDED
-    close(stream, want, torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    stream = torch.randn(M, N, device="cuda", generator=g) * 3.0
+    weight = 1.0 + 0.3 * torch.randn(N, device="cuda", generator=g)
+    norm = _Norm(weight.to(torch.bfloat16), eps)
+    want_stream = stream.double() + x.double() @ w.double().t()
+    # the add alone
+    alone = stream.clone()
+    assert kernels.linear(x, w, accumulate=alone) is ADDED
+    close(alone, want_stream, torch.bfloat16)
+    # the add with the norm prepared
+    prepared = kernels.linear(x, w, accumulate=stream, next_norm=norm)
+    assert isinstance(prepared, DeferredNorm) and prepared.made_for is norm
+    close(stream, want_stream, torch.bfloat16)
+    normed = _rms(stream, norm.weight, eps)            # of the stream as the kernel left it
+    close(prepared.materialize(), normed, torch.bfloat16)
+    w2 = (torch.randn(320, N, device="cuda", generator=g) / math.sqrt(N)).to(torch.bfloat16)
+    for out_dtype in (torch.bfloat16, torch.float32):
+        got = kernels.linear(prepared, w2, out_dtype=out_dtype)
+        assert got.dtype == out_dtype
+        close(got, normed @ w2.double().t(), torch.bfloat16)
+    close(kernels.linear_swiglu(prepared, w2), twin.linear_swiglu(normed, w2.double()), torch.bfloat16)
+    # finished by a product that also ends a sub-layer
+    stream2 = torch.randn(M, 320, device="cuda", generator=g)
+    want2 = stream2.double() + normed @ w2.double().t()
+    assert kernels.linear(prepared, w2, accumulate=stream2) is ADDED
+    close(stream2, want2, torch.bfloat16)
 
 
 def test_products_that_cannot_fuse_fall_back_to_the_steps_one_by_one(fusing):
-    kernels = fusing
-    """More rows than the skinny kernel takes, or float32: the deferred norm is materialised and the
-    product comes back for the caller to add."""
+    """More rows than the skinny kernel takes, or float32: the product comes back for the caller to add,
+    and a DeferredNorm that reaches such a product is materialised."""
     from tt_transformers_b200.parts.base import DeferredNorm
 
+    kernels = fusing
     g = torch.Generator(device="cuda").manual_seed(32)
     for dtype, M in ((torch.bfloat16, 40), (torch.float32, 4)):
-        residual = torch.randn(M, 96, device="cuda", generator=g)
-        weight = (1.0 + 0.1 * torch.randn(96, device="cuda", generator=g)).to(dtype)
+        x = torch.randn(M, 96, device="cuda", generator=g).to(dtype)
         w = (torch.randn(64, 96, device="cuda", generator=g) / 10).to(dtype)
+        stream = torch.zeros(M, 64, device="cuda")
+        out = kernels.linear(x, w, accumulate=stream, next_norm=_Norm(torch.ones(64, device="cuda", dtype=dtype), 1e-5))
+        assert torch.is_tensor(out) and float(stream.abs().max()) == 0.0
         calls = []
 
         def materialize():
             calls.append(1)
-            return kernels.add_rmsnorm(residual, None, weight, 1e-5, dtype)
+            return x
 
-        d = DeferredNorm(residual, weight.float(), 1e-5, materialize)
-        got = kernels.linear(d, w)
+        got = kernels.linear(DeferredNorm(x, torch.zeros(1, 16, device="cuda"), 1e-5, None, materialize), w)
         assert calls == [1]
-        close(got, _rms(residual, weight, 1e-5) @ w.double().t(), dtype)
-        stream = torch.zeros(M, 64, device="cuda")
-        out = kernels.linear(got.new_zeros(M, 96) + 1, w, accumulate=stream)
-        assert torch.is_tensor(out) and float(stream.abs().max()) == 0.0
+        close(got, x.double() @ w.double().t(), dtype)
 
 
-def test_fused_qkv_projection_takes_the_norm(fusing, twin):
+def test_fused_qkv_projection_finishes_a_prepared_norm(fusing, twin):
     kernels = fusing
     heads, kv_heads, head_dim, page_size, width = 8, 2, 64, 16, 256
     segments = [(300, 1), (0, 1), (17, 1), (64, 1)]
     _, batch, view = make_paged_case(torch.bfloat16, heads, kv_heads, head_dim, page_size, segments, seed=23)
     g = torch.Generator(device="cuda").manual_seed(24)
     M = len(segments)
-    residual = torch.randn(M, width, device="cuda", generator=g) * 2
-    weight = 1.0 + 0.2 * torch.randn(width, device="cuda", generator=g)
+    stream = torch.randn(M, width, device="cuda", generator=g) * 2
+    norm = _Norm((1.0 + 0.2 * torch.randn(width, device="cuda", generator=g)).to(torch.bfloat16), 1e-5)
+    x0 = torch.randn(M, 64, device="cuda", generator=g).to(torch.bfloat16)
+    w0 = (torch.randn(width, 64, device="cuda", generator=g) / 8).to(torch.bfloat16)
+    prepared = kernels.linear(x0, w0, accumulate=stream, next_norm=norm)
     w = (torch.randn((heads + 2 * kv_heads) * head_dim, width, device="cuda", generator=g) / math.sqrt(width)).to(torch.bfloat16)
     inv_freq = (1.0 / (500000.0 ** (torch.arange(0, head_dim, 2).float() / head_dim))).cuda()
     view2 = SimpleNamespace(keys=view.keys.float(), values=view.values.float(), block_table=view.block_table,
                             page_size=page_size, window=None)
-    q = kernels.fused_qkv_rope(_deferred(residual, weight, 1e-5), w, batch, inv_freq, head_dim, heads, kv_heads, head_dim, view, True)
+    q = kernels.fused_qkv_rope(prepared, w, batch, inv_freq, head_dim, heads, kv_heads, head_dim, view, True)
     assert q is not None
-    qkv = (_rms(residual, weight, 1e-5) @ w.double().t()).float()
+    qkv = (_rms(stream, norm.weight, 1e-5) @ w.double().t()).float()
     twin.rope_kv_write(qkv, batch, inv_freq, head_dim, heads, kv_heads, head_dim, view2, True)
     close(q, qkv[:, :heads * head_dim], torch.bfloat16)
     close(view.keys, view2.keys, torch.bfloat16)

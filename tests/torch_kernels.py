@@ -41,7 +41,7 @@ class TorchKernels:
     def gather_rows(self, x, rows):
         return x[rows.long()].clone()
 
-    def linear(self, x, w, out_dtype=None, accumulate=None):
+    def linear(self, x, w, out_dtype=None, accumulate=None, next_norm=None):
         # `accumulate` is an offer, not an order: the twin returns the product and the caller adds it
         return (x.float() @ w.float().t()).to(out_dtype or x.dtype)
 

@@ -19,13 +19,14 @@
 //         their positions (float32 angles, accurate sincosf), write the queries out and put keys and
 //         values straight into their cache pages; no rotation kernel and no qkv round trip
 //
-// Two fusions with the steps around the product, so that a decode layer needs no norm kernel:
-//   NORM   x is not a bfloat16 matrix but the float32 residual stream; the kernel multiplies it by the norm's
-//          weight on the way into the fragments (rounded to bfloat16 once, as the norm kernel would), gathers
-//          sum(x^2) of every row from the values it loads anyway, and scales its sums by
-//          1 / sqrt(mean(x^2) + eps) in the epilogue: W (g * x / rms) = (W (g * x)) / rms.
-//   residual != null   the epilogue adds the product to the float32 residual stream in place (every element
-//          belongs to one thread) instead of writing `out`.
+// Two fusions with the steps around the product take the norm kernel out of a decode layer. The
+// product that ends a sub-layer (`residual` set) adds its result to the float32 residual stream in
+// place, writes xg = bfloat16(g * residual), g being the weight of the norm that follows, and leaves
+// the sum of residual^2 over its rows of every token in ssq_out[block]. The product that begins the
+// next sub-layer (NORM) takes xg as its x, adds the partial sums up and scales its results by
+// 1 / sqrt(sum / K + eps):  W (g * r / rms(r)) = (W (g * r)) / rms(r). Every element of the stream
+// belongs to one thread of one block, and the partial sums are added in a fixed order, so the
+// result does not change from run to run.
 #include "common.cuh"
 
 #define GM_FULL 0
@@ -45,12 +46,19 @@ struct GmRope {
     int table_width, page_size, num_pages, heads, kv_heads, head_dim, write_kv;
 };
 
-// The fusions' operands (all null / 0 when unused).
+// The fusions' operands (null / 0 when unused).
 struct GmFuse {
-    const float* norm_weight;    // [K] float32: NORM input
+    // the product that begins a sub-layer: x = g * residual, to be divided by the rows' RMS
+    const float* ssq_in;         // [ssq_parts][16] partial sums of residual^2 per token
+    int ssq_parts;
     float eps;
-    float* residual;             // [M, ldr] float32: accumulate the product here
+    // the product that ends a sub-layer
+    float* residual;             // [M, ldr] float32: the product is added here
     int ldr;
+    const float* next_weight;    // [N] float32 weight of the norm that follows (null: only the add)
+    __nv_bfloat16* xg;           // [M, ldxg] = bfloat16(next_weight * residual)
+    int ldxg;
+    float* ssq_out;              // [blocks][16]
 };
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
@@ -65,12 +73,6 @@ __device__ __forceinline__ uint4 ldg_cached(const void* p) {
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     return v;
 }
-// Four floats through L1 (not the read-only path: the residual stream is written by the kernel before this one).
-__device__ __forceinline__ float4 ldg_cached_f4(const float* p) {
-    float4 v;
-    asm volatile("ld.global.ca.v4.f32 {%0,%1,%2,%3}, [%4];\n" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
-    return v;
-}
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
     asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
@@ -78,15 +80,17 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <int NB, int RG, int MODE, int GM_WARPS, typename TO, bool NORM>
+// ACCUM (the epilogue that adds to the residual stream) is a template parameter and not a test of
+// `fuse.residual`: with that epilogue compiled in, the plain 8-row shapes came out with 58 registers
+// a thread instead of 32, and although the product by itself got faster, the decode step got slower
+// (fewer blocks of the kernels before and after fit beside them while those start early and wait).
+template <int NB, int RG, int MODE, int GM_WARPS, typename TO, bool NORM, bool ACCUM>
 __global__ void __launch_bounds__(GM_WARPS * 32)
-gemv_mma_kernel(const void* __restrict__ x_any, const __nv_bfloat16* __restrict__ w, TO* __restrict__ out,
+gemv_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w, TO* __restrict__ out,
                 int M, int N, int K, int ldx, int ldw, int ldo, int pair_offset, GmRope rope, GmFuse fuse) {
-    const __nv_bfloat16* x = NORM ? nullptr : static_cast<const __nv_bfloat16*>(x_any);
-    const float* xf = NORM ? static_cast<const float*>(x_any) : nullptr;
     constexpr int ROWS_PER_GROUP = (MODE == GM_FULL) ? 16 : 8;
     constexpr int GM_THREADS = GM_WARPS * 32;
-    extern __shared__ float4 partial[];          // [GM_WARPS][RG * NB * 32], then (NORM) float [GM_WARPS][NB * 8] sums of squares
+    extern __shared__ float4 partial[];          // [GM_WARPS][RG * NB * 32], then (NORM) float [GM_WARPS * 2][16] sums of squares
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     int n0 = blockIdx.x * ROWS_PER_GROUP * RG;
@@ -113,7 +117,9 @@ gemv_mma_kernel(const void* __restrict__ x_any, const __nv_bfloat16* __restrict_
         }
     }
     // The weights do not depend on the kernels before this one: ask L2 for this block's rows now,
-    // then wait for the predecessor (whose output is x).
+    // then wait for the predecessor (whose output is x). (Loading the first k-blocks into registers
+    // here instead made a chain of products faster and the whole decode step slower: the loads of
+    // blocks that wait compete with the kernel that the step is waiting for.)
     pdl_launch_dependents();
     {
         const int row_bytes = K * 2;
@@ -131,17 +137,18 @@ gemv_mma_kernel(const void* __restrict__ x_any, const __nv_bfloat16* __restrict_
         }
     }
     pdl_wait();
+    // NORM: thread `tid` adds up the partial sums of token tid % 16 over the parts tid / 16, tid / 16 + threads / 16, ...
+    float ssq_mine = 0.f;
+    if (NORM) {
+        for (int p = threadIdx.x >> 4; p < fuse.ssq_parts; p += GM_THREADS >> 4) ssq_mine += fuse.ssq_in[p * 16 + (threadIdx.x & 15)];
+    }
     const __nv_bfloat16* xrow[NB];
-    const float* xfrow[NB];
     bool xok[NB];
-    float ssq[NB];
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
         const int m = nb * 8 + g;
         xok[nb] = m < M;
-        xrow[nb] = NORM ? nullptr : x + (size_t)(xok[nb] ? m : 0) * ldx;
-        xfrow[nb] = NORM ? xf + (size_t)(xok[nb] ? m : 0) * ldx : nullptr;
-        ssq[nb] = 0.f;
+        xrow[nb] = x + (size_t)(xok[nb] ? m : 0) * ldx;
     }
 
     float acc[RG][NB][4];
@@ -167,38 +174,11 @@ gemv_mma_kernel(const void* __restrict__ x_any, const __nv_bfloat16* __restrict_
                 wv[u][rg][0] = in ? ldg_stream(wrow[rg][0] + k) : zero;
                 wv[u][rg][1] = (in && MODE != GM_HALF) ? ldg_stream(wrow[rg][1] + k) : zero;
             }
-            if (!NORM) {
 #pragma unroll
-                for (int nb = 0; nb < NB; ++nb) xv[u][nb] = (in && xok[nb]) ? ldg_cached(xrow[nb] + k) : zero;
-            }
+            for (int nb = 0; nb < NB; ++nb) xv[u][nb] = (in && xok[nb]) ? ldg_cached(xrow[nb] + k) : zero;
         }
 #pragma unroll
-        for (int u = 0; u < UNROLL; ++u) {
-            if (NORM) {
-                // Eight float32 values of the residual stream times the norm's weight, rounded to bfloat16 once.
-                // They come from L1 (every block of the SM reads the same rows), so they are fetched here, one
-                // k-block at a time, and only the weights above are kept in flight across the unrolled blocks.
-                const int k = kb0 + u * GM_WARPS * 32 + t * 8;
-                const bool in = k < K;
-                float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
-                if (in) {
-                    g0 = ldg_cached_f4(fuse.norm_weight + k);
-                    g1 = ldg_cached_f4(fuse.norm_weight + k + 4);
-                }
-#pragma unroll
-                for (int nb = 0; nb < NB; ++nb) {
-                    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-                    if (in && xok[nb]) {
-                        a = ldg_cached_f4(xfrow[nb] + k);
-                        b = ldg_cached_f4(xfrow[nb] + k + 4);
-                    }
-                    ssq[nb] += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
-                    __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x * g0.x, a.y * g0.y), p1 = __floats2bfloat162_rn(a.z * g0.z, a.w * g0.w);
-                    __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x * g1.x, b.y * g1.y), p3 = __floats2bfloat162_rn(b.z * g1.z, b.w * g1.w);
-                    xv[u][nb] = make_uint4(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1),
-                                           *reinterpret_cast<uint32_t*>(&p2), *reinterpret_cast<uint32_t*>(&p3));
-                }
-            }
+        for (int u = 0; u < UNROLL; ++u)
 #pragma unroll
             for (int rg = 0; rg < RG; ++rg)
 #pragma unroll
@@ -208,7 +188,6 @@ gemv_mma_kernel(const void* __restrict__ x_any, const __nv_bfloat16* __restrict_
                     mma16816(acc[rg][nb], wv[u][rg][0].z, wv[u][rg][1].z, wv[u][rg][0].w, wv[u][rg][1].w,
                              xv[u][nb].z, xv[u][nb].w);
                 }
-        }
     }
 
     // ---- the warps add up
@@ -219,16 +198,8 @@ gemv_mma_kernel(const void* __restrict__ x_any, const __nv_bfloat16* __restrict_
         for (int nb = 0; nb < NB; ++nb)
             partial[warp * PER_WARP + (rg * NB + nb) * 32 + lane] =
                 make_float4(acc[rg][nb][0], acc[rg][nb][1], acc[rg][nb][2], acc[rg][nb][3]);
-    float* ssq_part = reinterpret_cast<float*>(partial + GM_WARPS * PER_WARP);       // [GM_WARPS][NB * 8]
-    if (NORM) {
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {      // the four lanes of a quad hold different k of the same row
-            float v = ssq[nb];
-            v += __shfl_xor_sync(0xffffffffu, v, 1);
-            v += __shfl_xor_sync(0xffffffffu, v, 2);
-            if (t == 0) ssq_part[warp * NB * 8 + nb * 8 + g] = v;
-        }
-    }
+    float* ssq_groups = reinterpret_cast<float*>(partial + GM_WARPS * PER_WARP);     // [GM_THREADS / 16][16]
+    if (NORM) ssq_groups[threadIdx.x] = ssq_mine;
     __syncthreads();
     for (int e = threadIdx.x; e < PER_WARP; e += GM_THREADS) {
         float4 s = partial[e];
@@ -244,9 +215,9 @@ gemv_mma_kernel(const void* __restrict__ x_any, const __nv_bfloat16* __restrict_
         if (NORM) {
             float q0 = 0.f, q1 = 0.f;
 #pragma unroll
-            for (int wp = 0; wp < GM_WARPS; ++wp) {
-                q0 += ssq_part[wp * NB * 8 + m0];
-                q1 += ssq_part[wp * NB * 8 + m1];
+            for (int grp = 0; grp < (GM_THREADS >> 4); ++grp) {        // the same order in every block and on every run
+                q0 += ssq_groups[grp * 16 + (m0 & 15)];
+                q1 += ssq_groups[grp * 16 + (m1 & 15)];
             }
             const float r0 = rsqrtf(q0 / (float)K + fuse.eps), r1 = rsqrtf(q1 / (float)K + fuse.eps);
             s.x *= r0; s.z *= r0;
@@ -294,17 +265,33 @@ gemv_mma_kernel(const void* __restrict__ x_any, const __nv_bfloat16* __restrict_
                 if (m0 < M) out[(size_t)m0 * ldo + lower] = from_float<TO>(s.x / (1.f + __expf(-s.x)) * s.z);
                 if (m1 < M) out[(size_t)m1 * ldo + lower] = from_float<TO>(s.y / (1.f + __expf(-s.y)) * s.w);
             }
-        } else if (fuse.residual != nullptr) {
-            float* res = fuse.residual;
-            if (lower < N) {
-                if (m0 < M) res[(size_t)m0 * fuse.ldr + lower] += s.x;
-                if (m1 < M) res[(size_t)m1 * fuse.ldr + lower] += s.y;
+        } else if (ACCUM) {
+            // the end of a sub-layer: add to the stream; for the norm that follows, g * stream and the rows' squares
+            const int upper = n0 + rg * 16 + 8 + eg;
+            float q0 = 0.f, q1 = 0.f;
+#pragma unroll
+            for (int which = 0; which < 4; ++which) {
+                const int m = (which & 1) ? m1 : m0, n = (which & 2) ? upper : lower;
+                if ((which & 2) && MODE != GM_FULL) continue;
+                if (m >= M || n >= N) continue;
+                const float delta = which == 0 ? s.x : which == 1 ? s.y : which == 2 ? s.z : s.w;
+                float* at = fuse.residual + (size_t)m * fuse.ldr + n;
+                const float r = *at + delta;
+                *at = r;
+                if (fuse.xg != nullptr) {
+                    fuse.xg[(size_t)m * fuse.ldxg + n] = __float2bfloat16_rn(r * fuse.next_weight[n]);
+                    if (which & 1) q1 += r * r; else q0 += r * r;
+                }
             }
-            if (MODE == GM_FULL) {
-                const int upper = n0 + rg * 16 + 8 + eg;
-                if (upper < N) {
-                    if (m0 < M) res[(size_t)m0 * fuse.ldr + upper] += s.z;
-                    if (m1 < M) res[(size_t)m1 * fuse.ldr + upper] += s.w;
+            if (fuse.xg != nullptr) {      // whole warps are here (RG = 1): lanes that differ in eg hold different rows of w
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                    q0 += __shfl_xor_sync(0xffffffffu, q0, o);
+                    q1 += __shfl_xor_sync(0xffffffffu, q1, o);
+                }
+                if (eg == 0) {
+                    fuse.ssq_out[(size_t)blockIdx.x * 16 + (m0 & 15)] = q0;
+                    fuse.ssq_out[(size_t)blockIdx.x * 16 + (m1 & 15)] = q1;
                 }
             }
         } else {
@@ -323,14 +310,14 @@ gemv_mma_kernel(const void* __restrict__ x_any, const __nv_bfloat16* __restrict_
     }
 }
 
-template <int NB, int RG, int MODE, int GM_WARPS, typename TO, bool NORM = false>
+template <int NB, int RG, int MODE, int GM_WARPS, typename TO, bool NORM = false, bool ACCUM = false>
 static int gemv_mma_launch(const void* x, const void* w, void* out, int M, int N, int K, int ldx, int ldw, int ldo,
                            int pair_offset, cudaStream_t stream, const GmRope* rope = nullptr,
                            const GmFuse* fuse = nullptr) {
     constexpr int rows = ((MODE == GM_FULL) ? 16 : 8) * RG;
-    const size_t smem = (size_t)GM_WARPS * RG * NB * 32 * sizeof(float4) + (NORM ? (size_t)GM_WARPS * NB * 8 * sizeof(float) : 0);
-    auto kernel = gemv_mma_kernel<NB, RG, MODE, GM_WARPS, TO, NORM>;
     constexpr int GM_THREADS = GM_WARPS * 32;
+    const size_t smem = (size_t)GM_WARPS * RG * NB * 32 * sizeof(float4) + (NORM ? (size_t)GM_THREADS * sizeof(float) : 0);
+    auto kernel = gemv_mma_kernel<NB, RG, MODE, GM_WARPS, TO, NORM, ACCUM>;
     static bool configured = false;
     if (!configured && smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -341,28 +328,32 @@ static int gemv_mma_launch(const void* x, const void* w, void* out, int M, int N
     GmFuse plain = {};
     const int blocks = (MODE == GM_ROPE) ? N / 16 : (N + rows - 1) / rows;
     ttb_launch(kernel, dim3(blocks), dim3(GM_THREADS), smem, stream,
-        x, (const __nv_bfloat16*)w, (TO*)out, M, N, K, ldx, ldw, ldo, pair_offset,
+        (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (TO*)out, M, N, K, ldx, ldw, ldo, pair_offset,
         rope ? *rope : none, fuse ? *fuse : plain);
     return ttb_launch_status();
 }
 
-template <int MODE, typename TO, bool NORM = false>
+// few blocks and a long K: sixteen warps per block keep enough loads in flight
+static bool gemv_mma_wide(int N, int K, int rows_small) { return K >= 4096 && (N + rows_small - 1) / rows_small < 4 * 148; }
+// matrices with few rows get 8-row fragments, so that there are blocks enough for every SM
+static bool gemv_mma_half(int M, int N) { return (N / 16) < 2 * 148 && M <= 32; }
+
+template <int MODE, typename TO, bool NORM = false, bool ACCUM = false>
 static int gemv_mma_by_rows(const void* x, const void* w, void* out, int M, int N, int K, int ldx, int ldw, int ldo,
                             int pair_offset, cudaStream_t stream, const GmFuse* fuse = nullptr) {
-    // few blocks and a long K: sixteen warps per block keep enough loads in flight
     constexpr int rows_small = (MODE == GM_FULL) ? 16 : 8;
-    const bool wide = K >= 4096 && (N + rows_small - 1) / rows_small < 4 * 148;
+    const bool wide = gemv_mma_wide(N, K, rows_small);
 #define GM_GO(NB, RG)                                                                                                      \
     do {                                                                                                                   \
         if (wide)                                                                                                          \
-            return gemv_mma_launch<NB, RG, MODE, 16, TO, NORM>(x, w, out, M, N, K, ldx, ldw, ldo, pair_offset, stream,     \
-                                                               nullptr, fuse);                                             \
-        return gemv_mma_launch<NB, RG, MODE, 8, TO, NORM>(x, w, out, M, N, K, ldx, ldw, ldo, pair_offset, stream, nullptr, \
-                                                          fuse);                                                           \
+            return gemv_mma_launch<NB, RG, MODE, 16, TO, NORM, ACCUM>(x, w, out, M, N, K, ldx, ldw, ldo, pair_offset,      \
+                                                                      stream, nullptr, fuse);                              \
+        return gemv_mma_launch<NB, RG, MODE, 8, TO, NORM, ACCUM>(x, w, out, M, N, K, ldx, ldw, ldo, pair_offset, stream,   \
+                                                                 nullptr, fuse);                                           \
     } while (0)
     if (M <= 8) GM_GO(1, 1);
     if (M <= 16) GM_GO(2, 1);
-    if constexpr (!NORM) {          // the norm fusion is built for the row counts it is used at
+    if constexpr (!NORM && !ACCUM) {          // the fusions are built for the row counts they are used at
         if (M <= 32) GM_GO(4, 1);
         GM_GO(8, 2);
     }
@@ -374,13 +365,16 @@ template <bool NORM>
 static int gemv_mma_dispatch(const void* x, const void* w, void* out, int out_dtype, int M, int N, int K, int ldx, int ldw,
                              int ldo, int pair_rows, const GmFuse* fuse, cudaStream_t stream) {
     const bool f32 = out_dtype == TTB_DTYPE_F32;
+    if (fuse != nullptr && fuse->residual != nullptr) {       // the result goes to the stream: `out` and its type play no part
+        if (gemv_mma_half(M, N))
+            return gemv_mma_by_rows<GM_HALF, float, NORM, true>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream, fuse);
+        return gemv_mma_by_rows<GM_FULL, float, NORM, true>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream, fuse);
+    }
     if (pair_rows > 0) {
         return f32 ? gemv_mma_by_rows<GM_PAIR, float, NORM>(x, w, out, M, N, K, ldx, ldw, ldo, pair_rows, stream, fuse)
                    : gemv_mma_by_rows<GM_PAIR, __nv_bfloat16, NORM>(x, w, out, M, N, K, ldx, ldw, ldo, pair_rows, stream, fuse);
     }
-    // matrices with few rows get 8-row fragments, so that there are blocks enough for every SM
-    const bool half = (N / 16) < 2 * 148 && M <= 32;
-    if (half)
+    if (gemv_mma_half(M, N))
         return f32 ? gemv_mma_by_rows<GM_HALF, float, NORM>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream, fuse)
                    : gemv_mma_by_rows<GM_HALF, __nv_bfloat16, NORM>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream, fuse);
     return f32 ? gemv_mma_by_rows<GM_FULL, float, NORM>(x, w, out, M, N, K, ldx, ldw, ldo, 0, stream, fuse)
@@ -399,22 +393,32 @@ TTB_EXPORT int ttb_gemv_mma(const void* x, const void* w, void* out, int out_dty
     return gemv_mma_dispatch<false>(x, w, out, out_dtype, M, N, K, ldx, ldw, ldo, pair_rows, nullptr, stream);
 }
 
-// The same product with the steps around it fused in (M <= 16):
-//   norm_weight != null: x is the float32 residual stream [M, ldx] and the product is taken of its RMS norm
-//       with this float32 weight [K] and eps (x itself is left as it is);
-//   residual != null: the product is added to the float32 matrix residual [M, ldr] and `out` is not written
-//       (not with pair_rows).
-TTB_EXPORT int ttb_gemv_mma_fused(const void* x, const float* norm_weight, float eps, const void* w, void* out,
+// How many blocks the product of an [M <= 16, K] x with an [N, K] w runs as: the first extent of the
+// partial sums of squares that ttb_gemv_mma_fused writes.
+TTB_EXPORT int ttb_gemv_mma_parts(int M, int N) {
+    const int rows = gemv_mma_half(M, N) ? 8 : 16;
+    return (N + rows - 1) / rows;
+}
+
+// The same product with the steps around it fused in (M <= 16), see the head of this file.
+//   ssq_in != null: x is g * residual (bfloat16) and the results are divided by the rows' RMS, taken from the
+//       partial sums ssq_in [ssq_parts][16] and eps;
+//   residual != null: the product is added to the float32 matrix residual [M, ldr] and `out` is not written (not
+//       with pair_rows); with next_weight [N] float32 also xg [M, ldxg] = bfloat16(next_weight * residual) and
+//       ssq_out [ttb_gemv_mma_parts(M, N)][16] are written.
+TTB_EXPORT int ttb_gemv_mma_fused(const void* x, const float* ssq_in, int ssq_parts, float eps, const void* w, void* out,
                                   int out_dtype, int M, int N, int K, int ldx, int ldw, int ldo, int pair_rows,
-                                  float* residual, int ldr, cudaStream_t stream) {
+                                  float* residual, int ldr, const float* next_weight, void* xg, int ldxg, float* ssq_out,
+                                  cudaStream_t stream) {
     if (M == 0 || N == 0) return TTB_OK;
     if (!x || !w || (!out && !residual)) return TTB_ERR_ARGUMENT;
     if (residual && pair_rows > 0) return TTB_ERR_ARGUMENT;
-    if (M > 16 || K < 8 || (K & 7) || (ldw & 7) || !aligned16(x) || !aligned16(w)) return TTB_ERR_UNSUPPORTED;
-    if (norm_weight ? ((ldx & 3) || !aligned16(norm_weight)) : (ldx & 7)) return TTB_ERR_UNSUPPORTED;
+    if (next_weight && (!residual || !xg || !ssq_out)) return TTB_ERR_ARGUMENT;
+    if (ssq_in && ssq_parts < 1) return TTB_ERR_ARGUMENT;
+    if (M > 16 || K < 8 || (K & 7) || (ldx & 7) || (ldw & 7) || !aligned16(x) || !aligned16(w)) return TTB_ERR_UNSUPPORTED;
     if (out_dtype != TTB_DTYPE_F32 && out_dtype != TTB_DTYPE_BF16) return TTB_ERR_UNSUPPORTED;
-    GmFuse fuse = {norm_weight, eps, residual, ldr};
-    if (norm_weight) return gemv_mma_dispatch<true>(x, w, out, out_dtype, M, N, K, ldx, ldw, ldo, pair_rows, &fuse, stream);
+    GmFuse fuse = {ssq_in, ssq_parts, eps, residual, ldr, next_weight, next_weight ? (__nv_bfloat16*)xg : nullptr, ldxg, ssq_out};
+    if (ssq_in) return gemv_mma_dispatch<true>(x, w, out, out_dtype, M, N, K, ldx, ldw, ldo, pair_rows, &fuse, stream);
     return gemv_mma_dispatch<false>(x, w, out, out_dtype, M, N, K, ldx, ldw, ldo, pair_rows, &fuse, stream);
 }
 
@@ -423,9 +427,9 @@ TTB_EXPORT int ttb_gemv_mma_fused(const void* x, const float* norm_weight, float
 // x [M <= 8, K], w [(heads + 2 kv_heads) * head_dim, K] (queries, keys, values stacked), bfloat16;
 // q_out [M, heads * head_dim] gets the rotated queries; rotated keys and the values go to their
 // pages. head_dim a multiple of 16, full rotary (every pair of a head is rotated).
-// norm_weight != null: x is the float32 residual stream and the projection is taken of its RMS norm.
-TTB_EXPORT int ttb_gemv_qkv_rope(const void* x, const float* norm_weight, float eps, const void* w, void* q_out, int M,
-                                 int K, int ldx, int ldw,
+// ssq_in != null: x is g * residual and the projection is divided by the rows' RMS (see above).
+TTB_EXPORT int ttb_gemv_qkv_rope(const void* x, const float* ssq_in, int ssq_parts, float eps, const void* w, void* q_out,
+                                 int M, int K, int ldx, int ldw,
                                  const int* positions, const int* seg_of_token, const float* inv_freq, int heads,
                                  int kv_heads, int head_dim, void* key_pages, void* value_pages,
                                  const int* block_table, int table_width, int page_size, int num_pages, int write_kv,
@@ -433,14 +437,14 @@ TTB_EXPORT int ttb_gemv_qkv_rope(const void* x, const float* norm_weight, float 
     if (M == 0) return TTB_OK;
     if (!x || !w || !q_out || !positions || !inv_freq || !status) return TTB_ERR_ARGUMENT;
     if (write_kv && (!seg_of_token || !key_pages || !value_pages || !block_table)) return TTB_ERR_ARGUMENT;
-    if (M > 8 || K < 8 || (K & 7) || (ldw & 7) || !aligned16(x) || !aligned16(w)) return TTB_ERR_UNSUPPORTED;
-    if (norm_weight ? ((ldx & 3) || !aligned16(norm_weight)) : (ldx & 7)) return TTB_ERR_UNSUPPORTED;
+    if (ssq_in && ssq_parts < 1) return TTB_ERR_ARGUMENT;
+    if (M > 8 || K < 8 || (K & 7) || (ldx & 7) || (ldw & 7) || !aligned16(x) || !aligned16(w)) return TTB_ERR_UNSUPPORTED;
     if (head_dim < 16 || (head_dim & 15)) return TTB_ERR_UNSUPPORTED;
     GmRope rope = {positions, seg_of_token, inv_freq, block_table, (__nv_bfloat16*)key_pages, (__nv_bfloat16*)value_pages,
                    status, table_width, page_size, num_pages, heads, kv_heads, head_dim, write_kv};
-    GmFuse fuse = {norm_weight, eps, nullptr, 0};
+    GmFuse fuse = {ssq_in, ssq_parts, eps, nullptr, 0, nullptr, nullptr, 0, nullptr};
     const int N = (heads + 2 * kv_heads) * head_dim;
-    if (norm_weight)
+    if (ssq_in)
         return gemv_mma_launch<1, 1, GM_ROPE, 8, __nv_bfloat16, true>(x, w, q_out, M, N, K, ldx, ldw, heads * head_dim,
                                                                       head_dim / 2, stream, &rope, &fuse);
     return gemv_mma_launch<1, 1, GM_ROPE, 8, __nv_bfloat16>(x, w, q_out, M, N, K, ldx, ldw, heads * head_dim,

@@ -154,7 +154,8 @@ class Engine:
             buf[start + real * W:start + R * W] = 0
         layout = dict(T=T, R=R, N=N, W=W, o_tok=o_tok, o_pos=o_pos, o_seg=o_seg, o_cu=o_cu, o_p0=o_p0, o_slot=o_slot,
                       o_want=o_want, o_tab=o_tab, total=total, groups=groups)
-        lists = dict(seg_lens=seg_lens_all, seg_pos0=pos0_all, seg_slot=slot_all, max_context=max_context)
+        lists = dict(seg_lens=seg_lens_all, seg_pos0=pos0_all, seg_slot=slot_all, max_context=max_context,
+                     wants_every_row=want_rows == list(range(T)))
         return host, layout, lists
 
     def _batch_from(self, dev: torch.Tensor, layout: dict, lists: dict) -> StepBatch:
@@ -168,6 +169,7 @@ class Engine:
             want_rows=dev[L["o_want"]:L["o_want"] + N], num_wanted=N,
             seg_lens=lists["seg_lens"], seg_pos0_list=lists["seg_pos0"], seg_slot_list=lists["seg_slot"],
             max_seg_len=max(lists["seg_lens"]), max_context=lists["max_context"],
+            wants_every_row=lists.get("wants_every_row", False),
         )
         for i, g in enumerate(L["groups"]):
             start = L["o_tab"] + i * _round4(R * W)

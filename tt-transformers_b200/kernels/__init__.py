@@ -74,7 +74,7 @@ class CudaKernels:
         for name in ("ttb_embedding", "ttb_add_rmsnorm", "ttb_swiglu", "ttb_gather_rows", "ttb_rope_kv_write",
                      "ttb_paged_attention_generic", "ttb_gemm_simt", "ttb_gemv", "ttb_sample",
                      "ttb_paged_attention_mma", "ttb_attention_mma_tile_rows", "ttb_attention_mma_supports",
-                     "ttb_gemv_mma", "ttb_gemv_mma_fused", "ttb_argmax", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm",
+                     "ttb_gemv_mma", "ttb_gemv_mma_fused", "ttb_gemv_mma_parts", "ttb_argmax", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm",
                      "ttb_gemm_tcgen05", "ttb_paged_attention_tcgen05", "ttb_attention_tcgen05_supports",
                      "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge", "ttb_gemv_qkv_rope"):
             getattr(self.lib, name).restype = ctypes.c_int
@@ -92,7 +92,8 @@ class CudaKernels:
         # decode steps (up to 16 query rows per segment and KV head): the transposed-product kernel with TMA
         # loads of attention_decode.cu (False: the decode shape of the mma.sync kernel)
         self.use_tma_decode = os.environ.get("TTB200_TMA_DECODE", "1") == "1"
-        # skinny products take the norm before them and the residual add after them into their own kernel
+        # skinny products take the residual add after them into their epilogue (fuse_add) and prepare the norm
+        # that follows there, which the next skinny product finishes (fuse_norm)
         self.fuse_norm = os.environ.get("TTB200_FUSE_NORM", "0") == "1"
         self.fuse_add = os.environ.get("TTB200_FUSE_ADD", "0") == "1"
         # bfloat16 products with more rows than the skinny kernel takes: the TMA + tcgen05 kernel of
@@ -178,48 +179,59 @@ class CudaKernels:
         return out
 
     # ------------------------------------------------------------------ matrix products
-    def defers_norm(self, residual: torch.Tensor, dtype: torch.dtype) -> bool:
-        """Whether a norm over these residual rows may be left to the product that follows it."""
-        return (self.fuse_norm and dtype == torch.bfloat16 and residual.dtype == torch.float32
-                and residual.shape[0] <= self.TENSOR_SKINNY_ROWS and residual.shape[1] % 8 == 0
-                and residual.stride(1) == 1 and residual.stride(0) % 4 == 0)
-
-    def _skinny_fused(self, norm, x, w, out, out_dtype, M, N, K, pair_rows, accumulate, what):
-        """The tensor-core skinny product with a deferred norm as its input and/or the residual stream as its output."""
-        src = norm.residual if norm is not None else x
+    def _skinny_fused(self, norm, x, w, out, out_dtype, M, N, K, pair_rows, accumulate, next_norm, what):
+        """The tensor-core skinny product with a DeferredNorm as its input and/or the residual stream as its
+        output. With next_norm (a norm part) it prepares that norm and returns the DeferredNorm for it."""
+        src = norm.xg if norm is not None else x
+        xg = ssq = None
+        if next_norm is not None:
+            weight, eps = next_norm.fusion_args()
+            xg = torch.empty(M, N, dtype=w.dtype, device=self.device)
+            ssq = torch.empty(int(self.lib.ttb_gemv_mma_parts(M, N)), 16, dtype=torch.float32, device=self.device)
         self._check(self.lib.ttb_gemv_mma_fused(
-            self._p(src), self._p(norm.weight if norm is not None else None), ctypes.c_float(norm.eps if norm is not None else 0.0),
-            self._p(w), self._p(out), _dtype_code(out_dtype), M, N, K, src.stride(0), w.stride(0), N, pair_rows,
-            self._p(accumulate), accumulate.stride(0) if accumulate is not None else 0, self._stream()), what)
+            self._p(src), self._p(norm.ssq if norm is not None else None), norm.ssq.shape[0] if norm is not None else 0,
+            ctypes.c_float(norm.eps if norm is not None else 0.0), self._p(w), self._p(out), _dtype_code(out_dtype),
+            M, N, K, src.stride(0), w.stride(0), N, pair_rows, self._p(accumulate),
+            accumulate.stride(0) if accumulate is not None else 0, self._p(weight if next_norm is not None else None),
+            self._p(xg), N, self._p(ssq), self._stream()), what)
+        if next_norm is None:
+            return None
+        dtype = w.dtype
+        return DeferredNorm(xg, ssq, eps, next_norm,
+                            lambda: self.add_rmsnorm(accumulate, None, next_norm.weight, eps, dtype))
 
-    def linear(self, x, w: torch.Tensor, out_dtype: Optional[torch.dtype] = None, accumulate: torch.Tensor = None):
+    def linear(self, x, w: torch.Tensor, out_dtype: Optional[torch.dtype] = None, accumulate: torch.Tensor = None,
+               next_norm=None):
         """x [M, K] times w [N, K] transposed -> [M, N]. x may be a DeferredNorm. With `accumulate` (the float32
         residual stream [M, N]) the product may be added there instead of being returned: ADDED comes back then,
-        else the product as usual (the caller adds it)."""
+        or, with next_norm (the norm part that follows), a DeferredNorm made for it; else the product as usual
+        (the caller adds it)."""
         norm = None
         if isinstance(x, DeferredNorm):
-            if (w.dtype == torch.bfloat16 and x.shape[0] <= self.TENSOR_SKINNY_ROWS and w.stride(1) == 1
-                    and w.stride(0) % 8 == 0 and w.shape[1] == x.shape[1]):
-                norm = x
+            if (self.fuse_norm and w.dtype == torch.bfloat16 and x.shape[0] <= self.TENSOR_SKINNY_ROWS
+                    and w.stride(1) == 1 and w.stride(0) % 8 == 0 and w.shape[1] == x.shape[1]
+                    and x.xg.dtype == torch.bfloat16 and x.xg.stride(1) == 1 and x.xg.stride(0) % 8 == 0):
+                norm, x = x, x.xg
             else:
                 x = x.materialize()
         M, K = x.shape
         N = w.shape[0]
-        in_dtype = w.dtype if norm is not None else x.dtype
-        out_dtype = out_dtype or in_dtype
-        if w.shape[1] != K or in_dtype != w.dtype:
-            raise KernelError(f"linear: x {tuple(x.shape)} {in_dtype} does not match w {tuple(w.shape)} {w.dtype}")
-        if norm is None and (x.stride(1) != 1 or w.stride(1) != 1):
+        out_dtype = out_dtype or x.dtype
+        if w.shape[1] != K or x.dtype != w.dtype:
+            raise KernelError(f"linear: x {tuple(x.shape)} {x.dtype} does not match w {tuple(w.shape)} {w.dtype}")
+        if x.stride(1) != 1 or w.stride(1) != 1:
             raise KernelError("linear: operands must be contiguous along K")
-        skinny = (in_dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS and K % 8 == 0 and w.stride(0) % 8 == 0
-                  and (norm is not None or x.stride(0) % 8 == 0))
-        if skinny:
+        if (x.dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS and K % 8 == 0 and x.stride(0) % 8 == 0
+                and w.stride(0) % 8 == 0):
             fuse_add = (accumulate is not None and self.fuse_add and accumulate.dtype == torch.float32
                         and accumulate.shape == (M, N) and accumulate.stride(1) == 1)
             if norm is not None or fuse_add:
                 out = None if fuse_add else torch.empty(M, N, dtype=out_dtype, device=self.device)
-                self._skinny_fused(norm, x, w, out, out_dtype, M, N, K, 0, accumulate if fuse_add else None, "gemv_mma_fused")
-                return ADDED if fuse_add else out
+                prepared = self._skinny_fused(norm, x, w, out, out_dtype, M, N, K, 0, accumulate if fuse_add else None,
+                                              next_norm if (fuse_add and self.fuse_norm) else None, "gemv_mma_fused")
+                if not fuse_add:
+                    return out
+                return prepared if prepared is not None else ADDED
             out = torch.empty(M, N, dtype=out_dtype, device=self.device)
             self._check(self.lib.ttb_gemv_mma(self._p(x), self._p(w), self._p(out), _dtype_code(out_dtype), M, N, K,
                                               x.stride(0), w.stride(0), N, 0, self._stream()), "gemv_mma")
@@ -255,10 +267,12 @@ class CudaKernels:
         if isinstance(x, DeferredNorm):
             M, K = x.shape
             inter = w_gate_up.shape[0] // 2
-            if (w_gate_up.dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS and w_gate_up.shape[1] == K
-                    and w_gate_up.stride(1) == 1 and w_gate_up.stride(0) % 8 == 0):
+            if (self.fuse_norm and w_gate_up.dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS
+                    and w_gate_up.shape[1] == K and w_gate_up.stride(1) == 1 and w_gate_up.stride(0) % 8 == 0
+                    and x.xg.dtype == torch.bfloat16 and x.xg.stride(1) == 1 and x.xg.stride(0) % 8 == 0):
                 out = torch.empty(M, inter, dtype=w_gate_up.dtype, device=self.device)
-                self._skinny_fused(x, None, w_gate_up, out, w_gate_up.dtype, M, inter, K, inter, None, "gemv_mma_norm_swiglu")
+                self._skinny_fused(x, None, w_gate_up, out, w_gate_up.dtype, M, inter, K, inter, None, None,
+                                   "gemv_mma_norm_swiglu")
                 return out
             x = x.materialize()
         M, K = x.shape
@@ -286,16 +300,18 @@ class CudaKernels:
         apply (then the caller runs the three steps one by one)."""
         M, K = x.shape
         norm = x if isinstance(x, DeferredNorm) else None
-        src = norm.residual if norm is not None else x
+        if norm is not None and not self.fuse_norm:
+            return None
+        src = norm.xg if norm is not None else x
         if not (w_qkv.dtype == torch.bfloat16 and M <= 8 and K % 8 == 0 and src.stride(1) == 1
-                and (norm is not None or (x.dtype == torch.bfloat16 and x.stride(0) % 8 == 0))
+                and src.dtype == torch.bfloat16 and src.stride(0) % 8 == 0
                 and w_qkv.stride(1) == 1 and w_qkv.stride(0) % 8 == 0 and inv_freq is not None
                 and rotary_dim == head_dim and head_dim % 16 == 0 and view is not None
                 and view.keys.dtype == torch.bfloat16 and view.keys.is_contiguous() and view.values.is_contiguous()):
             return None
         q = torch.empty(M, heads * head_dim, dtype=w_qkv.dtype, device=self.device)
         self._check(self.lib.ttb_gemv_qkv_rope(
-            self._p(src), self._p(norm.weight if norm is not None else None),
+            self._p(src), self._p(norm.ssq if norm is not None else None), norm.ssq.shape[0] if norm is not None else 0,
             ctypes.c_float(norm.eps if norm is not None else 0.0), self._p(w_qkv), self._p(q), M, K, src.stride(0),
             w_qkv.stride(0), self._p(batch.positions),
             self._p(batch.seg_of_token), self._p(inv_freq), heads, kv_heads, head_dim, self._p(view.keys),

@@ -52,7 +52,7 @@ class Attention(Mixer):
     fuses_norm = True
     fuses_residual = True
 
-    def forward(self, x, batch, cache, write_cache=True, residual=None):
+    def forward(self, x, batch, cache, write_cache=True, residual=None, next_norm=None):
         k = self.runtime.kernels
         rotation = self.position.rotation() if self.position is not None else None
         inv_freq, rotary_dim = rotation if rotation is not None else (None, 0)
@@ -65,7 +65,8 @@ class Attention(Mixer):
             k.rope_kv_write(qkv, batch, inv_freq, rotary_dim, self.heads, self.kv_heads, self.head_dim, cache, write_cache)
         mixed = k.paged_attention(qkv, batch, self.heads, self.kv_heads, self.head_dim, self.scale, cache)
         if residual is not None:
-            return k.linear(mixed, self.w_o, accumulate=residual)      # ADDED, or the product where that is not fused
+            # ADDED or a DeferredNorm where the product's epilogue takes the add, else the product itself
+            return k.linear(mixed, self.w_o, accumulate=residual, next_norm=next_norm)
         return k.linear(mixed, self.w_o)
 
 

@@ -105,24 +105,27 @@ class StepBatch:
     seg_slot_list: List[int] = field(default_factory=list)
     max_seg_len: int = 1
     max_context: int = 1          # the largest pos0 + len over the segments
+    wants_every_row: bool = False  # want_rows is 0, 1, .. num_tokens-1
     block_tables: Dict[int, torch.Tensor] = field(default_factory=dict)  # group index -> [R, W]
     extras: dict = field(default_factory=dict)   # per-step tables that kernels derive once and reuse in every layer
 
 
 class DeferredNorm:
-    """A norm that has been asked for but not computed: the float32 residual rows, the norm's
-    float32 weight and eps. A kernel that can take the norm into its own loads (a skinny matrix
-    product reads the residual stream, scales by the weight and divides its sums by the rows'
-    RMS) accepts this in place of the normalised tensor; everything else calls materialize()."""
+    """A norm whose scaling is still to come. The product that ended the sub-layer before it has
+    left `xg` = compute-dtype(g * residual) [rows, width], g being the norm's weight, and `ssq`
+    [parts, 16] float32, partial sums of residual^2 per row; the norm's output is
+    xg / sqrt(sum(ssq) / width + eps). A skinny matrix product takes this in place of the normalised
+    tensor (it divides its sums instead of its input); everything else calls materialize().
+    `made_for`: the norm part whose weight and eps went in."""
 
-    __slots__ = ("residual", "weight", "eps", "_materialize")
+    __slots__ = ("xg", "ssq", "eps", "made_for", "_materialize")
 
-    def __init__(self, residual, weight, eps, materialize):
-        self.residual, self.weight, self.eps, self._materialize = residual, weight, float(eps), materialize
+    def __init__(self, xg, ssq, eps, made_for, materialize):
+        self.xg, self.ssq, self.eps, self.made_for, self._materialize = xg, ssq, float(eps), made_for, materialize
 
     @property
     def shape(self):
-        return self.residual.shape
+        return self.xg.shape
 
     def materialize(self):
         return self._materialize()
@@ -142,7 +145,8 @@ ADDED = _Added()
 class Part:
     """Base of all parts. Two optional capabilities, off unless a part says otherwise:
     `fuses_norm`: forward() accepts a DeferredNorm in place of x; `fuses_residual`: forward()
-    accepts residual=<float32 stream> and may add its output there and return ADDED."""
+    accepts residual=<float32 stream> and next_norm=<the norm part that follows, or None>, may add
+    its output to the stream itself and then returns ADDED, or a DeferredNorm made for next_norm."""
 
     fuses_norm = False
     fuses_residual = False
@@ -180,8 +184,9 @@ class FeedForward(Part):
 class Norm(Part):
     """forward_add(residual, delta) adds delta (or nothing, if None) into the
     float32 residual stream in place and returns the normalised tensor in the
-    compute dtype. A norm with `can_defer` also takes defer=True and may then
-    return a DeferredNorm when there is nothing to add."""
+    compute dtype. delta may be ADDED (nothing left to add). A norm with `can_defer`
+    has fusion_args() -> (float32 weight, eps), accepts a DeferredNorm made for it as delta and,
+    with defer=True, may hand it on instead of a tensor."""
 
     can_defer = False
 

@@ -32,11 +32,12 @@ class SwiGLU(FeedForward):
     fuses_norm = True
     fuses_residual = True
 
-    def forward(self, x, batch, residual=None):
+    def forward(self, x, batch, residual=None, next_norm=None):
         k = self.runtime.kernels
         h = k.linear_swiglu(x, self.w_gate_up)
         if residual is not None:
-            return k.linear(h, self.w_down, accumulate=residual)       # ADDED, or the product where that is not fused
+            # ADDED or a DeferredNorm where the product's epilogue takes the add, else the product itself
+            return k.linear(h, self.w_down, accumulate=residual, next_norm=next_norm)
         return k.linear(h, self.w_down)
 
 

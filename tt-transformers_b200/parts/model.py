@@ -17,7 +17,7 @@ from typing import Dict, List, Optional
 
 import torch
 
-from .base import ADDED, PartSpec, Runtime, StepBatch, TensorSpec, build_part
+from .base import ADDED, DeferredNorm, PartSpec, Runtime, StepBatch, TensorSpec, build_part
 from .embedding import Embedding, Head
 
 
@@ -132,19 +132,36 @@ class DecoderModel:
         if self.input_position is not None:
             x = self.input_position.embed(x, batch)
         delta = None
-        for i, call in enumerate(self.spec.order):
+        order = self.spec.order
+        for i, call in enumerate(order):
             owner = i if call.cache_of is None else call.cache_of
-            x, delta = self.layers[call.layer].forward(x, delta, batch, cache.view(owner, batch),
-                                                       write_cache=call.cache_of is None)
+            block = self.layers[call.layer]
+            view = cache.view(owner, batch)
+            if getattr(block, "takes_next_norm", False):
+                # the norm that will run on this block's result, if what follows it can take it half done
+                if i + 1 < len(order):
+                    nxt = self.layers[order[i + 1].layer]
+                    norm, consumer = getattr(nxt, "norm1", None), getattr(nxt, "mixer", None)
+                else:
+                    norm, consumer = self.final_norm, self.head
+                    if not batch.wants_every_row:
+                        norm = None              # the head sees a selection of the rows
+                ok = (norm is not None and getattr(norm, "can_defer", False) and getattr(consumer, "fuses_norm", False))
+                x, delta = block.forward(x, delta, batch, view, write_cache=call.cache_of is None,
+                                         next_norm=norm if ok else None)
+            else:
+                if delta is ADDED or isinstance(delta, DeferredNorm):
+                    delta = None
+                x, delta = block.forward(x, delta, batch, view, write_cache=call.cache_of is None)
         if batch.num_wanted == 0:
             return torch.empty(0, self.spec.vocab_size, dtype=torch.float32, device=x.device)
-        x = k.gather_rows(x, batch.want_rows)
-        if delta is ADDED:
+        if isinstance(delta, DeferredNorm) and delta.made_for is self.final_norm and batch.wants_every_row:
+            return self.head.forward(self.final_norm.forward_add(x, delta, defer=True))
+        if delta is ADDED or isinstance(delta, DeferredNorm):
             delta = None
-        if delta is not None:
-            delta = k.gather_rows(delta, batch.want_rows)
-        if getattr(self.final_norm, "can_defer", False) and getattr(self.head, "fuses_norm", False):
-            h = self.final_norm.forward_add(x, delta, defer=True)
-        else:
-            h = self.final_norm.forward_add(x, delta)
+        if not batch.wants_every_row:
+            x = k.gather_rows(x, batch.want_rows)
+            if delta is not None:
+                delta = k.gather_rows(delta, batch.want_rows)
+        h = self.final_norm.forward_add(x, delta)
         return self.head.forward(h)

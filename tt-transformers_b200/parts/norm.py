@@ -7,7 +7,7 @@ as well and is written back to the residual stream.
 
 from __future__ import annotations
 
-from .base import DeferredNorm, Norm, TensorSpec, register_part
+from .base import ADDED, DeferredNorm, Norm, TensorSpec, register_part
 
 
 class RMSNorm(Norm):
@@ -24,15 +24,22 @@ class RMSNorm(Norm):
         self.weight = runtime.vector(tensors[self.weight_name])
         self._weight_f32 = None
 
+    def fusion_args(self):
+        """What a product needs to prepare this norm in its epilogue: the weight in float32 and eps."""
+        if self._weight_f32 is None:
+            self._weight_f32 = self.weight.float().contiguous()
+        return self._weight_f32, self.eps
+
     def forward_add(self, residual, delta, defer=False):
-        """defer: the caller's next step can take the norm into its own kernel. With nothing to add
-        and rows few enough for such a kernel, no kernel runs here."""
+        """defer: the caller's next step takes a DeferredNorm. If the sub-layer before has prepared this
+        norm (delta is a DeferredNorm made for it), no kernel runs here."""
         k = self.runtime.kernels
-        if defer and delta is None and getattr(k, "defers_norm", None) and k.defers_norm(residual, self.runtime.dtype):
-            if self._weight_f32 is None:
-                self._weight_f32 = self.weight.float().contiguous()
-            return DeferredNorm(residual, self._weight_f32, self.eps,
-                                lambda: k.add_rmsnorm(residual, None, self.weight, self.eps, self.runtime.dtype))
+        if isinstance(delta, DeferredNorm):
+            if delta.made_for is self:
+                return delta if defer else delta.materialize()
+            delta = None                         # prepared for another norm: the stream itself is up to date
+        if delta is ADDED:
+            delta = None
         return k.add_rmsnorm(residual, delta, self.weight, self.eps, self.runtime.dtype)
 
 
