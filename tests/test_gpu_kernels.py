@@ -237,6 +237,7 @@ DECODE_CASES = [
     (8, 2, 64, 16, [(500, 1), (99, 1), (100, 1), (101, 2), (10, 1)], 100),         # windows
     (4, 1, 128, 32, [(2000, 1), (300, 3)], 257),
     (8, 4, 64, 256, [(1000, 1), (255, 1), (256, 1)], 300),
+    (4, 2, 64, 16, [(20000, 1), (16383, 1), (16384, 2)], None),                    # more pages than a block keeps in shared memory
 ]
 
 
