@@ -8,7 +8,7 @@
 // Page layout: [num_pages, kv_heads, page_size, head_dim].
 #include "common.cuh"
 
-template <typename T>
+template <typename T, bool VEC>
 __global__ void rope_kv_write_kernel(T* __restrict__ qkv, const int* __restrict__ positions,
                                      const int* __restrict__ seg_of_token, const float* __restrict__ inv_freq,
                                      int rotary_dim, int heads, int kv_heads, int head_dim,
@@ -33,6 +33,54 @@ __global__ void rope_kv_write_kernel(T* __restrict__ qkv, const int* __restrict_
     T* row = qkv + (size_t)t * (heads + 2 * kv_heads) * head_dim;
     const int half = head_dim / 2;
 
+    if constexpr (VEC) {
+        // Every pair of a head is rotated (rotary_dim == head_dim), head_dim is a multiple of 16 and rows and
+        // pages are 16-byte aligned: a work item is eight consecutive elements i .. i+7 and their partners
+        // i + half .., moved as two 16-byte words each way. Items: heads of q, then of k, then of v.
+        constexpr int E = 16 / (int)sizeof(T);                  // elements in 16 bytes
+        const int per_head = half / E;
+        int page = -1, in_page = 0;
+        if (write_kv) {
+            const int page_index = pos / page_size;
+            if (page_index >= table_width) {
+                if (threadIdx.x == 0) atomicExch(status, 0x1000000 + t);
+            } else {
+                page = block_table[(size_t)seg_of_token[t] * table_width + page_index];
+                if (page < 0 || page >= num_pages) {
+                    if (threadIdx.x == 0) atomicExch(status, 0x2000000 + t);
+                    page = -1;
+                }
+                in_page = pos - page_index * page_size;
+            }
+        }
+        const int items = (heads + (write_kv ? 2 * kv_heads : 0)) * per_head;
+        for (int w = threadIdx.x; w < items; w += blockDim.x) {
+            const int h = w / per_head, i = (w - h * per_head) * E;      // h counts q heads, then k heads, then v heads
+            const T* src = row + (size_t)h * head_dim;
+            uint4 lo = *reinterpret_cast<const uint4*>(src + i), hi = *reinterpret_cast<const uint4*>(src + i + half);
+            T* dst;
+            if (h < heads) {
+                dst = row + (size_t)h * head_dim;
+            } else {
+                if (page < 0) continue;
+                const int g = (h - heads) % kv_heads;
+                dst = (h - heads < kv_heads ? key_pages : value_pages) + (((size_t)page * kv_heads + g) * page_size + in_page) * head_dim;
+            }
+            if (h < heads + kv_heads) {                                   // queries and keys are rotated
+                T* a = reinterpret_cast<T*>(&lo);
+                T* b = reinterpret_cast<T*>(&hi);
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    const float x = to_float(a[e]), y = to_float(b[e]);
+                    const float c = trig[i + e], sn = trig[half_rot + i + e];
+                    a[e] = from_float<T>(x * c - y * sn);
+                    b[e] = from_float<T>(y * c + x * sn);
+                }
+            }
+            *reinterpret_cast<uint4*>(dst + i) = lo;
+            *reinterpret_cast<uint4*>(dst + i + half) = hi;
+        }
+    } else {
     // queries: rotate in place
     for (int w = threadIdx.x; w < heads * half; w += blockDim.x) {
         const int h = w / half, i = w - h * half;
@@ -83,6 +131,7 @@ __global__ void rope_kv_write_kernel(T* __restrict__ qkv, const int* __restrict_
             key_pages[dst + i] = k_row[g * head_dim + i];
         }
     }
+    }
 }
 
 TTB_EXPORT int ttb_rope_kv_write(void* qkv, int dtype, const int* positions, const int* seg_of_token,
@@ -98,13 +147,25 @@ TTB_EXPORT int ttb_rope_kv_write(void* qkv, int dtype, const int* positions, con
     if (rotary_dim > 0 && !inv_freq) return TTB_ERR_ARGUMENT;
     const int threads = 256;
     const size_t smem = (size_t)(rotary_dim > 0 ? rotary_dim : 2) * sizeof(float);
-    if (dtype == TTB_DTYPE_BF16)
-        ttb_launch(rope_kv_write_kernel<__nv_bfloat16>, tokens, threads, smem, stream,
+    const int elem = dtype == TTB_DTYPE_BF16 ? 2 : 4;
+    const bool vec = rotary_dim == head_dim && head_dim % (32 / elem) == 0 && aligned16(qkv) &&
+                     (!write_kv || (aligned16(key_pages) && aligned16(value_pages)));
+    if (vec && dtype == TTB_DTYPE_BF16)
+        ttb_launch(rope_kv_write_kernel<__nv_bfloat16, true>, tokens, threads, smem, stream,
+            (__nv_bfloat16*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
+            (__nv_bfloat16*)key_pages, (__nv_bfloat16*)value_pages, block_table, table_width, page_size, num_pages,
+            write_kv, status);
+    else if (vec && dtype == TTB_DTYPE_F32)
+        ttb_launch(rope_kv_write_kernel<float, true>, tokens, threads, smem, stream,
+            (float*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
+            (float*)key_pages, (float*)value_pages, block_table, table_width, page_size, num_pages, write_kv, status);
+    else if (dtype == TTB_DTYPE_BF16)
+        ttb_launch(rope_kv_write_kernel<__nv_bfloat16, false>, tokens, threads, smem, stream,
             (__nv_bfloat16*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
             (__nv_bfloat16*)key_pages, (__nv_bfloat16*)value_pages, block_table, table_width, page_size, num_pages,
             write_kv, status);
     else if (dtype == TTB_DTYPE_F32)
-        ttb_launch(rope_kv_write_kernel<float>, tokens, threads, smem, stream,
+        ttb_launch(rope_kv_write_kernel<float, false>, tokens, threads, smem, stream,
             (float*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
             (float*)key_pages, (float*)value_pages, block_table, table_width, page_size, num_pages, write_kv, status);
     else
