@@ -64,6 +64,14 @@ __device__ __forceinline__ void ad_tma_2d(uint32_t dst, const CUtensorMap* map, 
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
                  ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(bar) : "memory");
 }
+// A float at the same shared-memory offset in the block of rank `rank` of this cluster.
+__device__ __forceinline__ float ad_ld_cluster(uint32_t local_addr, int rank) {
+    uint32_t remote;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
 __device__ __forceinline__ void ad_ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
@@ -107,7 +115,7 @@ attention_decode_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_
                         const int* __restrict__ block_table, int table_width, int page_size, int page_shift,
                         int heads, int kv_heads, float scale_log2, int window, int num_splits,
                         float* __restrict__ partial_o, float* __restrict__ partial_ml, int num_pages,
-                        int* __restrict__ status, int* __restrict__ error_flag) {
+                        int* __restrict__ status, int* __restrict__ error_flag, int cluster_merge) {
     constexpr int ROWS = 8 * NT;                 // query rows of the tile
     constexpr int CHUNKS = HD / 8;               // 16-byte chunks per row
     constexpr int HALVES = HD / 64;
@@ -374,6 +382,12 @@ attention_decode_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_
             }
     }
     __syncthreads();
+    // With key splits and cluster_merge, the blocks of one (segment, KV head) are one thread-block cluster:
+    // each leaves its result in its own shared memory and the rows are finished by reading the others'
+    // through distributed shared memory; no partial results in global memory and no merge kernel.
+    float* blk_o = merge_ml + AD_CONSUMERS * ROWS * 2;                          // [ROWS][HD]
+    float* blk_ml = blk_o + ROWS * HD;                                          // [ROWS][2]
+    const bool in_cluster = num_splits > 1 && cluster_merge != 0;
     for (int idx = tid; idx < ROWS * HD; idx += AD_THREADS) {
         const int r = idx / HD, c = idx % HD;
         if (r >= valid_rows) continue;
@@ -390,13 +404,42 @@ attention_decode_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_
         }
         const int token = r / rep, head = kvh * rep + r % rep;
         const size_t row_index = (size_t)(seg_start + token) * heads + head;
-        if (num_splits > 1) {
+        if (in_cluster) {
+            blk_o[r * HD + c] = o;
+            if (c == 0) { blk_ml[r * 2] = m; blk_ml[r * 2 + 1] = sum; }
+        } else if (num_splits > 1) {
             const size_t slot = row_index * num_splits + split;
             partial_o[slot * HD + c] = o;
             if (c == 0) { partial_ml[slot * 2] = m; partial_ml[slot * 2 + 1] = sum; }
         } else {
             out[row_index * HD + c] = __float2bfloat16_rn(sum > 0.f ? o / sum : 0.f);
         }
+    }
+    if (in_cluster) {
+        // every thread of every block of the cluster comes here (the early return above is taken by all of a
+        // cluster's blocks or by none: they share the segment)
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        // row r is finished by the block of rank r mod num_splits
+        for (int r = split; r < valid_rows; r += num_splits) {
+            const int token = r / rep, head = kvh * rep + r % rep;
+            const size_t row_index = (size_t)(seg_start + token) * heads + head;
+            for (int c = tid; c < HD; c += AD_THREADS) {
+                const uint32_t ml_local = ad_smem(blk_ml + r * 2), o_local = ad_smem(blk_o + r * HD + c);
+                float m = -INFINITY;
+                for (int s2 = 0; s2 < num_splits; ++s2) m = fmaxf(m, ad_ld_cluster(ml_local, s2));
+                float sum = 0.f, o = 0.f;
+                for (int s2 = 0; s2 < num_splits; ++s2) {
+                    const float ms = ad_ld_cluster(ml_local, s2);
+                    if (ms == -INFINITY) continue;
+                    const float f = exp2f(ms - m);
+                    sum += f * ad_ld_cluster(ml_local + 4, s2);
+                    o += f * ad_ld_cluster(o_local, s2);
+                }
+                out[row_index * HD + c] = __float2bfloat16_rn(sum > 0.f ? o / sum : 0.f);
+            }
+        }
+        // nobody leaves while its shared memory may still be read
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
     }
 }
 
@@ -431,6 +474,40 @@ TTB_EXPORT int ttb_attention_decode_supports(int heads, int kv_heads, int head_d
 // Blocks that fit one SM at a time (by shared memory): what the host sizes key splits by.
 TTB_EXPORT int ttb_attention_decode_blocks_per_sm(int head_dim) { return head_dim == 64 ? 3 : 2; }
 
+extern "C" int ttb_attention_merge(const float* partial_o, const float* partial_ml, void* out, int rows, int num_splits,
+                                   int head_dim, cudaStream_t stream);
+
+// Key splits up to this many are merged inside the kernel by a thread-block cluster (16 is the most the
+// hardware takes, with the opt-in below); TTB200_CLUSTER_MERGE=0 in the environment turns it off.
+#define AD_MAX_CLUSTER 16
+static int ad_cluster_limit() {
+    static int limit = -1;
+    if (limit < 0) {
+        const char* e = getenv("TTB200_CLUSTER_MERGE");
+        limit = (e && e[0] == '0') ? 0 : AD_MAX_CLUSTER;
+    }
+    return limit;
+}
+
+static int ad_sm_count() {
+    static int count = 0;
+    if (count == 0) {
+        int device = 0;
+        cudaGetDevice(&device);
+        cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
+        if (count <= 0) count = 1;
+    }
+    return count;
+}
+
+// Whether a call with this many key splits and blocks (segments x KV heads x splits) needs no partial results
+// and no merge kernel. Clusters are placed as a whole, which costs occupancy once the grid is larger than the
+// GPU: measured at Llama 3.2 1B geometry and 8,192 keys, the step is 2 to 3 % faster with them at batch 1 and 2
+// (128 and 256 blocks) and 5 to 12 % slower at batch 4, 8 and 64 (416 blocks and more).
+TTB_EXPORT int ttb_attention_decode_merges_in_kernel(int num_splits, int blocks) {
+    return num_splits > 1 && num_splits <= ad_cluster_limit() && blocks <= 2 * ad_sm_count();
+}
+
 template <int HD, int NT, int STAGES>
 static int launch_attention_decode(const CUtensorMap& map_k, const CUtensorMap& map_v, const void* qkv, int q_row_stride,
                                    void* out, const int* cu_seqlens, const int* seg_pos0, const int* block_table,
@@ -438,7 +515,7 @@ static int launch_attention_decode(const CUtensorMap& map_k, const CUtensorMap& 
                                    int window, int num_splits, float* partial_o, float* partial_ml, int num_pages,
                                    int* status, int* error_flag, cudaStream_t stream) {
     const size_t stage_bytes = (size_t)STAGES * 2 * AD_BN * HD * 2;
-    const size_t merge_bytes = (size_t)AD_CONSUMERS * 8 * NT * (HD + 2) * sizeof(float);
+    const size_t merge_bytes = (size_t)(AD_CONSUMERS + 1) * 8 * NT * (HD + 2) * sizeof(float);
     const size_t smem = 1024 + (stage_bytes > merge_bytes ? stage_bytes : merge_bytes) + (size_t)8 * NT * HD * 2 +
                         AD_TABLE_CACHE * sizeof(int) + 2 * STAGES * sizeof(uint64_t);
     auto kernel = attention_decode_kernel<HD, NT, STAGES>;
@@ -446,25 +523,51 @@ static int launch_attention_decode(const CUtensorMap& map_k, const CUtensorMap& 
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return (int)e;
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) cudaGetLastError();
         configured = true;
     }
     int page_shift = 0;
     while ((1 << page_shift) < page_size) ++page_shift;
-    ttb_launch(kernel, dim3(segments, kv_heads, num_splits), dim3(AD_THREADS), smem, stream, map_k, map_v,
-               (const __nv_bfloat16*)qkv, q_row_stride, (__nv_bfloat16*)out, cu_seqlens, seg_pos0, block_table, table_width,
-               page_size, page_shift, heads, kv_heads, scale * 1.4426950408889634f, window, num_splits, partial_o,
-               partial_ml, num_pages, status, error_flag);
+    const bool cluster = ttb_attention_decode_merges_in_kernel(num_splits, segments * kv_heads * num_splits) != 0;
+    if (!cluster && num_splits > 1 && (!partial_o || !partial_ml)) return TTB_ERR_ARGUMENT;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(segments, kv_heads, num_splits);
+    cfg.blockDim = dim3(AD_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int n_attr = 0;
+    if (ttb_pdl_enabled()) {
+        attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n_attr].val.programmaticStreamSerializationAllowed = 1;
+        ++n_attr;
+    }
+    if (cluster) {
+        attr[n_attr].id = cudaLaunchAttributeClusterDimension;
+        attr[n_attr].val.clusterDim.x = 1;
+        attr[n_attr].val.clusterDim.y = 1;
+        attr[n_attr].val.clusterDim.z = num_splits;
+        ++n_attr;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n_attr;
+    cudaLaunchKernelEx(&cfg, kernel, map_k, map_v, (const __nv_bfloat16*)qkv, q_row_stride, (__nv_bfloat16*)out, cu_seqlens,
+                       seg_pos0, block_table, table_width, page_size, page_shift, heads, kv_heads,
+                       scale * 1.4426950408889634f, window, num_splits, partial_o, partial_ml, num_pages, status, error_flag,
+                       cluster ? 1 : 0);
     return ttb_launch_status();
 }
 
 // One query tile per segment: all its tokens' heads of a KV group, max_rows = max tokens x heads / kv_heads <= 16.
 // qkv [tokens, q_row_stride] bfloat16 (queries first), pages [num_pages, kv_heads, page_size, head_dim] bfloat16.
-// With num_splits > 1: partial_o [tokens * heads * num_splits * head_dim], partial_ml [tokens * heads * num_splits * 2]
-// floats for ttb_attention_merge. status: set on a page id outside the pool; error_flag: set if a wait gave up.
+// With num_splits > 1 and not ttb_attention_decode_merges_in_kernel(num_splits, segments * kv_heads * num_splits): partial_o [tokens * heads *
+// num_splits * head_dim] and partial_ml [tokens * heads * num_splits * 2] floats of scratch memory, merged by a second
+// kernel that this call launches too. `tokens`: the rows of qkv. status: set on a page id outside the pool;
+// error_flag: set if a wait gave up.
 TTB_EXPORT int ttb_paged_attention_decode(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens,
                                           const int* seg_pos0, const void* key_pages, const void* value_pages,
                                           const int* block_table, int table_width, int page_size, int segments,
-                                          int max_rows, int heads, int kv_heads, int head_dim, float scale, int window,
+                                          int tokens, int max_rows, int heads, int kv_heads, int head_dim, float scale, int window,
                                           int num_splits, float* partial_o, float* partial_ml, int num_pages,
                                           int* status, int* error_flag, cudaStream_t stream) {
     if (segments == 0) return TTB_OK;
@@ -474,7 +577,6 @@ TTB_EXPORT int ttb_paged_attention_decode(const void* qkv, int q_row_stride, voi
     if ((q_row_stride & 7) || !aligned16(qkv) || !aligned16(key_pages) || !aligned16(value_pages)) return TTB_ERR_UNSUPPORTED;
     if (num_splits < 1 || num_splits > 65535 || kv_heads > 65535 || num_pages < 1) return TTB_ERR_UNSUPPORTED;
     if ((size_t)num_pages * kv_heads * page_size > 0x7fffffffull) return TTB_ERR_UNSUPPORTED;
-    if (num_splits > 1 && (!partial_o || !partial_ml)) return TTB_ERR_ARGUMENT;
     AdEncodeFn encode = ad_encode_fn();
     if (!encode) return TTB_ERR_UNSUPPORTED;
     CUtensorMap map_k, map_v;
@@ -491,8 +593,13 @@ TTB_EXPORT int ttb_paged_attention_decode(const void* qkv, int q_row_stride, voi
     }
 #define AD_ARGS map_k, map_v, qkv, q_row_stride, out, cu_seqlens, seg_pos0, block_table, table_width, page_size, segments, \
                 heads, kv_heads, scale, window, num_splits, partial_o, partial_ml, num_pages, status, error_flag, stream
+    int code;
     if (head_dim == 64)
-        return max_rows <= 8 ? launch_attention_decode<64, 1, 4>(AD_ARGS) : launch_attention_decode<64, 2, 4>(AD_ARGS);
-    return max_rows <= 8 ? launch_attention_decode<128, 1, 3>(AD_ARGS) : launch_attention_decode<128, 2, 3>(AD_ARGS);
+        code = max_rows <= 8 ? launch_attention_decode<64, 1, 4>(AD_ARGS) : launch_attention_decode<64, 2, 4>(AD_ARGS);
+    else
+        code = max_rows <= 8 ? launch_attention_decode<128, 1, 3>(AD_ARGS) : launch_attention_decode<128, 2, 3>(AD_ARGS);
 #undef AD_ARGS
+    if (code != TTB_OK || num_splits == 1 || ttb_attention_decode_merges_in_kernel(num_splits, segments * kv_heads * num_splits))
+        return code;
+    return ttb_attention_merge(partial_o, partial_ml, out, tokens * heads, num_splits, head_dim, stream);
 }

@@ -74,7 +74,7 @@ class CudaKernels:
         for name in ("ttb_embedding", "ttb_add_rmsnorm", "ttb_swiglu", "ttb_gather_rows", "ttb_rope_kv_write",
                      "ttb_paged_attention_generic", "ttb_gemm_simt", "ttb_gemv", "ttb_sample",
                      "ttb_paged_attention_mma", "ttb_attention_mma_tile_rows", "ttb_attention_mma_supports",
-                     "ttb_gemv_mma", "ttb_gemv_mma_fused", "ttb_gemv_mma_parts", "ttb_argmax", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm",
+                     "ttb_gemv_mma", "ttb_gemv_mma_fused", "ttb_gemv_mma_parts", "ttb_argmax", "ttb_attention_decode_merges_in_kernel", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm",
                      "ttb_gemm_tcgen05", "ttb_paged_attention_tcgen05", "ttb_attention_tcgen05_supports",
                      "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge", "ttb_gemv_qkv_rope"):
             getattr(self.lib, name).restype = ctypes.c_int
@@ -413,23 +413,25 @@ class CudaKernels:
             return self._attention_tcgen05(qkv, out, batch, heads, kv_heads, head_dim, scale, view)
         decode_shape, seg, tok0, n_tiles, splits = self._attention_plan(batch, heads // kv_heads, kv_heads, head_dim)
         partial_o = partial_ml = None
-        if splits > 1:
-            partial_o = torch.empty(tokens * heads * splits * head_dim, dtype=torch.float32, device=self.device)
-            partial_ml = torch.empty(tokens * heads * splits * 2, dtype=torch.float32, device=self.device)
         max_rows = batch.max_seg_len * (heads // kv_heads)
         if (decode_shape and self.use_tma_decode and view.keys.is_contiguous() and view.values.is_contiguous()
                 and self.lib.ttb_attention_decode_supports(heads, kv_heads, head_dim, view.page_size, max_rows)):
+            in_kernel = bool(self.lib.ttb_attention_decode_merges_in_kernel(splits, batch.num_segments * kv_heads * splits))  # a cluster merges the key splits
+            if splits > 1 and not in_kernel:
+                partial_o = torch.empty(tokens * heads * splits * head_dim, dtype=torch.float32, device=self.device)
+                partial_ml = torch.empty(tokens * heads * splits * 2, dtype=torch.float32, device=self.device)
             self._check(self.lib.ttb_paged_attention_decode(
                 self._p(qkv), qkv.stride(0), self._p(out), self._p(batch.cu_seqlens), self._p(batch.seg_pos0),
                 self._p(view.keys), self._p(view.values), self._p(view.block_table), view.block_table.shape[1],
-                view.page_size, batch.num_segments, max_rows, heads, kv_heads, head_dim, ctypes.c_float(scale),
+                view.page_size, batch.num_segments, tokens, max_rows, heads, kv_heads, head_dim, ctypes.c_float(scale),
                 int(view.window or 0), splits, self._p(partial_o), self._p(partial_ml), view.keys.shape[0],
                 self._p(self.status), self._p(self.tc_error), self._stream()), "paged_attention_decode")
-            if splits > 1:
-                self._check(self.lib.ttb_attention_merge(self._p(partial_o), self._p(partial_ml), self._p(out),
-                                                         tokens * heads, splits, head_dim, self._stream()),
-                            "attention_merge")
+            if splits > 1 and not in_kernel:
+                self.launches += 1
             return
+        if splits > 1:
+            partial_o = torch.empty(tokens * heads * splits * head_dim, dtype=torch.float32, device=self.device)
+            partial_ml = torch.empty(tokens * heads * splits * 2, dtype=torch.float32, device=self.device)
         self._check(self.lib.ttb_paged_attention_mma_checked(
             self._p(qkv), qkv.stride(0), self._p(out), self._p(batch.cu_seqlens), self._p(batch.seg_pos0),
             self._p(view.keys), self._p(view.values), self._p(view.block_table), view.block_table.shape[1],
