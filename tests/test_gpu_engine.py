@@ -49,3 +49,40 @@ def test_cuttings_match_plain(tiny_folders, dtype, name, lengths, page, cut):
     assert engine.cache.free_pages() == engine.cache.num_pages      # everything was given back
     check(got, ref, dtype)
     engine.close()
+
+
+@pytest.mark.parametrize("name,lengths,page", [("C", (150, 40), 16), ("D", (300, 45, 130, 70, 64), 16), ("B", (5, 17, 33, 90), 8)])
+@pytest.mark.parametrize("cut,graphs", [("tail", False), ("tail", True), ("mixed", True)])
+def test_sub_layers_that_add_to_the_stream_and_hand_on_a_prepared_norm(tiny_folders, name, lengths, page, cut, graphs):
+    """With the fusions of the skinny products switched on (the last product of a sub-layer adds to the residual
+    stream and prepares the next norm, the first product of the next finishes it), a decode step runs the norm
+    kernel once, after the embedding; portions of prompts take the unfused way. Same tolerance as without."""
+    from tt_transformers_b200.config import EngineConfig
+    from tt_transformers_b200.engine.step import build_engine
+
+    requests = requests_for(name, lengths)
+    ref = helpers.plain_logits(tiny_folders[name], requests)
+    steps = {"tail": helpers.steps_decode_tail, "mixed": helpers.steps_mixed}[cut](requests)
+    tokens = helpers.max_live_tokens(requests, steps, rounding=page)
+    engine = build_engine(tiny_folders[name], EngineConfig(
+        dtype="bfloat16", page_size=page, num_pages=-(-tokens // page), max_batch_size=4, max_seq_len=512,
+        max_step_tokens=4096, cuda_graph=graphs, device="cuda:0"))
+    kernels = engine.kernels
+    before = kernels.fuse_norm, kernels.fuse_add
+    plain_norm = kernels.add_rmsnorm
+    rows_normed = []
+    kernels.fuse_norm = kernels.fuse_add = True
+    kernels.add_rmsnorm = lambda *a, **kw: (rows_normed.append(a[0].shape[0]), plain_norm(*a, **kw))[1]
+    try:
+        got = helpers.run_steps(engine, steps)
+        check(got, ref, "bfloat16")
+        engine.cache.audit()
+    finally:
+        kernels.add_rmsnorm = plain_norm
+        kernels.fuse_norm, kernels.fuse_add = before
+        engine.close()
+    if not graphs:
+        decode_steps = sum(1 for s in steps if s["entries"] and all(len(e["tokens"]) == 1 for e in s["entries"]))
+        small = sum(1 for rows in rows_normed if rows <= 16)
+        # one per decode step; a prompt portion adds one more for the few rows of its wanted places
+        assert 0 < decode_steps <= small <= len(steps)
