@@ -264,7 +264,7 @@ def test_decode_attention(kernels, twin, case, tma):
     before = kernels.use_tma_decode
     kernels.use_tma_decode = tma
     try:
-        for splits in (None, 1, 3, 16, 20):         # 16: the largest cluster; 20: partial results and the merge kernel
+        for splits in (None, 1, 3, 16, 20, 40):     # 16: the largest cluster; 20, 40: partial results and the merge kernel
             batch.extras.clear()
             if splits is not None:
                 plan = kernels._attention_plan(batch, heads // kv_heads, kv_heads, head_dim)

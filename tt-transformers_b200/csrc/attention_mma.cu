@@ -369,6 +369,8 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
 }
 
 // out[row, :] = sum_s w_s O_s / sum_s w_s l_s with w_s = 2^(m_s - max m); one warp per (token, head) row.
+// Lane s holds split s's maximum and sum (splits beyond 32 in further rounds), so that the weights of all
+// splits come from two loads and a few shuffles; the partial outputs are then read eight splits at a time.
 template <int HD>
 __global__ void attention_merge_kernel(const float* __restrict__ partial_o, const float* __restrict__ partial_ml,
                                        __nv_bfloat16* __restrict__ out, int rows, int num_splits) {
@@ -377,21 +379,39 @@ __global__ void attention_merge_kernel(const float* __restrict__ partial_o, cons
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
-    const float* ml = partial_ml + (size_t)row * num_splits * 2;
+    const float2* ml = reinterpret_cast<const float2*>(partial_ml) + (size_t)row * num_splits;
     float m = -INFINITY;
-    for (int s = 0; s < num_splits; ++s) m = fmaxf(m, ml[2 * s]);
+    for (int s0 = 0; s0 < num_splits; s0 += 32) {
+        const float mine = s0 + lane < num_splits ? ml[s0 + lane].x : -INFINITY;
+        m = fmaxf(m, warp_max(mine));
+    }
     float acc[HD / 32];
 #pragma unroll
     for (int i = 0; i < HD / 32; ++i) acc[i] = 0.f;
     float sum = 0.f;
-    for (int s = 0; s < num_splits; ++s) {
-        const float ms = ml[2 * s];
-        if (ms == -INFINITY) continue;
-        const float f = exp2f(ms - m);
-        sum += f * ml[2 * s + 1];
-        const float* o = partial_o + ((size_t)row * num_splits + s) * HD;
+    for (int s0 = 0; s0 < num_splits; s0 += 32) {
+        float2 mine = make_float2(-INFINITY, 0.f);
+        if (s0 + lane < num_splits) mine = ml[s0 + lane];
+        const float f_mine = mine.x == -INFINITY ? 0.f : exp2f(mine.x - m);
+        sum += warp_sum(f_mine * mine.y);
+        const int count = min(32, num_splits - s0);
+        for (int j0 = 0; j0 < count; j0 += 8) {
+            float v[8][HD / 32];
 #pragma unroll
-        for (int i = 0; i < HD / 32; ++i) acc[i] += f * o[lane + 32 * i];
+            for (int j = 0; j < 8; ++j) {
+                const float* o = partial_o + ((size_t)row * num_splits + s0 + min(j0 + j, count - 1)) * HD;
+#pragma unroll
+                for (int i = 0; i < HD / 32; ++i) v[j][i] = o[lane + 32 * i];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float f = __shfl_sync(0xffffffffu, f_mine, min(j0 + j, count - 1));
+                if (j0 + j < count) {
+#pragma unroll
+                    for (int i = 0; i < HD / 32; ++i) acc[i] += f * v[j][i];
+                }
+            }
+        }
     }
     const float inv = sum > 0.f ? 1.f / sum : 0.f;
 #pragma unroll
