@@ -51,9 +51,42 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ residual, const TD* __res
                                    const TW* __restrict__ weight, TO* __restrict__ out, int width, float eps) {
     extern __shared__ float row[];
     __shared__ float scratch[32];
+    const size_t base = (size_t)blockIdx.x * width;
+    if (VEC && width <= (int)blockDim.x * 8) {
+        // A row in one pass (decode: a handful of rows, every microsecond of this kernel is on the step's
+        // critical path): the thread's eight values stay in registers, and the norm's weight, which no
+        // kernel writes, is fetched before the wait for the kernel before this one.
+        const int c = threadIdx.x * 8;
+        const bool mine = c < width;
+        float w[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (mine) load8(weight + c, w);
+        pdl_wait();
+        pdl_launch_dependents();
+        float sumsq = 0.f;
+        if (mine) {
+            load8(residual + base + c, v);
+            if (delta != nullptr) {
+                float d[8];
+                load8(delta + base + c, d);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] += d[e];
+                store8(residual + base + c, v);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sumsq += v[e] * v[e];
+        }
+        sumsq = block_sum(sumsq, scratch);
+        const float scale = rsqrtf(sumsq / (float)width + eps);
+        if (mine) {
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = v[e] * scale * w[e];
+            store8(out + base + c, o);
+        }
+        return;
+    }
     pdl_wait();
     pdl_launch_dependents();
-    const size_t base = (size_t)blockIdx.x * width;
     float sumsq = 0.f;
     if (VEC) {      // width a multiple of 8, all pointers 16-byte aligned: eight elements per thread and pass
         for (int c = threadIdx.x * 8; c < width; c += blockDim.x * 8) {
