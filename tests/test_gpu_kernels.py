@@ -165,6 +165,11 @@ ATTN_CASES = [
     (8, 2, 64, 16, [(0, 150), (400, 1), (90, 20)], 100),
     (32, 8, 64, 16, [(2000, 1)], None),
     (10, 2, 64, 16, [(50, 70)], None),
+    # the tcgen05 kernel at head size 128 and with heads per KV head that do not divide 128
+    (32, 8, 128, 16, [(0, 300), (1000, 37)], None),
+    (24, 8, 128, 16, [(0, 130), (700, 50), (64, 64)], None),
+    (12, 4, 64, 32, [(0, 257), (3000, 43)], None),
+    (7, 1, 128, 8, [(0, 90), (500, 30)], None),
 ]
 
 
@@ -284,6 +289,7 @@ def test_decode_attention(kernels, twin, case, tma):
     (32, 8, 64, 16, [(0, 300), (1000, 37)], None),
     (8, 2, 64, 16, [(0, 150), (90, 20)], 100),                      # a window: the mma.sync kernel
     (3, 1, 128, 16, [(0, 100), (129, 40)], None),
+    (32, 8, 128, 16, [(0, 200), (1100, 45)], None),
     (6, 3, 80, 8, [(9, 30)], 16),                                   # the kernel for any size
 ])
 def test_prompt_attention_ignores_slots_that_hold_nothing(kernels, twin, case):

@@ -1,4 +1,4 @@
-// Paged causal flash attention for prompt portions on the fifth-generation tensor cores, head size 64.
+// Paged causal flash attention for prompt portions on the fifth-generation tensor cores, head sizes 64 and 128.
 //
 // A block owns 128 query rows: 128 / (heads per KV head) tokens of one segment times the query heads of
 // one KV head, token-major, so all rows share the keys and values that are loaded. Per tile of 64 keys:
@@ -19,7 +19,9 @@
 // frees its tensor memory and returns. Rows of V beyond the last visible key are zeroed in shared memory
 // before they meet a probability of zero, so stale or poisoned cache contents never reach the output.
 //
-// Takes: head size 64; heads per KV head in {1, 2, 4, 8, 16}; page size dividing 64; no window.
+// A head of 128 is two halves of 64 columns everywhere (the 128-byte swizzle's width): Q, K and V tiles are
+// [half][rows][64], Q K^T runs over both halves' k-steps, P V is issued once per half of V into its half of O.
+// Takes: head sizes 64 and 128; up to 16 heads per KV head; page size dividing 64; no window.
 // Everything else goes to attention_mma.cu or attention_generic.cu.
 #include <cuda.h>
 
@@ -27,15 +29,14 @@
 
 #define FA_BM 128
 #define FA_BN 64
-#define FA_HD 64
-#define FA_STAGES 3
+#define FA_MAX_STAGES 3
 #define FA_THREADS 192
 #define FA_WAIT_LIMIT (1u << 20)
 #define FA_TABLE 1024                 // block-table entries kept in shared memory per block
-#define FA_TMEM_COLS 256              // S0: 0-63, S1: 64-127, O: 128-191
+#define FA_TMEM_COLS 256              // S0: 0-63, S1: 64-127, O: 128 .. 128 + head size
 
-#define FA_TILE_BYTES (FA_BN * FA_HD * 2)     // one K or V stage: 8 KB
-#define FA_QP_BYTES (FA_BM * FA_HD * 2)       // Q tile, P tile: 16 KB each
+#define FA_HALF_TILE (FA_BN * 128)            // 64 keys x 64 columns of K or V: 8 KB
+#define FA_ROWS_TILE (FA_BM * 128)            // 128 rows x 64 columns of Q, or the P tile: 16 KB
 
 __device__ __forceinline__ uint32_t fa_smem(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void fa_mbar_init(uint32_t bar, uint32_t count) {
@@ -66,6 +67,10 @@ __device__ __forceinline__ void fa_tma_2d(uint32_t dst, const CUtensorMap* map, 
 __device__ __forceinline__ void fa_tma_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
     asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
                  ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void fa_tma_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint32_t bar) {
+    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+                 ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar) : "memory");
 }
 __device__ __forceinline__ void fa_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fa_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -128,9 +133,10 @@ __device__ __forceinline__ uint64_t fa_desc(uint32_t addr) {
 struct FaBars {
     // p_full[b]: the softmax warps have written P buffer b; p_free[b]: the P V that read buffer b has completed
     // (so the buffer may be written again, and O holds that product)
-    uint64_t q_full, kv_full[FA_STAGES], kv_empty[FA_STAGES], s_full[2], s_empty[2], p_full[2], p_free[2];
+    uint64_t q_full, kv_full[FA_MAX_STAGES], kv_empty[FA_MAX_STAGES], s_full[2], s_empty[2], p_full[2], p_free[2];
 };
 
+template <int HD>
 __global__ void __launch_bounds__(FA_THREADS)
 attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                          const __grid_constant__ CUtensorMap map_v, __nv_bfloat16* __restrict__ out,
@@ -142,9 +148,12 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                          int* __restrict__ error_flag) {
     extern __shared__ unsigned char fa_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~(uintptr_t)1023);
-    unsigned char* q_tile = base;
-    unsigned char* p_tile = base + FA_QP_BYTES;
-    unsigned char* k_stage = p_tile + 2 * FA_QP_BYTES;          // two P buffers
+    constexpr int HALVES = HD / 64;
+    constexpr int FA_STAGES = HD == 64 ? 3 : 2;
+    constexpr int FA_TILE_BYTES = HALVES * FA_HALF_TILE;        // one K or V stage
+    unsigned char* q_tile = base;                               // [half][128 rows][64]
+    unsigned char* p_tile = base + HALVES * FA_ROWS_TILE;       // two P buffers
+    unsigned char* k_stage = p_tile + 2 * FA_ROWS_TILE;         // [stage][half][64 keys][64]
     unsigned char* v_stage = k_stage + FA_STAGES * FA_TILE_BYTES;
     FaBars* bars = reinterpret_cast<FaBars*>(v_stage + FA_STAGES * FA_TILE_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1);
@@ -214,8 +223,9 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
     if (warp == 0) {
         // ------------------------------------------------------------------ producer
         if (lane == 0 && num_tiles > 0) {
-            fa_expect_tx(fa_smem(&bars->q_full), FA_QP_BYTES);
-            fa_tma_3d(fa_smem(q_tile), &map_q, 0, g * rep, seg_start + tok0, fa_smem(&bars->q_full));
+            fa_expect_tx(fa_smem(&bars->q_full), (uint32_t)(HALVES * rep * tokens_per_tile * 128));      // whole boxes, whatever lies outside
+            for (int h = 0; h < HALVES; ++h)
+                fa_tma_4d(fa_smem(q_tile) + h * FA_ROWS_TILE, &map_q, 0, h, g * rep, seg_start + tok0, fa_smem(&bars->q_full));
             const int pages_per_tile = FA_BN >> page_shift;
             for (int j = 0; j < num_tiles; ++j) {
                 const int s = j % FA_STAGES;
@@ -226,16 +236,18 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                 const int key0 = k_begin + j * FA_BN;
                 const int pages = min(pages_per_tile, ((k_end - key0) + page_size - 1) >> page_shift);
                 const uint32_t bar = fa_smem(&bars->kv_full[s]);
-                fa_expect_tx(bar, (uint32_t)pages * page_size * FA_HD * 2 * 2);
+                fa_expect_tx(bar, (uint32_t)pages * page_size * HD * 2 * 2);
                 for (int pg = 0; pg < pages; ++pg) {
                     const int page_index = (key0 >> page_shift) + pg;
                     const int rel = page_index - page_base;
                     int page = rel < FA_TABLE ? page_cache[rel] : table[page_index];
                     if ((unsigned)page >= (unsigned)num_pages) page = 0;
                     const int row = (page * kv_heads + g) * page_size;
-                    const uint32_t off = (uint32_t)(s * FA_TILE_BYTES + pg * page_size * FA_HD * 2);
-                    fa_tma_2d(fa_smem(k_stage) + off, &map_k, 0, row, bar);
-                    fa_tma_2d(fa_smem(v_stage) + off, &map_v, 0, row, bar);
+                    for (int h = 0; h < HALVES; ++h) {
+                        const uint32_t off = (uint32_t)(s * FA_TILE_BYTES + h * FA_HALF_TILE + pg * page_size * 128);
+                        fa_tma_2d(fa_smem(k_stage) + off, &map_k, h * 64, row, bar);
+                        fa_tma_2d(fa_smem(v_stage) + off, &map_v, h * 64, row, bar);
+                    }
                 }
             }
         }
@@ -244,7 +256,7 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
         if (lane == 0 && num_tiles > 0) {
             // float32 accumulate, bfloat16 operands, M = 128, N = 64; for P V the second operand is MN-major
             const uint32_t idesc_qk = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(FA_BN >> 3) << 17) | ((uint32_t)(FA_BM >> 4) << 24);
-            const uint32_t idesc_pv = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(FA_HD >> 3) << 17) | ((uint32_t)(FA_BM >> 4) << 24);
+            const uint32_t idesc_pv = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(FA_BM >> 4) << 24);
             bool ok = fa_wait(fa_smem(&bars->q_full), 0);
             if (!ok) atomicExch(error_flag, 12);
             auto issue_qk = [&](int j) -> bool {
@@ -254,8 +266,9 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                 fa_fence_after();
                 const uint32_t qa = fa_smem(q_tile), ka = fa_smem(k_stage) + s * FA_TILE_BYTES;
 #pragma unroll
-                for (int k = 0; k < FA_HD / 16; ++k)
-                    fa_mma(tmem_base + b * FA_BN, fa_desc(qa + k * 32), fa_desc(ka + k * 32), idesc_qk, k > 0 ? 1u : 0u);
+                for (int k = 0; k < HD / 16; ++k)
+                    fa_mma(tmem_base + b * FA_BN, fa_desc(qa + (k >> 2) * FA_ROWS_TILE + (k & 3) * 32),
+                           fa_desc(ka + (k >> 2) * FA_HALF_TILE + (k & 3) * 32), idesc_qk, k > 0 ? 1u : 0u);
                 fa_commit(fa_smem(&bars->s_full[b]));
                 return true;
             };
@@ -265,10 +278,13 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                 if (!fa_wait(fa_smem(&bars->p_full[j & 1]), (j >> 1) & 1)) { atomicExch(error_flag, 14); ok = false; break; }
                 fa_fence_after();
                 const int s = j % FA_STAGES;
-                const uint32_t pa = fa_smem(p_tile) + (j & 1) * FA_QP_BYTES, va = fa_smem(v_stage) + s * FA_TILE_BYTES;
+                const uint32_t pa = fa_smem(p_tile) + (j & 1) * FA_ROWS_TILE, va = fa_smem(v_stage) + s * FA_TILE_BYTES;
 #pragma unroll
-                for (int k = 0; k < FA_BN / 16; ++k)
-                    fa_mma(tmem_o, fa_desc(pa + k * 32), fa_desc(va + k * 16 * FA_HD * 2), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+                for (int h = 0; h < HALVES; ++h)
+#pragma unroll
+                    for (int k = 0; k < FA_BN / 16; ++k)
+                        fa_mma(tmem_o + h * 64, fa_desc(pa + k * 32), fa_desc(va + h * FA_HALF_TILE + k * 16 * 128), idesc_pv,
+                               (j > 0 || k > 0) ? 1u : 0u);
                 fa_commit(fa_smem(&bars->kv_empty[s]));
                 fa_commit(fa_smem(&bars->p_free[j & 1]));
             }
@@ -344,16 +360,19 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                     // O must hold the P V of tile j - 1 before it is rescaled
                     if (!fa_wait(fa_smem(&bars->p_free[(j - 1) & 1]), ((j - 1) >> 1) & 1)) { ok = false; break; }
                     fa_fence_after();
-                    uint32_t o[2][32];
-                    fa_ld32(lane_base + 2 * FA_BN, o[0]);
-                    fa_ld32(lane_base + 2 * FA_BN + 32, o[1]);
-                    fa_wait_ld();
 #pragma unroll
-                    for (int h = 0; h < 2; ++h)
+                    for (int pair = 0; pair < HD / 64; ++pair) {
+                        uint32_t o[2][32];
+                        fa_ld32(lane_base + 2 * FA_BN + pair * 64, o[0]);
+                        fa_ld32(lane_base + 2 * FA_BN + pair * 64 + 32, o[1]);
+                        fa_wait_ld();
 #pragma unroll
-                        for (int c = 0; c < 32; ++c) o[h][c] = __float_as_uint(__uint_as_float(o[h][c]) * alpha);
-                    fa_st32(lane_base + 2 * FA_BN, o[0]);
-                    fa_st32(lane_base + 2 * FA_BN + 32, o[1]);
+                        for (int h = 0; h < 2; ++h)
+#pragma unroll
+                            for (int c = 0; c < 32; ++c) o[h][c] = __float_as_uint(__uint_as_float(o[h][c]) * alpha);
+                        fa_st32(lane_base + 2 * FA_BN + pair * 64, o[0]);
+                        fa_st32(lane_base + 2 * FA_BN + pair * 64 + 32, o[1]);
+                    }
                     fa_wait_st();
                 }
             }
@@ -361,13 +380,14 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
             const int visible_keys = k_end - key0;
             if (visible_keys < FA_BN) {
                 unsigned char* v_tile = v_stage + s * FA_TILE_BYTES;
-                for (int i = (warp - 2) * 32 + lane; i < (FA_BN - visible_keys) * 8; i += 128) {
-                    const int r = visible_keys + i / 8, c = i % 8;
-                    *reinterpret_cast<uint4*>(v_tile + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+                for (int i = (warp - 2) * 32 + lane; i < (FA_BN - visible_keys) * 8 * HALVES; i += 128) {
+                    const int h = i / ((FA_BN - visible_keys) * 8), rest = i % ((FA_BN - visible_keys) * 8);
+                    const int r = visible_keys + rest / 8, c = rest % 8;
+                    *reinterpret_cast<uint4*>(v_tile + h * FA_HALF_TILE + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
                 }
             }
             // P row in the swizzled K-major layout: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
-            unsigned char* p_row = p_tile + (j & 1) * FA_QP_BYTES + row * 128;
+            unsigned char* p_row = p_tile + (j & 1) * FA_ROWS_TILE + row * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c)
                 *reinterpret_cast<uint4*>(p_row + ((c ^ (row & 7)) << 4)) =
@@ -383,32 +403,37 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
             if (lane == 0) atomicExch(error_flag, 16);
         }
         fa_fence_after();
-        // ---- epilogue
-        float o_row[64];
-        if (ok && num_tiles > 0) {
-            uint32_t o[2][32];
-            fa_ld32(lane_base + 2 * FA_BN, o[0]);
-            fa_ld32(lane_base + 2 * FA_BN + 32, o[1]);
-            fa_wait_ld();
+        // ---- epilogue, 64 columns of the row at a time
+        const int token = tok0 + row / rep, head = g * rep + row % rep;
+        const size_t row_index = (size_t)(seg_start + token) * heads + head;
+        const bool writes = row < valid_rows && ok;
+        const float inv = row_sum > 0.f ? 1.f / row_sum : 0.f;
 #pragma unroll
-            for (int c = 0; c < 64; ++c) o_row[c] = __uint_as_float(o[c >> 5][c & 31]);
-        } else {
+        for (int pair = 0; pair < HD / 64; ++pair) {
+            float o_row[64];
+            if (ok && num_tiles > 0) {
+                uint32_t o[2][32];
+                fa_ld32(lane_base + 2 * FA_BN + pair * 64, o[0]);
+                fa_ld32(lane_base + 2 * FA_BN + pair * 64 + 32, o[1]);
+                fa_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 64; ++c) o_row[c] = 0.f;
-        }
-        if (row < valid_rows && ok) {
-            const int token = tok0 + row / rep, head = g * rep + row % rep;
-            const size_t row_index = (size_t)(seg_start + token) * heads + head;
+                for (int c = 0; c < 64; ++c) o_row[c] = __uint_as_float(o[c >> 5][c & 31]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 64; ++c) o_row[c] = 0.f;
+            }
+            if (!writes) continue;
             if (num_splits > 1) {
                 const size_t slot = row_index * num_splits + split;
-                float4* dst = reinterpret_cast<float4*>(partial_o + slot * FA_HD);
+                float4* dst = reinterpret_cast<float4*>(partial_o + slot * HD + pair * 64);
 #pragma unroll
                 for (int c = 0; c < 16; ++c) dst[c] = make_float4(o_row[4 * c], o_row[4 * c + 1], o_row[4 * c + 2], o_row[4 * c + 3]);
-                partial_ml[slot * 2] = (row_max == -INFINITY) ? -INFINITY : row_max * scale_log2;
-                partial_ml[slot * 2 + 1] = row_sum;
+                if (pair == 0) {
+                    partial_ml[slot * 2] = (row_max == -INFINITY) ? -INFINITY : row_max * scale_log2;
+                    partial_ml[slot * 2 + 1] = row_sum;
+                }
             } else {
-                const float inv = row_sum > 0.f ? 1.f / row_sum : 0.f;
-                uint4* dst = reinterpret_cast<uint4*>(out + row_index * FA_HD);
+                uint4* dst = reinterpret_cast<uint4*>(out + row_index * HD + pair * 64);
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
                     uint32_t w[4];
@@ -450,19 +475,42 @@ static FaEncodeFn fa_encode_fn() {
 }
 
 TTB_EXPORT int ttb_attention_tcgen05_supports(int heads, int kv_heads, int head_dim, int page_size, int window) {
-    if (head_dim != FA_HD || window > 0 || kv_heads < 1 || heads % kv_heads) return 0;
-    const int rep = heads / kv_heads;
-    if (rep != 1 && rep != 2 && rep != 4 && rep != 8 && rep != 16) return 0;
+    if ((head_dim != 64 && head_dim != 128) || window > 0 || kv_heads < 1 || heads % kv_heads) return 0;
+    if (heads / kv_heads > 16) return 0;
     if (page_size < 8 || page_size > FA_BN || (page_size & (page_size - 1))) return 0;
     return 1;
 }
 
 TTB_EXPORT int ttb_attention_tcgen05_tile_rows() { return FA_BM; }
 
-// qkv [tokens, q_row_stride] bfloat16 (queries first), pages [num_pages, kv_heads, page_size, 64] bfloat16.
+template <int HD>
+static int launch_attention_tcgen05(const CUtensorMap& map_q, const CUtensorMap& map_k, const CUtensorMap& map_v, void* out,
+                                    const int* cu_seqlens, const int* seg_pos0, const int* block_table, int table_width,
+                                    int page_size, const int* qtile_seg, const int* qtile_tok0, int n_qtiles, int heads,
+                                    int kv_heads, float scale, int num_splits, float* partial_o, float* partial_ml,
+                                    int num_pages, int* status, int* error_flag, cudaStream_t stream) {
+    constexpr int halves = HD / 64, stages = HD == 64 ? 3 : 2;
+    const size_t smem = 1024 + (size_t)(halves + 2) * FA_ROWS_TILE + 2 * (size_t)stages * halves * FA_HALF_TILE + sizeof(FaBars) + 16 +
+                        FA_TABLE * sizeof(int);
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return (int)e;
+        configured = true;
+    }
+    int page_shift = 0;
+    while ((1 << page_shift) < page_size) ++page_shift;
+    dim3 grid(n_qtiles, kv_heads, num_splits);
+    ttb_launch(attention_tcgen05_kernel<HD>, grid, dim3(FA_THREADS), smem, stream, map_q, map_k, map_v, (__nv_bfloat16*)out,
+               cu_seqlens, seg_pos0, block_table, table_width, page_size, page_shift, qtile_seg, qtile_tok0, heads,
+               kv_heads, scale * 1.4426950408889634f, num_splits, partial_o, partial_ml, num_pages, status, error_flag);
+    return ttb_launch_status();
+}
+
+// qkv [tokens, q_row_stride] bfloat16 (queries first), pages [num_pages, kv_heads, page_size, head_dim] bfloat16.
 // qtile_seg / qtile_tok0: the segment and first token of each query tile of 128 / (heads / kv_heads) tokens.
-// With num_splits > 1: partial_o [tokens * heads * num_splits * 64], partial_ml [tokens * heads * num_splits * 2] floats,
-// in the format that attention_mma.cu's merge kernel reads. error_flag: device int, set if a wait gave up.
+// With num_splits > 1: partial_o [tokens * heads * num_splits * head_dim], partial_ml [tokens * heads * num_splits * 2]
+// floats, in the format that attention_mma.cu's merge kernel reads. error_flag: device int, set if a wait gave up.
 TTB_EXPORT int ttb_paged_attention_tcgen05(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens,
                                            const int* seg_pos0, const void* key_pages, const void* value_pages,
                                            const int* block_table, int table_width, int page_size,
@@ -475,7 +523,7 @@ TTB_EXPORT int ttb_paged_attention_tcgen05(const void* qkv, int q_row_stride, vo
         !qtile_tok0 || !error_flag)
         return TTB_ERR_ARGUMENT;
     if (!ttb_attention_tcgen05_supports(heads, kv_heads, head_dim, page_size, 0)) return TTB_ERR_UNSUPPORTED;
-    if (q_row_stride % FA_HD || !aligned16(qkv) || !aligned16(key_pages) || !aligned16(value_pages) || !aligned16(out))
+    if (q_row_stride % head_dim || !aligned16(qkv) || !aligned16(key_pages) || !aligned16(value_pages) || !aligned16(out))
         return TTB_ERR_UNSUPPORTED;
     if (num_splits < 1 || num_splits > 65535 || kv_heads > 65535) return TTB_ERR_UNSUPPORTED;
     if (num_splits > 1 && (!partial_o || !partial_ml)) return TTB_ERR_ARGUMENT;
@@ -483,20 +531,20 @@ TTB_EXPORT int ttb_paged_attention_tcgen05(const void* qkv, int q_row_stride, vo
     if (!encode) return TTB_ERR_UNSUPPORTED;
     const int rep = heads / kv_heads;
     CUtensorMap map_q, map_k, map_v;
-    {   // queries: (64 elements, head, token)
-        cuuint64_t dims[3] = {FA_HD, (cuuint64_t)(q_row_stride / FA_HD), (cuuint64_t)tokens};
-        cuuint64_t strides[2] = {FA_HD * 2, (cuuint64_t)q_row_stride * 2};
-        cuuint32_t box[3] = {FA_HD, (cuuint32_t)rep, (cuuint32_t)(FA_BM / rep)};
-        cuuint32_t elem[3] = {1, 1, 1};
-        if (encode(&map_q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(qkv), dims, strides, box, elem,
+    {   // queries: (64 elements, half of the head, head, token)
+        cuuint64_t dims[4] = {64, (cuuint64_t)(head_dim / 64), (cuuint64_t)(q_row_stride / head_dim), (cuuint64_t)tokens};
+        cuuint64_t strides[3] = {128, (cuuint64_t)head_dim * 2, (cuuint64_t)q_row_stride * 2};
+        cuuint32_t box[4] = {64, 1, (cuuint32_t)rep, (cuuint32_t)(FA_BM / rep)};
+        cuuint32_t elem[4] = {1, 1, 1, 1};
+        if (encode(&map_q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(qkv), dims, strides, box, elem,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return TTB_ERR_UNSUPPORTED;
     }
-    for (int which = 0; which < 2; ++which) {   // pages: (64 elements, row = (page, kv head, slot))
-        cuuint64_t dims[2] = {FA_HD, (cuuint64_t)num_pages * kv_heads * page_size};
-        cuuint64_t strides[1] = {FA_HD * 2};
-        cuuint32_t box[2] = {FA_HD, (cuuint32_t)page_size};
+    for (int which = 0; which < 2; ++which) {   // pages: (head_dim elements, row = (page, kv head, slot)), boxes of 64 columns
+        cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)num_pages * kv_heads * page_size};
+        cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
+        cuuint32_t box[2] = {64, (cuuint32_t)page_size};
         cuuint32_t elem[2] = {1, 1};
         if (encode(which ? &map_v : &map_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                    const_cast<void*>(which ? value_pages : key_pages), dims, strides, box, elem,
@@ -504,18 +552,8 @@ TTB_EXPORT int ttb_paged_attention_tcgen05(const void* qkv, int q_row_stride, vo
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return TTB_ERR_UNSUPPORTED;
     }
-    const size_t smem = 1024 + 3 * FA_QP_BYTES + 2 * FA_STAGES * FA_TILE_BYTES + sizeof(FaBars) + 16 + FA_TABLE * sizeof(int);
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return (int)e;
-        configured = true;
-    }
-    int page_shift = 0;
-    while ((1 << page_shift) < page_size) ++page_shift;
-    dim3 grid(n_qtiles, kv_heads, num_splits);
-    ttb_launch(attention_tcgen05_kernel, grid, dim3(FA_THREADS), smem, stream, map_q, map_k, map_v, (__nv_bfloat16*)out,
-               cu_seqlens, seg_pos0, block_table, table_width, page_size, page_shift, qtile_seg, qtile_tok0, heads,
-               kv_heads, scale * 1.4426950408889634f, num_splits, partial_o, partial_ml, num_pages, status, error_flag);
-    return ttb_launch_status();
+#define FA_ARGS map_q, map_k, map_v, out, cu_seqlens, seg_pos0, block_table, table_width, page_size, qtile_seg, qtile_tok0,  \
+                n_qtiles, heads, kv_heads, scale, num_splits, partial_o, partial_ml, num_pages, status, error_flag, stream
+    return head_dim == 64 ? launch_attention_tcgen05<64>(FA_ARGS) : launch_attention_tcgen05<128>(FA_ARGS);
+#undef FA_ARGS
 }
