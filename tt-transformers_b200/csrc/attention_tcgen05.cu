@@ -32,7 +32,8 @@
 #define FA_MAX_STAGES 3
 #define FA_THREADS 192
 #define FA_WAIT_LIMIT (1u << 20)
-#define FA_TABLE 1024                 // block-table entries kept in shared memory per block
+#define FA_TABLE_64 1024              // block-table entries kept in shared memory per block, head size 64
+#define FA_TABLE_128 128              // ... head size 128, where two blocks an SM leave no room for more
 #define FA_TMEM_COLS 256              // S0: 0-63, S1: 64-127, O: 128 .. 128 + head size
 
 #define FA_HALF_TILE (FA_BN * 128)            // 64 keys x 64 columns of K or V: 8 KB
@@ -146,14 +147,18 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                          float scale_log2, int num_splits, float* __restrict__ partial_o,
                          float* __restrict__ partial_ml, int num_pages, int* __restrict__ status,
                          int* __restrict__ error_flag) {
-    extern __shared__ unsigned char fa_raw[];
-    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~(uintptr_t)1023);
+    extern __shared__ __align__(1024) unsigned char fa_raw[];
+    unsigned char* base = fa_raw;        // the 128-byte swizzle wants tiles on 1,024-byte boundaries
     constexpr int HALVES = HD / 64;
+    // head size 128: one P buffer instead of two, so that two blocks fit an SM (a second block hides more
+    // than a second P buffer does)
+    constexpr int NP = HD == 64 ? 2 : 1;
+    constexpr int FA_TABLE = HD == 64 ? FA_TABLE_64 : FA_TABLE_128;
     constexpr int FA_STAGES = HD == 64 ? 3 : 2;
     constexpr int FA_TILE_BYTES = HALVES * FA_HALF_TILE;        // one K or V stage
     unsigned char* q_tile = base;                               // [half][128 rows][64]
-    unsigned char* p_tile = base + HALVES * FA_ROWS_TILE;       // two P buffers
-    unsigned char* k_stage = p_tile + 2 * FA_ROWS_TILE;         // [stage][half][64 keys][64]
+    unsigned char* p_tile = base + HALVES * FA_ROWS_TILE;       // NP buffers
+    unsigned char* k_stage = p_tile + NP * FA_ROWS_TILE;        // [stage][half][64 keys][64]
     unsigned char* v_stage = k_stage + FA_STAGES * FA_TILE_BYTES;
     FaBars* bars = reinterpret_cast<FaBars*>(v_stage + FA_STAGES * FA_TILE_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1);
@@ -275,10 +280,10 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
             if (ok && !issue_qk(0)) { atomicExch(error_flag, 13); ok = false; }
             for (int j = 0; j < num_tiles && ok; ++j) {
                 if (j + 1 < num_tiles && !issue_qk(j + 1)) { atomicExch(error_flag, 13); ok = false; break; }
-                if (!fa_wait(fa_smem(&bars->p_full[j & 1]), (j >> 1) & 1)) { atomicExch(error_flag, 14); ok = false; break; }
+                if (!fa_wait(fa_smem(&bars->p_full[j % NP]), (j / NP) & 1)) { atomicExch(error_flag, 14); ok = false; break; }
                 fa_fence_after();
                 const int s = j % FA_STAGES;
-                const uint32_t pa = fa_smem(p_tile) + (j & 1) * FA_ROWS_TILE, va = fa_smem(v_stage) + s * FA_TILE_BYTES;
+                const uint32_t pa = fa_smem(p_tile) + (j % NP) * FA_ROWS_TILE, va = fa_smem(v_stage) + s * FA_TILE_BYTES;
 #pragma unroll
                 for (int h = 0; h < HALVES; ++h)
 #pragma unroll
@@ -286,7 +291,7 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                         fa_mma(tmem_o + h * 64, fa_desc(pa + k * 32), fa_desc(va + h * FA_HALF_TILE + k * 16 * 128), idesc_pv,
                                (j > 0 || k > 0) ? 1u : 0u);
                 fa_commit(fa_smem(&bars->kv_empty[s]));
-                fa_commit(fa_smem(&bars->p_free[j & 1]));
+                fa_commit(fa_smem(&bars->p_free[j % NP]));
             }
         }
     } else {
@@ -352,13 +357,13 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                 packed[(c >> 1) + 1] = *reinterpret_cast<uint32_t*>(&h1);
             }
             row_sum = row_sum * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
-            // P buffer j & 1 is free once the P V of tile j - 2 has completed
-            if (j >= 2 && !fa_wait(fa_smem(&bars->p_free[j & 1]), ((j >> 1) - 1) & 1)) { ok = false; break; }
+            // P buffer j % NP is free once the P V of tile j - NP has completed
+            if (j >= NP && !fa_wait(fa_smem(&bars->p_free[j % NP]), ((j / NP) - 1) & 1)) { ok = false; break; }
             if (j > 0) {
                 const bool moved = alpha != 1.f;
                 if (__any_sync(0xffffffffu, moved)) {          // warp-collective: rows whose reference stayed scale by 1
                     // O must hold the P V of tile j - 1 before it is rescaled
-                    if (!fa_wait(fa_smem(&bars->p_free[(j - 1) & 1]), ((j - 1) >> 1) & 1)) { ok = false; break; }
+                    if (!fa_wait(fa_smem(&bars->p_free[(j - 1) % NP]), ((j - 1) / NP) & 1)) { ok = false; break; }
                     fa_fence_after();
 #pragma unroll
                     for (int pair = 0; pair < HD / 64; ++pair) {
@@ -387,7 +392,7 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                 }
             }
             // P row in the swizzled K-major layout: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
-            unsigned char* p_row = p_tile + (j & 1) * FA_ROWS_TILE + row * 128;
+            unsigned char* p_row = p_tile + (j % NP) * FA_ROWS_TILE + row * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c)
                 *reinterpret_cast<uint4*>(p_row + ((c ^ (row & 7)) << 4)) =
@@ -395,10 +400,10 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
             fa_fence_async();            // generic-proxy writes become visible to the tensor core's reads
             fa_fence_before();
             __syncwarp();
-            if (lane == 0) fa_arrive(fa_smem(&bars->p_full[j & 1]));
+            if (lane == 0) fa_arrive(fa_smem(&bars->p_full[j % NP]));
         }
         if (!ok && lane == 0) atomicExch(error_flag, 15);
-        if (ok && num_tiles > 0 && !fa_wait(fa_smem(&bars->p_free[(num_tiles - 1) & 1]), ((num_tiles - 1) >> 1) & 1)) {
+        if (ok && num_tiles > 0 && !fa_wait(fa_smem(&bars->p_free[(num_tiles - 1) % NP]), ((num_tiles - 1) / NP) & 1)) {
             ok = false;
             if (lane == 0) atomicExch(error_flag, 16);
         }
@@ -490,8 +495,9 @@ static int launch_attention_tcgen05(const CUtensorMap& map_q, const CUtensorMap&
                                     int kv_heads, float scale, int num_splits, float* partial_o, float* partial_ml,
                                     int num_pages, int* status, int* error_flag, cudaStream_t stream) {
     constexpr int halves = HD / 64, stages = HD == 64 ? 3 : 2;
-    const size_t smem = 1024 + (size_t)(halves + 2) * FA_ROWS_TILE + 2 * (size_t)stages * halves * FA_HALF_TILE + sizeof(FaBars) + 16 +
-                        FA_TABLE * sizeof(int);
+    constexpr int p_buffers = HD == 64 ? 2 : 1, table = HD == 64 ? FA_TABLE_64 : FA_TABLE_128;
+    const size_t smem = (size_t)(halves + p_buffers) * FA_ROWS_TILE + 2 * (size_t)stages * halves * FA_HALF_TILE + sizeof(FaBars) + 16 +
+                        table * sizeof(int);
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
