@@ -170,6 +170,8 @@ ATTN_CASES = [
     (24, 8, 128, 16, [(0, 130), (700, 50), (64, 64)], None),
     (12, 4, 64, 32, [(0, 257), (3000, 43)], None),
     (7, 1, 128, 8, [(0, 90), (500, 30)], None),
+    (8, 2, 64, 128, [(0, 300), (200, 100)], None),                 # pages larger than a key tile
+    (8, 4, 128, 256, [(0, 70), (250, 20), (256, 30)], None),
 ]
 
 

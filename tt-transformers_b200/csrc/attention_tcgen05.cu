@@ -21,7 +21,7 @@
 //
 // A head of 128 is two halves of 64 columns everywhere (the 128-byte swizzle's width): Q, K and V tiles are
 // [half][rows][64], Q K^T runs over both halves' k-steps, P V is issued once per half of V into its half of O.
-// Takes: head sizes 64 and 128; up to 16 heads per KV head; page size dividing 64; no window.
+// Takes: head sizes 64 and 128; up to 16 heads per KV head; page sizes that are powers of two from 8 on; no window.
 // Everything else goes to attention_mma.cu or attention_generic.cu.
 #include <cuda.h>
 
@@ -231,7 +231,8 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
             fa_expect_tx(fa_smem(&bars->q_full), (uint32_t)(HALVES * rep * tokens_per_tile * 128));      // whole boxes, whatever lies outside
             for (int h = 0; h < HALVES; ++h)
                 fa_tma_4d(fa_smem(q_tile) + h * FA_ROWS_TILE, &map_q, 0, h, g * rep, seg_start + tok0, fa_smem(&bars->q_full));
-            const int pages_per_tile = FA_BN >> page_shift;
+            const int box_rows = min(page_size, FA_BN);            // a copy brings a page, or 64 rows of a larger one
+            const int boxes_per_tile = FA_BN / box_rows;
             for (int j = 0; j < num_tiles; ++j) {
                 const int s = j % FA_STAGES;
                 if (j >= FA_STAGES && !fa_wait(fa_smem(&bars->kv_empty[s]), ((j / FA_STAGES) - 1) & 1)) {
@@ -239,17 +240,18 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                     break;
                 }
                 const int key0 = k_begin + j * FA_BN;
-                const int pages = min(pages_per_tile, ((k_end - key0) + page_size - 1) >> page_shift);
+                const int boxes = min(boxes_per_tile, ((k_end - key0) + box_rows - 1) / box_rows);
                 const uint32_t bar = fa_smem(&bars->kv_full[s]);
-                fa_expect_tx(bar, (uint32_t)pages * page_size * HD * 2 * 2);
-                for (int pg = 0; pg < pages; ++pg) {
-                    const int page_index = (key0 >> page_shift) + pg;
+                fa_expect_tx(bar, (uint32_t)boxes * box_rows * HD * 2 * 2);
+                for (int pg = 0; pg < boxes; ++pg) {
+                    const int key = key0 + pg * box_rows;
+                    const int page_index = key >> page_shift;
                     const int rel = page_index - page_base;
                     int page = rel < FA_TABLE ? page_cache[rel] : table[page_index];
                     if ((unsigned)page >= (unsigned)num_pages) page = 0;
-                    const int row = (page * kv_heads + g) * page_size;
+                    const int row = (page * kv_heads + g) * page_size + (key & (page_size - 1));
                     for (int h = 0; h < HALVES; ++h) {
-                        const uint32_t off = (uint32_t)(s * FA_TILE_BYTES + h * FA_HALF_TILE + pg * page_size * 128);
+                        const uint32_t off = (uint32_t)(s * FA_TILE_BYTES + h * FA_HALF_TILE + pg * box_rows * 128);
                         fa_tma_2d(fa_smem(k_stage) + off, &map_k, h * 64, row, bar);
                         fa_tma_2d(fa_smem(v_stage) + off, &map_v, h * 64, row, bar);
                     }
@@ -482,7 +484,7 @@ static FaEncodeFn fa_encode_fn() {
 TTB_EXPORT int ttb_attention_tcgen05_supports(int heads, int kv_heads, int head_dim, int page_size, int window) {
     if ((head_dim != 64 && head_dim != 128) || window > 0 || kv_heads < 1 || heads % kv_heads) return 0;
     if (heads / kv_heads > 16) return 0;
-    if (page_size < 8 || page_size > FA_BN || (page_size & (page_size - 1))) return 0;
+    if (page_size < 8 || (page_size & (page_size - 1))) return 0;
     return 1;
 }
 
@@ -550,7 +552,7 @@ TTB_EXPORT int ttb_paged_attention_tcgen05(const void* qkv, int q_row_stride, vo
     for (int which = 0; which < 2; ++which) {   // pages: (head_dim elements, row = (page, kv head, slot)), boxes of 64 columns
         cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)num_pages * kv_heads * page_size};
         cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
-        cuuint32_t box[2] = {64, (cuuint32_t)page_size};
+        cuuint32_t box[2] = {64, (cuuint32_t)(page_size < FA_BN ? page_size : FA_BN)};
         cuuint32_t elem[2] = {1, 1};
         if (encode(which ? &map_v : &map_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                    const_cast<void*>(which ? value_pages : key_pages), dims, strides, box, elem,
