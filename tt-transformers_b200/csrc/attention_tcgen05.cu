@@ -184,6 +184,10 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
     const int* table = block_table + (size_t)seg * table_width;
     const int page_base = k_begin >> page_shift;
 
+    if (fa_smem(base) & 1023u) {          // the launch did not honour the alignment asked for above: say so, do nothing
+        if (threadIdx.x == 0) atomicExch(error_flag, 17);
+        return;
+    }
     if (threadIdx.x == 0) {
         fa_mbar_init(fa_smem(&bars->q_full), 1);
         for (int s = 0; s < FA_STAGES; ++s) {

@@ -130,6 +130,7 @@ class CudaKernels:
                     11: "attention's TMA producer", 12: "attention's MMA issuer waiting for the queries",
                     13: "attention's MMA issuer waiting for keys", 14: "attention's MMA issuer waiting for P",
                     15: "attention's softmax warps", 16: "attention's epilogue",
+                    17: "attention's shared memory, which is not aligned to 1,024 bytes",
                     21: "decode attention's TMA producer", 22: "decode attention's consumer warps"}.get(tc, f"role {tc}")
             raise EngineDeviceError(f"a tcgen05 kernel gave up waiting on a barrier ({role}); its result is invalid")
         value = int(self.status.item())
