@@ -18,6 +18,9 @@ from typing import Dict, List
 import torch
 
 
+OWN_ARGMAX = "own argmax"        # token_feedback value: the tokens are the argmax of this graph's replay before
+
+
 class DecodeGraphs:
     def __init__(self, engine):
         self._engine = weakref.ref(engine)       # no cycle with the engine: both go when the last user lets go
@@ -30,6 +33,8 @@ class DecodeGraphs:
         self._graphs: Dict[int, tuple] = {}
         self.replays = 0
         self.pool = None
+        self._last_size = None
+        self.greedy = None
 
     @property
     def engine(self):
@@ -67,13 +72,17 @@ class DecodeGraphs:
         try:
             with torch.cuda.graph(graph, pool=self.pool):
                 logits = eng.model.forward(batch, eng.cache)
+                # the greedy choice of every row, left where the next replay's embedding looks for its tokens:
+                # a greedy decode loop then needs neither a sampling launch nor a copy between two replays
+                greedy = eng.kernels.sample(logits)
+                static[layout["o_tok"]:layout["o_tok"] + size].copy_(greedy)
         finally:
             if gc_was_on:
                 gc.enable()
         if self.pool is None:
             self.pool = graph.pool()
         kernels_in_graph = eng.kernels.launches - before
-        return graph, static, layout, logits, kernels_in_graph
+        return graph, static, layout, logits, kernels_in_graph, greedy
 
     def run(self, entries: List, token_feedback: torch.Tensor = None) -> torch.Tensor:
         """Replay the captured step for these entries. With token_feedback (int32 on the device, one
@@ -84,14 +93,22 @@ class DecodeGraphs:
         size = self._bucket(rows)
         if size not in self._graphs:
             self._graphs[size] = self._capture(size, entries)
-        graph, static, layout, logits, kernels_in_graph = self._graphs[size]
+        graph, static, layout, logits, kernels_in_graph, greedy = self._graphs[size]
         host, new_layout, _ = eng._fill_host(entries, pad_to=size, table_width=eng.cache.table_width, want_all=True)
         assert new_layout["total"] == layout["total"]
-        static.copy_(host, non_blocking=True)
+        if isinstance(token_feedback, str) and token_feedback == OWN_ARGMAX:
+            if self._last_size != size:
+                raise ValueError("OWN_ARGMAX needs the step before to have been a replay of the same captured size")
+            first = layout["o_pos"]                     # everything but the token ids, which the replay before left in place
+            static[first:].copy_(host[first:], non_blocking=True)
+        else:
+            static.copy_(host, non_blocking=True)
         eng._record_staging()
-        if token_feedback is not None:
+        if torch.is_tensor(token_feedback):
             static[layout["o_tok"]:layout["o_tok"] + rows].copy_(token_feedback[:rows])
         graph.replay()
+        self._last_size = size
+        self.greedy = greedy[:rows]                     # overwritten by the next replay of this size
         eng.kernels.launches += kernels_in_graph
         self.replays += 1
         want = [i for i, e in enumerate(entries) if len(e.want)]

@@ -254,12 +254,14 @@ class Engine:
                 cur = self.kernels.sample(logits).tolist()
                 out.append(cur)
             return out
+        from .graph import OWN_ARGMAX
+
         host = torch.empty(steps, rows, dtype=torch.int32, pin_memory=True)
         feedback, cur = None, list(tokens)
         for s in range(steps):
-            logits = self.step([StepEntry(r, [t], [0]) for r, t in zip(request_ids, cur)], token_feedback=feedback)
-            feedback = self.kernels.sample(logits)
-            host[s].copy_(feedback, non_blocking=True)
+            self.step([StepEntry(r, [t], [0]) for r, t in zip(request_ids, cur)], token_feedback=feedback)
+            host[s].copy_(self.graphs.greedy, non_blocking=True)     # the captured step's own argmax
+            feedback = OWN_ARGMAX
             cur = [0] * rows                      # placeholders: the device feeds the real ids
         torch.cuda.current_stream(self.runtime.device).synchronize()
         return host.tolist()
