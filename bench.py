@@ -270,14 +270,15 @@ def main(argv=None) -> int:
       for _ in range(warmup):
         llm.step()
       torch.cuda.synchronize()
+      h2d, d2h = engine.h2d_bytes, llm.d2h_bytes
       t0 = time.perf_counter()
       for _ in range(args.steps):
         llm.step()
       torch.cuda.synchronize()
       e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
       e2e = {"value": round(args.batch / e2e_ms * 1e3, 1), "unit": "tokens/s",
-             "h2d_bytes_per_step": 4 * (3 * 4 * max(1, args.batch // 4 + (args.batch % 4 > 0)) + 16 + args.batch * pages_per_request),
-             "d2h_bytes_per_step": 4 * args.batch}
+             "h2d_bytes_per_step": (engine.h2d_bytes - h2d) // args.steps,
+             "d2h_bytes_per_step": (llm.d2h_bytes - d2h) // args.steps}
 
     line = {
         "metric": "decode tokens/s, Llama 3.2 1B sizes, batch 8", "value": round(value, 1), "unit": "tokens/s",

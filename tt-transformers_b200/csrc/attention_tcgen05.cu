@@ -5,15 +5,16 @@
 //   producer (warp 0, one thread)   TMA loads of whole cache pages (cp.async.bulk.tensor, 128-byte swizzle,
 //                                   no multicast) into a ring of K and V stages; the page ids of the
 //                                   block's key range are first copied from the block table to shared memory
-//   MMA (warp 1, one thread)        S = Q K^T by tcgen05.mma into one of two S buffers in tensor memory, then,
-//                                   once the softmax warps have written P to shared memory, O += P V into the
-//                                   O accumulator in tensor memory; the next tile's S is issued before this
-//                                   tile's P V, so that it runs under the softmax
+//   first product (warp 1, one thread)   S = Q K^T by tcgen05.mma into one of two S buffers in tensor memory, as
+//                                   soon as the keys have arrived and the buffer is free: the next tile's S
+//                                   is computed under this tile's softmax
+//   second product (warp 6, one thread)  once the softmax warps have written P, O += P V into the O accumulator
+//                                   in tensor memory, with P as the first operand from tensor memory
 //   softmax (warps 2-5)             thread r owns query row r: reads its 64 scores with tcgen05.ld, masks the
 //                                   tiles that the causal edge or the end of the key range cuts, keeps the
 //                                   running maximum and sum in float32 (no shuffles: a row is one thread),
 //                                   rescales its O row in tensor memory when the maximum moved, writes P as
-//                                   bfloat16 in the swizzled layout the MMA reads; at the end normalises O
+//                                   bfloat16 to tensor memory with tcgen05.st; at the end normalises O
 //                                   and stores it (or, with key splits, the unnormalised partial result)
 // Every wait on an mbarrier is bounded; a role that runs out of patience sets *error_flag, and the block
 // frees its tensor memory and returns. Rows of V beyond the last visible key are zeroed in shared memory
@@ -30,14 +31,14 @@
 #define FA_BM 128
 #define FA_BN 64
 #define FA_MAX_STAGES 3
-#define FA_THREADS 192
+#define FA_THREADS 224
 #define FA_WAIT_LIMIT (1u << 20)
-#define FA_TABLE_64 1024              // block-table entries kept in shared memory per block, head size 64
-#define FA_TABLE_128 128              // ... head size 128, where two blocks an SM leave no room for more
-#define FA_TMEM_COLS 256              // S0: 0-63, S1: 64-127, O: 128 .. 128 + head size
+#define FA_TABLE 1024                 // block-table entries kept in shared memory per block
+#define FA_TMEM_COLS 256              // S0: 0-63, S1: 64-127, O: 128 .. 128 + head size; head size 64: P0 192-223, P1 224-255
+#define FA_P_COL 192                  // first tensor-memory column of the P buffers (head size 64 only)
 
 #define FA_HALF_TILE (FA_BN * 128)            // 64 keys x 64 columns of K or V: 8 KB
-#define FA_ROWS_TILE (FA_BM * 128)            // 128 rows x 64 columns of Q, or the P tile: 16 KB
+#define FA_ROWS_TILE (FA_BM * 128)            // 128 rows x 64 columns of Q: 16 KB
 
 __device__ __forceinline__ uint32_t fa_smem(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void fa_mbar_init(uint32_t bar, uint32_t count) {
@@ -86,6 +87,14 @@ __device__ __forceinline__ void fa_mma(uint32_t tmem_d, uint64_t desc_a, uint64_
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(tmem_d), "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate) : "memory");
 }
+// the first operand in tensor memory: row r in lane r, two bfloat16 of the reduction dimension a column
+__device__ __forceinline__ void fa_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate) : "memory");
+}
 __device__ __forceinline__ void fa_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -133,7 +142,7 @@ __device__ __forceinline__ uint64_t fa_desc(uint32_t addr) {
 
 struct FaBars {
     // p_full[b]: the softmax warps have written P buffer b; p_free[b]: the P V that read buffer b has completed
-    // (so the buffer may be written again, and O holds that product)
+    // (so the buffer, or the S buffer it lies in, may be written again, and O holds that product)
     uint64_t q_full, kv_full[FA_MAX_STAGES], kv_empty[FA_MAX_STAGES], s_full[2], s_empty[2], p_full[2], p_free[2];
 };
 
@@ -150,15 +159,17 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
     extern __shared__ __align__(1024) unsigned char fa_raw[];
     unsigned char* base = fa_raw;        // the 128-byte swizzle wants tiles on 1,024-byte boundaries
     constexpr int HALVES = HD / 64;
-    // head size 128: one P buffer instead of two, so that two blocks fit an SM (a second block hides more
-    // than a second P buffer does)
-    constexpr int NP = HD == 64 ? 2 : 1;
-    constexpr int FA_TABLE = HD == 64 ? FA_TABLE_64 : FA_TABLE_128;
+    // P lives in tensor memory (two buffers of 32 columns, two bfloat16 a column) and is the P V product's
+    // first operand from there: no copy through shared memory, no proxy fence. Head size 64 has 64 columns to
+    // spare for it. Head size 128 has none: P of tile j overwrites the first 32 columns of the S buffer that
+    // its scores came from (a thread has its row of scores in registers by then), and that S buffer is free
+    // for tile j + 2 only once the P V of tile j has completed.
+    constexpr int NP = 2;
+    constexpr bool P_ALIAS = true;
     constexpr int FA_STAGES = HD == 64 ? 3 : 2;
     constexpr int FA_TILE_BYTES = HALVES * FA_HALF_TILE;        // one K or V stage
     unsigned char* q_tile = base;                               // [half][128 rows][64]
-    unsigned char* p_tile = base + HALVES * FA_ROWS_TILE;       // NP buffers
-    unsigned char* k_stage = p_tile + NP * FA_ROWS_TILE;        // [stage][half][64 keys][64]
+    unsigned char* k_stage = base + HALVES * FA_ROWS_TILE;      // [stage][half][64 keys][64]
     unsigned char* v_stage = k_stage + FA_STAGES * FA_TILE_BYTES;
     FaBars* bars = reinterpret_cast<FaBars*>(v_stage + FA_STAGES * FA_TILE_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1);
@@ -267,13 +278,12 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
         if (lane == 0 && num_tiles > 0) {
             // float32 accumulate, bfloat16 operands, M = 128, N = 64; for P V the second operand is MN-major
             const uint32_t idesc_qk = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(FA_BN >> 3) << 17) | ((uint32_t)(FA_BM >> 4) << 24);
-            const uint32_t idesc_pv = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(FA_BM >> 4) << 24);
             bool ok = fa_wait(fa_smem(&bars->q_full), 0);
             if (!ok) atomicExch(error_flag, 12);
             auto issue_qk = [&](int j) -> bool {
                 const int s = j % FA_STAGES, b = j & 1;
                 if (!fa_wait(fa_smem(&bars->kv_full[s]), (j / FA_STAGES) & 1)) return false;
-                if (j >= 2 && !fa_wait(fa_smem(&bars->s_empty[b]), ((j >> 1) - 1) & 1)) return false;
+                if (j >= 2 && !fa_wait(fa_smem(P_ALIAS ? &bars->p_free[b] : &bars->s_empty[b]), ((j >> 1) - 1) & 1)) return false;
                 fa_fence_after();
                 const uint32_t qa = fa_smem(q_tile), ka = fa_smem(k_stage) + s * FA_TILE_BYTES;
 #pragma unroll
@@ -283,19 +293,26 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                 fa_commit(fa_smem(&bars->s_full[b]));
                 return true;
             };
-            if (ok && !issue_qk(0)) { atomicExch(error_flag, 13); ok = false; }
+            for (int j = 0; j < num_tiles && ok; ++j)
+                if (!issue_qk(j)) { atomicExch(error_flag, 13); ok = false; }
+        }
+    } else if (warp == 6) {
+        // ------------------------------------------------------------------ issuer of the second product
+        if (lane == 0 && num_tiles > 0) {
+            const uint32_t idesc_pv = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(FA_BM >> 4) << 24);
+            bool ok = true;
             for (int j = 0; j < num_tiles && ok; ++j) {
-                if (j + 1 < num_tiles && !issue_qk(j + 1)) { atomicExch(error_flag, 13); ok = false; break; }
                 if (!fa_wait(fa_smem(&bars->p_full[j % NP]), (j / NP) & 1)) { atomicExch(error_flag, 14); ok = false; break; }
                 fa_fence_after();
                 const int s = j % FA_STAGES;
-                const uint32_t pa = fa_smem(p_tile) + (j % NP) * FA_ROWS_TILE, va = fa_smem(v_stage) + s * FA_TILE_BYTES;
+                const uint32_t va = fa_smem(v_stage) + s * FA_TILE_BYTES;
+                const uint32_t pa = tmem_base + (P_ALIAS ? (j & 1) * FA_BN : FA_P_COL + (j & 1) * 32);
 #pragma unroll
                 for (int h = 0; h < HALVES; ++h)
 #pragma unroll
                     for (int k = 0; k < FA_BN / 16; ++k)
-                        fa_mma(tmem_o + h * 64, fa_desc(pa + k * 32), fa_desc(va + h * FA_HALF_TILE + k * 16 * 128), idesc_pv,
-                               (j > 0 || k > 0) ? 1u : 0u);
+                        fa_mma_ts(tmem_o + h * 64, pa + k * 8, fa_desc(va + h * FA_HALF_TILE + k * 16 * 128), idesc_pv,
+                                  (j > 0 || k > 0) ? 1u : 0u);
                 fa_commit(fa_smem(&bars->kv_empty[s]));
                 fa_commit(fa_smem(&bars->p_free[j % NP]));
             }
@@ -363,8 +380,9 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                 packed[(c >> 1) + 1] = *reinterpret_cast<uint32_t*>(&h1);
             }
             row_sum = row_sum * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
-            // P buffer j % NP is free once the P V of tile j - NP has completed
-            if (j >= NP && !fa_wait(fa_smem(&bars->p_free[j % NP]), ((j / NP) - 1) & 1)) { ok = false; break; }
+            // P buffer j % NP is free once the P V of tile j - NP has completed (where P lies over S, the scores
+            // of this tile could not have been written before that)
+            if (!P_ALIAS && j >= NP && !fa_wait(fa_smem(&bars->p_free[j % NP]), ((j / NP) - 1) & 1)) { ok = false; break; }
             if (j > 0) {
                 const bool moved = alpha != 1.f;
                 if (__any_sync(0xffffffffu, moved)) {          // warp-collective: rows whose reference stayed scale by 1
@@ -389,7 +407,9 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
             }
             // rows of V from the first invisible key on are zeroed (last tile of the range only)
             const int visible_keys = k_end - key0;
+            bool wrote_shared = false;
             if (visible_keys < FA_BN) {
+                wrote_shared = true;
                 unsigned char* v_tile = v_stage + s * FA_TILE_BYTES;
                 for (int i = (warp - 2) * 32 + lane; i < (FA_BN - visible_keys) * 8 * HALVES; i += 128) {
                     const int h = i / ((FA_BN - visible_keys) * 8), rest = i % ((FA_BN - visible_keys) * 8);
@@ -397,13 +417,10 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
                     *reinterpret_cast<uint4*>(v_tile + h * FA_HALF_TILE + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
                 }
             }
-            // P row in the swizzled K-major layout: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
-            unsigned char* p_row = p_tile + (j % NP) * FA_ROWS_TILE + row * 128;
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-                *reinterpret_cast<uint4*>(p_row + ((c ^ (row & 7)) << 4)) =
-                    make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-            fa_fence_async();            // generic-proxy writes become visible to the tensor core's reads
+            // P row into tensor memory: column c holds the probabilities of keys 2c and 2c + 1
+            fa_st32(lane_base + (P_ALIAS ? b * FA_BN : FA_P_COL + b * 32), packed);
+            fa_wait_st();
+            if (wrote_shared) fa_fence_async();      // generic-proxy writes become visible to the tensor core's reads
             fa_fence_before();
             __syncwarp();
             if (lane == 0) fa_arrive(fa_smem(&bars->p_full[j % NP]));
@@ -501,9 +518,8 @@ static int launch_attention_tcgen05(const CUtensorMap& map_q, const CUtensorMap&
                                     int kv_heads, float scale, int num_splits, float* partial_o, float* partial_ml,
                                     int num_pages, int* status, int* error_flag, cudaStream_t stream) {
     constexpr int halves = HD / 64, stages = HD == 64 ? 3 : 2;
-    constexpr int p_buffers = HD == 64 ? 2 : 1, table = HD == 64 ? FA_TABLE_64 : FA_TABLE_128;
-    const size_t smem = (size_t)(halves + p_buffers) * FA_ROWS_TILE + 2 * (size_t)stages * halves * FA_HALF_TILE + sizeof(FaBars) + 16 +
-                        table * sizeof(int);
+    const size_t smem = (size_t)halves * FA_ROWS_TILE + 2 * (size_t)stages * halves * FA_HALF_TILE + sizeof(FaBars) + 16 +
+                        FA_TABLE * sizeof(int);
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -101,8 +101,10 @@ class DecodeGraphs:
                 raise ValueError("OWN_ARGMAX needs the step before to have been a replay of the same captured size")
             first = layout["o_pos"]                     # everything but the token ids, which the replay before left in place
             static[first:].copy_(host[first:], non_blocking=True)
+            eng.h2d_bytes += 4 * (host.numel() - first)
         else:
             static.copy_(host, non_blocking=True)
+            eng.h2d_bytes += 4 * host.numel()
         eng._record_staging()
         if torch.is_tensor(token_feedback):
             static[layout["o_tok"]:layout["o_tok"] + rows].copy_(token_feedback[:rows])

@@ -19,6 +19,7 @@ import torch
 from ..config.engine import EngineConfig
 from ..sampling.params import SamplingParams
 from ..sampling.sampler import Sampler
+from .graph import OWN_ARGMAX
 from .scheduler import Request, Scheduler
 from .step import Engine, StepEntry, build_engine
 
@@ -57,6 +58,7 @@ class LLM:
         self._scheduler: Optional[Scheduler] = None
         self._next_id = 0
         self.steps = 0
+        self.d2h_bytes = 0                  # bytes of sampled token ids read back so far
         self.last_stats: Dict[str, float] = {}
 
     # ------------------------------------------------------------------ generation
@@ -180,16 +182,25 @@ class LLM:
     def _launch(self, plan, entries, feedback, ahead_by: int) -> _Flight:
         cache = self.engine.cache
         lengths = {e.request_id: (cache.length(e.request_id) if cache.is_live(e.request_id) else 0) for e in entries}
+        graphs = self.engine.graphs
+        replays = graphs.replays if graphs is not None else 0
         logits = self.engine.step(entries, token_feedback=feedback)
         wanted = [e.request for e in plan if e.sample]
         if not wanted:
             return _Flight(tuple(e.request_id for e in entries), None, torch.empty(0, dtype=torch.int32), None, lengths)
-        tokens_dev = self.sampler.sample_device(logits, [r.params for r in wanted], [r.seed for r in wanted],
-                                                [len(r.output) + ahead_by for r in wanted])
+        if (graphs is not None and graphs.replays > replays and len(wanted) == len(entries)
+                and all(r.params.greedy for r in wanted)):
+            # A captured step ends with the argmax of its own rows and leaves it where its next replay reads
+            # its tokens: an all-greedy batch needs no sampling launch, and the step ahead no token copy.
+            source, tokens_dev = graphs.greedy, OWN_ARGMAX
+        else:
+            source = tokens_dev = self.sampler.sample_device(logits, [r.params for r in wanted], [r.seed for r in wanted],
+                                                             [len(r.output) + ahead_by for r in wanted])
         if self.engine.runtime.device.type != "cuda":
-            return _Flight(tuple(e.request_id for e in entries), tokens_dev, tokens_dev.cpu(), None, lengths)
+            return _Flight(tuple(e.request_id for e in entries), tokens_dev, source.cpu(), None, lengths)
         host = torch.empty(len(wanted), dtype=torch.int32, pin_memory=True)
-        host.copy_(tokens_dev, non_blocking=True)
+        self.d2h_bytes += 4 * len(wanted)
+        host.copy_(source, non_blocking=True)     # queued before the next replay overwrites the source
         event = torch.cuda.Event()
         event.record()
         return _Flight(tuple(e.request_id for e in entries), tokens_dev, host, event, lengths)

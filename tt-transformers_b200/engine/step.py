@@ -53,6 +53,7 @@ class Engine:
         self._staging = [None, None]          # two host buffers in turn, each with the event of its last copy
         self._staging_events = [None, None]
         self._staging_turn = 0
+        self.h2d_bytes = 0                  # bytes of step inputs copied from the host so far
         self.steps_run = 0
         self.graphs = None
         if config.cuda_graph and runtime.device.type == "cuda" and model.graph_safe():
@@ -91,6 +92,7 @@ class Engine:
         if not self._pinned:
             return host.clone()
         dev = host.to(self.runtime.device, non_blocking=True)
+        self.h2d_bytes += host.numel() * host.element_size()
         self._record_staging()
         return dev
 
