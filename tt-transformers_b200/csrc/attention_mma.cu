@@ -86,7 +86,9 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
     pdl_wait();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int warp_m = warp / WN, warp_n = warp % WN;
-    const int qt = blockIdx.x, g = blockIdx.y, split = blockIdx.z;
+    // the tile list comes sorted, most keys first; blocks are handed out in the order of their linear index
+    const int linear = blockIdx.x + gridDim.x * blockIdx.y, split = blockIdx.z;
+    const int qt = linear / gridDim.y, g = linear % gridDim.y;
     const int rep = heads / kv_heads;
     const int seg = qtile_seg ? qtile_seg[qt] : qt;
     const int tok0 = qtile_tok0 ? qtile_tok0[qt] : 0;

@@ -176,8 +176,10 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
     int* page_cache = reinterpret_cast<int*>(tmem_slot + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // later tiles of a segment see more keys: they go first, so that the longest blocks do not end the grid
-    const int qt = gridDim.x - 1 - blockIdx.x, g = blockIdx.y, split = blockIdx.z;
+    // The tile list comes sorted, most keys first. Blocks are handed out in the order of their linear index:
+    // all KV heads of the longest tile go first, so that the longest blocks do not end the grid.
+    const int linear = blockIdx.x + gridDim.x * blockIdx.y, split = blockIdx.z;
+    const int qt = linear / kv_heads, g = linear % kv_heads;
     const int rep = heads / kv_heads;
     const int seg = qtile_seg[qt], tok0 = qtile_tok0[qt];
     const int seg_start = cu_seqlens[seg];

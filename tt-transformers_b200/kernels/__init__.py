@@ -366,11 +366,12 @@ class CudaKernels:
         if decode_shape:
             seg, tok0, n_tiles = None, None, batch.num_segments
         else:
-            seg_list, tok_list = [], []
-            for r, n in enumerate(batch.seg_lens):
+            tiles = []
+            for r, (n, pos0) in enumerate(zip(batch.seg_lens, batch.seg_pos0_list)):
                 for t in range(0, n, tokens_per_tile):
-                    seg_list.append(r)
-                    tok_list.append(t)
+                    tiles.append((-(pos0 + min(n, t + tokens_per_tile)), r, t))
+            tiles.sort()                      # the tile that sees most keys first: the longest blocks start first
+            seg_list, tok_list = [t[1] for t in tiles], [t[2] for t in tiles]
             n_tiles = len(seg_list)
             both = torch.tensor([seg_list, tok_list], dtype=torch.int32, pin_memory=True).to(self.device, non_blocking=True)
             seg, tok0 = both[0], both[1]
