@@ -41,6 +41,9 @@ def _dtype_code(dtype: torch.dtype) -> int:
     raise KernelError(f"kernels take float32 or bfloat16 tensors, not {dtype}")
 
 
+_raw_stream = torch._C._cuda_getCurrentRawStream      # device index -> handle of torch's current stream
+
+
 _ERRORS = {-2: "unsupported size or option", -3: "bad argument (null pointer, alignment or contradiction)"}
 
 
@@ -62,6 +65,7 @@ class CudaKernels:
         if not torch.cuda.is_available():
             raise KernelError("no CUDA device is available; this engine has no CPU implementation")
         self.device = torch.device(device)
+        self._device_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         try:
             path = build()
         except BuildError as e:
@@ -112,7 +116,8 @@ class CudaKernels:
         return ctypes.c_void_p(0 if t is None else t.data_ptr())
 
     def _stream(self):
-        return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        # the handle of torch's current stream on this device, without building a Stream object for every launch
+        return ctypes.c_void_p(_raw_stream(self._device_index))
 
     def _check(self, code: int, what: str):
         self.launches += 1
