@@ -385,10 +385,17 @@ class CudaKernels:
         blocks = n_tiles * kv_heads
         slots = self.sm_count * (2 if big_tiles else
                                  int(self.lib.ttb_attention_mma_blocks_per_sm(1 if decode_shape else 0, head_dim)))
-        if blocks < slots:
-            # the TMA decode kernel streams faster and pays relatively more for a split: chunks of at least 512 keys
-            least = 512 if (decode_shape and self.use_tma_decode) else 256
-            splits = max(1, min(slots // blocks, batch.max_context // least))
+        if blocks < slots and decode_shape and self.use_tma_decode:
+            # The TMA decode kernel streams faster and pays relatively more for a split: chunks of at least 512
+            # keys, and about 2.2 blocks an SM rather than all that fit (measured at 8,192 keys of context and
+            # head size 64: 320 blocks are 2.6 % faster than 384 at batch 8, and 6 % faster than 416 at batch 4;
+            # 256 are as slow as 384).
+            splits = max(1, int(min(slots, 2.2 * self.sm_count) / blocks + 0.5))
+            if splits * blocks > slots:
+                splits -= 1
+            splits = max(1, min(splits, batch.max_context // 512))
+        elif blocks < slots:
+            splits = max(1, min(slots // blocks, batch.max_context // 256))
         else:
             splits = max(1, min(batch.max_context // 2048, -(-4 * slots // blocks)))
         plan = (decode_shape, seg, tok0, n_tiles, splits)
