@@ -406,6 +406,35 @@ def test_tcgen05_product_with_swiglu(kernels, twin, M, inter, K):
     close(got, ref, torch.bfloat16)
 
 
+@pytest.mark.parametrize("M,N,K", [(17, 320, 96), (24, 2048, 8192), (33, 257, 1000), (64, 3072, 2048), (64, 2048, 8192),
+                                   (1, 130, 72), (50, 6, 264), (64, 128256, 256), (40, 200, 4104)])
+def test_tcgen05_product_that_streams_the_weights(kernels, twin, M, N, K):
+    """gemm_skinny_tcgen05.cu (17 to 64 rows; it takes fewer too): widths that are no multiple of its tiles, a
+    reduction that is no multiple of its k-block, every cluster size from 1 to 8 (few row tiles and a long K
+    give the most slices), both output types, and the SwiGLU form."""
+    g = torch.Generator(device="cuda").manual_seed(10)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K) * 2).to(torch.bfloat16)
+    before = kernels.TENSOR_SKINNY_ROWS, kernels.SKINNY_ROWS, kernels.SKINNY_TCGEN05_MIN_K, kernels.use_skinny_tcgen05
+    kernels.TENSOR_SKINNY_ROWS = kernels.SKINNY_ROWS = kernels.SKINNY_TCGEN05_MIN_K = 0
+    kernels.use_skinny_tcgen05 = True
+    try:
+        launches = kernels.launches
+        got = kernels.linear(x, w)
+        got32 = kernels.linear(x, w, out_dtype=torch.float32)
+        fused = kernels.linear_swiglu(x, w) if N % 2 == 0 else None
+        assert kernels.launches - launches == (3 if N % 2 == 0 else 2), "one launch of this package's kernels per product"
+        kernels.check_status()            # raises if a wait inside the kernel gave up
+    finally:
+        kernels.TENSOR_SKINNY_ROWS, kernels.SKINNY_ROWS, kernels.SKINNY_TCGEN05_MIN_K, kernels.use_skinny_tcgen05 = before
+    ref = x.double() @ w.double().t()
+    close(got, ref, torch.bfloat16)
+    assert got32.dtype == torch.float32
+    close(got32, ref, torch.bfloat16)
+    if fused is not None:
+        close(fused, twin.linear_swiglu(x.double(), w.double()), torch.bfloat16)
+
+
 @pytest.mark.parametrize("M,N,K", [(17, 320, 96), (32, 2048, 2048), (40, 100, 1000), (64, 3072, 2048), (64, 2048, 8192)])
 def test_skinny_tensor_core_product_at_all_its_row_counts(kernels, twin, M, N, K):
     """The weight-streaming kernel takes up to 64 rows, although the engine hands it 16 at most."""

@@ -60,6 +60,7 @@ class CudaKernels:
     # 13 us against 20 to 42 us for the down projection at 32 to 64 rows).
     TENSOR_SKINNY_ROWS = 16
     TCGEN05_SWIGLU_ROWS = 128
+    SKINNY_TCGEN05_MIN_K = 8192
 
     def __init__(self, device: torch.device):
         if not torch.cuda.is_available():
@@ -80,7 +81,8 @@ class CudaKernels:
                      "ttb_paged_attention_mma", "ttb_attention_mma_tile_rows", "ttb_attention_mma_supports",
                      "ttb_gemv_mma", "ttb_gemv_mma_fused", "ttb_gemv_mma_parts", "ttb_argmax", "ttb_attention_decode_merges_in_kernel", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm",
                      "ttb_gemm_tcgen05", "ttb_paged_attention_tcgen05", "ttb_attention_tcgen05_supports",
-                     "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge", "ttb_gemv_qkv_rope"):
+                     "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge", "ttb_gemv_qkv_rope",
+                     "ttb_gemm_skinny_tcgen05", "ttb_gemm_skinny_tcgen05_rows"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -107,6 +109,11 @@ class CudaKernels:
         # plain products go to the library (the tcgen05 kernel reaches 0.75 to 0.95 of it). True ("1"):
         # every such product goes to the tcgen05 kernel. False ("0"): none does.
         self.use_tcgen05 = {"1": True, "0": False}.get(os.environ.get("TTB200_TCGEN05", "auto"))
+        # bfloat16 products with more rows than the mma.sync skinny kernel takes and up to SKINNY_TCGEN05_ROWS
+        # (decode steps of many requests): the weight-streaming tcgen05 kernel of gemm_skinny_tcgen05.cu
+        # (False: the library's product)
+        self.use_skinny_tcgen05 = os.environ.get("TTB200_SKINNY_TCGEN05", "1") == "1"
+        self.SKINNY_TCGEN05_ROWS = int(self.lib.ttb_gemm_skinny_tcgen05_rows())
         with torch.cuda.device(self.device):
             self.tc_error = torch.zeros(1, dtype=torch.int32, device=self.device)
 
@@ -136,7 +143,9 @@ class CudaKernels:
                     13: "attention's MMA issuer waiting for keys", 14: "attention's MMA issuer waiting for P",
                     15: "attention's softmax warps", 16: "attention's epilogue",
                     17: "attention's shared memory, which is not aligned to 1,024 bytes",
-                    21: "decode attention's TMA producer", 22: "decode attention's consumer warps"}.get(tc, f"role {tc}")
+                    21: "decode attention's TMA producer", 22: "decode attention's consumer warps",
+                    31: "the skinny product's TMA producer", 32: "the skinny product's MMA issuer",
+                    33: "the skinny product's epilogue"}.get(tc, f"role {tc}")
             raise EngineDeviceError(f"a tcgen05 kernel gave up waiting on a barrier ({role}); its result is invalid")
         value = int(self.status.item())
         if value != 0:
@@ -250,6 +259,15 @@ class CudaKernels:
                                           _dtype_code(out_dtype), M, N, K, x.stride(0), w.stride(0), N,
                                           self._stream()), "gemv")
             return out
+        # long reductions only (the down projection): measured against the library at 24 to 64 rows, 0.9 to 1.0 of
+        # its time from K = 8,192 on and 1.1 to 1.4 for the QKV and output projections
+        if (x.dtype == torch.bfloat16 and self.use_skinny_tcgen05 and M <= self.SKINNY_TCGEN05_ROWS
+                and K >= self.SKINNY_TCGEN05_MIN_K and K % 8 == 0 and x.stride(0) % 8 == 0 and w.stride(0) % 8 == 0):
+            out = torch.empty(M, N, dtype=out_dtype, device=self.device)
+            self._check(self.lib.ttb_gemm_skinny_tcgen05(self._p(x), self._p(w), self._p(out), _dtype_code(out_dtype),
+                                                         M, N, K, x.stride(0), w.stride(0), N, 0, self._p(self.tc_error),
+                                                         self._stream()), "gemm_skinny_tcgen05")
+            return out
         if (x.dtype == torch.bfloat16 and self.use_tcgen05 and K % 8 == 0 and x.stride(0) % 8 == 0
                 and w.stride(0) % 8 == 0):
             out = torch.empty(M, N, dtype=out_dtype, device=self.device)
@@ -289,6 +307,14 @@ class CudaKernels:
             self._check(self.lib.ttb_gemv_mma(self._p(x), self._p(w_gate_up), self._p(out), _dtype_code(x.dtype), M,
                                               inter, K, x.stride(0), w_gate_up.stride(0), inter, inter,
                                               self._stream()), "gemv_mma_swiglu")
+            return out
+        if (x.dtype == torch.bfloat16 and self.use_skinny_tcgen05 and M <= self.SKINNY_TCGEN05_ROWS and K % 8 == 0
+                and x.stride(0) % 8 == 0 and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1
+                and w_gate_up.stride(1) == 1):
+            out = torch.empty(M, inter, dtype=x.dtype, device=self.device)
+            self._check(self.lib.ttb_gemm_skinny_tcgen05(self._p(x), self._p(w_gate_up), self._p(out), _dtype_code(x.dtype),
+                                                         M, inter, K, x.stride(0), w_gate_up.stride(0), inter, inter,
+                                                         self._p(self.tc_error), self._stream()), "gemm_skinny_tcgen05_swiglu")
             return out
         fused = self.use_tcgen05 if self.use_tcgen05 is not None else M >= self.TCGEN05_SWIGLU_ROWS
         if (x.dtype == torch.bfloat16 and fused and K % 8 == 0 and x.stride(0) % 8 == 0
