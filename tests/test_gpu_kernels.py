@@ -415,8 +415,8 @@ def test_tcgen05_product_that_streams_the_weights(kernels, twin, M, N, K):
     g = torch.Generator(device="cuda").manual_seed(10)
     x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K) * 2).to(torch.bfloat16)
-    before = kernels.TENSOR_SKINNY_ROWS, kernels.SKINNY_ROWS, kernels.SKINNY_TCGEN05_MIN_K, kernels.use_skinny_tcgen05
-    kernels.TENSOR_SKINNY_ROWS = kernels.SKINNY_ROWS = kernels.SKINNY_TCGEN05_MIN_K = 0
+    before = (kernels.SKINNY_TCGEN05_MIN_ROWS, kernels.SKINNY_TCGEN05_MIN_K, kernels.use_skinny_tcgen05)
+    kernels.SKINNY_TCGEN05_MIN_ROWS = kernels.SKINNY_TCGEN05_MIN_K = 0      # every product of up to 64 rows goes there
     kernels.use_skinny_tcgen05 = True
     try:
         launches = kernels.launches
@@ -426,7 +426,7 @@ def test_tcgen05_product_that_streams_the_weights(kernels, twin, M, N, K):
         assert kernels.launches - launches == (3 if N % 2 == 0 else 2), "one launch of this package's kernels per product"
         kernels.check_status()            # raises if a wait inside the kernel gave up
     finally:
-        kernels.TENSOR_SKINNY_ROWS, kernels.SKINNY_ROWS, kernels.SKINNY_TCGEN05_MIN_K, kernels.use_skinny_tcgen05 = before
+        kernels.SKINNY_TCGEN05_MIN_ROWS, kernels.SKINNY_TCGEN05_MIN_K, kernels.use_skinny_tcgen05 = before
     ref = x.double() @ w.double().t()
     close(got, ref, torch.bfloat16)
     assert got32.dtype == torch.float32
@@ -441,14 +441,14 @@ def test_skinny_tensor_core_product_at_all_its_row_counts(kernels, twin, M, N, K
     g = torch.Generator(device="cuda").manual_seed(9)
     x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
-    before = kernels.TENSOR_SKINNY_ROWS
-    kernels.TENSOR_SKINNY_ROWS = 64
+    before = kernels.TENSOR_SKINNY_ROWS, kernels.use_skinny_tcgen05
+    kernels.TENSOR_SKINNY_ROWS, kernels.use_skinny_tcgen05 = 64, False
     try:
         got = kernels.linear(x, w)
         if N % 2 == 0:
             fused = kernels.linear_swiglu(x, w)
     finally:
-        kernels.TENSOR_SKINNY_ROWS = before
+        kernels.TENSOR_SKINNY_ROWS, kernels.use_skinny_tcgen05 = before
     close(got, x.double() @ w.double().t(), torch.bfloat16)
     if N % 2 == 0:
         close(fused, twin.linear_swiglu(x.double(), w.double()), torch.bfloat16)

@@ -1,4 +1,4 @@
-// C[M, N] = X[M, K] * W[N, K]^T for 17 to 64 rows of X (decode steps of many requests) on the fifth-generation
+// C[M, N] = X[M, K] * W[N, K]^T for 9 to 64 rows of X (decode steps of many requests) on the fifth-generation
 // tensor cores: the product is bound by streaming W once, so W is the operand that fills the tensor core's M
 // side and the few rows of X sit on its N side.
 //

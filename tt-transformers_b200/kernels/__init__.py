@@ -61,6 +61,10 @@ class CudaKernels:
     TENSOR_SKINNY_ROWS = 16
     TCGEN05_SWIGLU_ROWS = 128
     SKINNY_TCGEN05_MIN_K = 8192
+    # from this many rows on the weight-streaming tcgen05 kernel takes the products it is good at from the mma.sync
+    # skinny kernel (measured at 9, 12 and 16 rows: down projection 10.8 to 11.1 us against 13.5 to 14.1, gate/up
+    # with SwiGLU 14.5 to 15.5 against 17.3 to 18.6)
+    SKINNY_TCGEN05_MIN_ROWS = 9
 
     def __init__(self, device: torch.device):
         if not torch.cuda.is_available():
@@ -236,8 +240,12 @@ class CudaKernels:
             raise KernelError(f"linear: x {tuple(x.shape)} {x.dtype} does not match w {tuple(w.shape)} {w.dtype}")
         if x.stride(1) != 1 or w.stride(1) != 1:
             raise KernelError("linear: operands must be contiguous along K")
-        if (x.dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS and K % 8 == 0 and x.stride(0) % 8 == 0
-                and w.stride(0) % 8 == 0):
+        streams = (x.dtype == torch.bfloat16 and self.use_skinny_tcgen05 and norm is None
+                   and self.SKINNY_TCGEN05_MIN_ROWS <= M <= self.SKINNY_TCGEN05_ROWS and K >= self.SKINNY_TCGEN05_MIN_K
+                   and K % 8 == 0 and x.stride(0) % 8 == 0 and w.stride(0) % 8 == 0
+                   and not (self.fuse_add and accumulate is not None))
+        if (not streams and x.dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS and K % 8 == 0
+                and x.stride(0) % 8 == 0 and w.stride(0) % 8 == 0):
             fuse_add = (accumulate is not None and self.fuse_add and accumulate.dtype == torch.float32
                         and accumulate.shape == (M, N) and accumulate.stride(1) == 1)
             if norm is not None or fuse_add:
@@ -253,7 +261,7 @@ class CudaKernels:
             return out
         if norm is not None:
             x = norm.materialize()
-        if M <= self.SKINNY_ROWS:
+        if M <= self.SKINNY_ROWS and not streams:
             out = torch.empty(M, N, dtype=out_dtype, device=self.device)
             self._check(self.lib.ttb_gemv(self._p(x), self._p(w), self._p(out), _dtype_code(x.dtype),
                                           _dtype_code(out_dtype), M, N, K, x.stride(0), w.stride(0), N,
@@ -261,8 +269,7 @@ class CudaKernels:
             return out
         # long reductions only (the down projection): measured against the library at 24 to 64 rows, 0.9 to 1.0 of
         # its time from K = 8,192 on and 1.1 to 1.4 for the QKV and output projections
-        if (x.dtype == torch.bfloat16 and self.use_skinny_tcgen05 and M <= self.SKINNY_TCGEN05_ROWS
-                and K >= self.SKINNY_TCGEN05_MIN_K and K % 8 == 0 and x.stride(0) % 8 == 0 and w.stride(0) % 8 == 0):
+        if streams:
             out = torch.empty(M, N, dtype=out_dtype, device=self.device)
             self._check(self.lib.ttb_gemm_skinny_tcgen05(self._p(x), self._p(w), self._p(out), _dtype_code(out_dtype),
                                                          M, N, K, x.stride(0), w.stride(0), N, 0, self._p(self.tc_error),
@@ -301,16 +308,19 @@ class CudaKernels:
             x = x.materialize()
         M, K = x.shape
         inter = w_gate_up.shape[0] // 2
-        if (x.dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS and K % 8 == 0 and x.stride(0) % 8 == 0
-                and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1 and w_gate_up.stride(1) == 1):
+        streams = (x.dtype == torch.bfloat16 and self.use_skinny_tcgen05
+                   and self.SKINNY_TCGEN05_MIN_ROWS <= M <= self.SKINNY_TCGEN05_ROWS and K % 8 == 0
+                   and x.stride(0) % 8 == 0 and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1
+                   and w_gate_up.stride(1) == 1)
+        if (not streams and x.dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS and K % 8 == 0
+                and x.stride(0) % 8 == 0 and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1
+                and w_gate_up.stride(1) == 1):
             out = torch.empty(M, inter, dtype=x.dtype, device=self.device)
             self._check(self.lib.ttb_gemv_mma(self._p(x), self._p(w_gate_up), self._p(out), _dtype_code(x.dtype), M,
                                               inter, K, x.stride(0), w_gate_up.stride(0), inter, inter,
                                               self._stream()), "gemv_mma_swiglu")
             return out
-        if (x.dtype == torch.bfloat16 and self.use_skinny_tcgen05 and M <= self.SKINNY_TCGEN05_ROWS and K % 8 == 0
-                and x.stride(0) % 8 == 0 and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1
-                and w_gate_up.stride(1) == 1):
+        if streams:
             out = torch.empty(M, inter, dtype=x.dtype, device=self.device)
             self._check(self.lib.ttb_gemm_skinny_tcgen05(self._p(x), self._p(w_gate_up), self._p(out), _dtype_code(x.dtype),
                                                          M, inter, K, x.stride(0), w_gate_up.stride(0), inter, inter,
