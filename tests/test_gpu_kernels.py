@@ -437,18 +437,20 @@ def test_tcgen05_product_that_streams_the_weights(kernels, twin, M, N, K):
 
 @pytest.mark.parametrize("M,N,K", [(17, 320, 96), (32, 2048, 2048), (40, 100, 1000), (64, 3072, 2048), (64, 2048, 8192)])
 def test_skinny_tensor_core_product_at_all_its_row_counts(kernels, twin, M, N, K):
-    """The weight-streaming kernel takes up to 64 rows, although the engine hands it 16 at most."""
+    """The mma.sync weight-streaming kernel takes up to 64 rows, although the engine hands it 16 at most."""
     g = torch.Generator(device="cuda").manual_seed(9)
     x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
-    before = kernels.TENSOR_SKINNY_ROWS, kernels.use_skinny_tcgen05
-    kernels.TENSOR_SKINNY_ROWS, kernels.use_skinny_tcgen05 = 64, False
+    before = kernels.TENSOR_SKINNY_ROWS, kernels.SKINNY_ROWS, kernels.use_skinny_tcgen05
+    kernels.TENSOR_SKINNY_ROWS, kernels.SKINNY_ROWS, kernels.use_skinny_tcgen05 = 64, 64, False
     try:
+        launches = kernels.launches
         got = kernels.linear(x, w)
+        assert kernels.launches == launches + 1, "the product ran on this package's kernel"
         if N % 2 == 0:
             fused = kernels.linear_swiglu(x, w)
     finally:
-        kernels.TENSOR_SKINNY_ROWS, kernels.use_skinny_tcgen05 = before
+        kernels.TENSOR_SKINNY_ROWS, kernels.SKINNY_ROWS, kernels.use_skinny_tcgen05 = before
     close(got, x.double() @ w.double().t(), torch.bfloat16)
     if N % 2 == 0:
         close(fused, twin.linear_swiglu(x.double(), w.double()), torch.bfloat16)
