@@ -243,6 +243,7 @@ class CudaKernels:
         streams = (x.dtype == torch.bfloat16 and self.use_skinny_tcgen05 and norm is None
                    and self.SKINNY_TCGEN05_MIN_ROWS <= M <= self.SKINNY_TCGEN05_ROWS and K >= self.SKINNY_TCGEN05_MIN_K
                    and K % 8 == 0 and x.stride(0) % 8 == 0 and w.stride(0) % 8 == 0
+                   and x.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0
                    and not (self.fuse_add and accumulate is not None))
         if (not streams and x.dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS and K % 8 == 0
                 and x.stride(0) % 8 == 0 and w.stride(0) % 8 == 0):
@@ -314,7 +315,7 @@ class CudaKernels:
         streams = (x.dtype == torch.bfloat16 and self.use_skinny_tcgen05
                    and self.SKINNY_TCGEN05_MIN_ROWS <= M <= self.SKINNY_TCGEN05_ROWS and K % 8 == 0
                    and x.stride(0) % 8 == 0 and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1
-                   and w_gate_up.stride(1) == 1)
+                   and w_gate_up.stride(1) == 1 and x.data_ptr() % 16 == 0 and w_gate_up.data_ptr() % 16 == 0)
         if (not streams and x.dtype == torch.bfloat16 and M <= self.TENSOR_SKINNY_ROWS and K % 8 == 0
                 and x.stride(0) % 8 == 0 and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1
                 and w_gate_up.stride(1) == 1):
