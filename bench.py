@@ -9,11 +9,13 @@ decoded tokens per second at batch 8 with every request holding about `context` 
 from __future__ import annotations
 
 import argparse
+import atexit
 import json
 import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -44,46 +46,67 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi in the background while the timed region runs (reading only)."""
+    """nvidia-smi in the background for the whole run (reading only); a timed region keeps the samples that
+    arrived while it ran, or, if the region was shorter than the sampling period, the sample nearest to it."""
 
     QUERY = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __enter__(self):
+    def __init__(self, period_ms: int = 20):
+        self.samples = []                   # (arrival time, SM MHz, max SM MHz, active reasons)
+        self.proc = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", "0", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", str(period_ms)],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
-            self.proc = None
-        return self
-
-    def __exit__(self, *exc):
-        self.summary = {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
-        if self.proc is None:
             return
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        clocks, reasons, max_clock = [], set(), None
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.splitlines():
+        atexit.register(self.stop)          # whatever way the run ends, the child does not outlive it
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 6:
                 continue
             try:
-                clocks.append(float(parts[0]))
-                max_clock = float(parts[1])
+                clock, max_clock = float(parts[0]), float(parts[1])
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[2:6]):
-                if flag.lower().startswith("active"):
-                    reasons.add(name)
-        if clocks:
-            self.summary = {"sm_mhz": statistics.median(clocks), "sm_max_mhz": max_clock, "reasons": sorted(reasons)}
+            reasons = [n for n, flag in zip(self.NAMES, parts[2:6]) if flag.lower().startswith("active")]
+            self.samples.append((time.perf_counter(), clock, max_clock, reasons))
+
+    def wait_for_first_sample(self, timeout_s: float = 5.0):
+        end = time.perf_counter() + timeout_s
+        while self.proc is not None and not self.samples and time.perf_counter() < end:
+            time.sleep(0.01)
+
+    def __enter__(self):
+        self.t0 = time.perf_counter()
+        return self
+
+    def __exit__(self, *exc):
+        t1 = time.perf_counter()
+        self.summary = {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
+        if self.proc is None:
+            return
+        time.sleep(0.03)                    # a sample taken at the region's end may still be on its way
+        inside = [x for x in self.samples if self.t0 <= x[0] <= t1 + 0.03]
+        if not inside and self.samples:
+            inside = [min(self.samples, key=lambda x: min(abs(x[0] - self.t0), abs(x[0] - t1)))]
+        if inside:
+            self.summary = {"sm_mhz": statistics.median(x[1] for x in inside), "sm_max_mhz": inside[-1][2],
+                            "reasons": sorted({r for x in inside for r in x[3]})}
+
+    def stop(self):
+        if self.proc is not None and self.proc.poll() is None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
 
 
 def decode_bytes(cfg, layers, batch, context, elem=2):
@@ -154,6 +177,7 @@ def main(argv=None) -> int:
     from tt_transformers_b200.sampling import SamplingParams
     from tt_transformers_b200.weights import random_tensors
 
+    sampler = ClockSampler()             # runs for the whole measurement; each timed region takes its own samples
     cfg = dict(MODEL_1B, num_hidden_layers=args.layers)
     pk = peaks()
     device = "cuda:0"
@@ -194,7 +218,9 @@ def main(argv=None) -> int:
     if not args.skip_prefill:
         for _ in range(3):
             prefill_once()
-        prefill_ms = timed(prefill_once, 5)
+        # steps back to back, so that the host's part of a step runs under the step before; the median of three
+        # such runs, so that one slow run does not decide
+        prefill_ms = statistics.median(timed(prefill_once, 5) for _ in range(3))
     flops = prefill_flops(cfg, args.layers, PREFILL_TOKENS)
     prefill = {"value": round(PREFILL_TOKENS / prefill_ms * 1e3, 1), "tokens": PREFILL_TOKENS,
                "ms": round(prefill_ms, 3), "frac": round(flops / (prefill_ms * 1e-3) / (pk["bf16_tflops"] * 1e12), 4)}
@@ -224,7 +250,8 @@ def main(argv=None) -> int:
         # before, on the device; the sampled ids reach the host behind the steps
         tokens = engine.decode_steps(ids, [1] * batch, warm)[-1]
         before = kernels.launches
-        with ClockSampler() as clocks:
+        sampler.wait_for_first_sample()
+        with sampler as clocks:
             ms = timed(lambda: engine.decode_steps(ids, tokens, steps), 1) / steps
         launches = kernels.launches - before
         for rid in ids:
@@ -298,6 +325,7 @@ def main(argv=None) -> int:
                      "frac": round(achieved / pk["hbm_gbs"], 4)},
         "points": points,
     }
+    sampler.stop()
     print(json.dumps(line))
     return 0
 
