@@ -53,7 +53,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self, period_ms: int = 20):
+    def __init__(self, period_ms: int = 50):
         self.samples = []                   # (arrival time, SM MHz, max SM MHz, active reasons)
         self.proc = None
         try:
