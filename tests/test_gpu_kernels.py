@@ -407,11 +407,11 @@ def test_tcgen05_product_with_swiglu(kernels, twin, M, inter, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(17, 320, 96), (24, 2048, 8192), (33, 257, 1000), (64, 3072, 2048), (64, 2048, 8192),
-                                   (1, 130, 72), (50, 6, 264), (64, 128256, 256), (40, 200, 4104)])
+                                   (1, 130, 72), (50, 6, 264), (64, 128256, 256), (40, 200, 4104), (64, 128, 2112)])
 def test_tcgen05_product_that_streams_the_weights(kernels, twin, M, N, K):
     """gemm_skinny_tcgen05.cu (17 to 64 rows; it takes fewer too): widths that are no multiple of its tiles, a
     reduction that is no multiple of its k-block, every cluster size from 1 to 8 (few row tiles and a long K
-    give the most slices), both output types, and the SwiGLU form."""
+    give the most slices; with K = 2,112 the last of eight slices is empty), both output types, and the SwiGLU form."""
     g = torch.Generator(device="cuda").manual_seed(10)
     x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K) * 2).to(torch.bfloat16)
