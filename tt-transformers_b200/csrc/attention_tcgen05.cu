@@ -34,8 +34,8 @@
 #define FA_THREADS 224
 #define FA_WAIT_LIMIT (1u << 20)
 #define FA_TABLE 1024                 // block-table entries kept in shared memory per block
-#define FA_TMEM_COLS 256              // S0: 0-63, S1: 64-127, O: 128 .. 128 + head size; head size 64: P0 192-223, P1 224-255
-#define FA_P_COL 192                  // first tensor-memory column of the P buffers (head size 64 only)
+#define FA_TMEM_COLS 256              // S0: 0-63, S1: 64-127 (P over the first 32 columns of each), O: 128 .. 128 + head size
+#define FA_P_COL 192                  // first column of separate P buffers (head size 64 with P_ALIAS false: P0 192-223, P1 224-255)
 
 #define FA_HALF_TILE (FA_BN * 128)            // 64 keys x 64 columns of K or V: 8 KB
 #define FA_ROWS_TILE (FA_BM * 128)            // 128 rows x 64 columns of Q: 16 KB
@@ -160,10 +160,11 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
     unsigned char* base = fa_raw;        // the 128-byte swizzle wants tiles on 1,024-byte boundaries
     constexpr int HALVES = HD / 64;
     // P lives in tensor memory (two buffers of 32 columns, two bfloat16 a column) and is the P V product's
-    // first operand from there: no copy through shared memory, no proxy fence. Head size 64 has 64 columns to
-    // spare for it. Head size 128 has none: P of tile j overwrites the first 32 columns of the S buffer that
-    // its scores came from (a thread has its row of scores in registers by then), and that S buffer is free
-    // for tile j + 2 only once the P V of tile j has completed.
+    // first operand from there: no copy through shared memory, no proxy fence. P of tile j overwrites the first
+    // 32 columns of the S buffer that its scores came from (a thread has its row of scores in registers by
+    // then), and that S buffer is free for tile j + 2 only once the P V of tile j has completed. Head size 128
+    // has no other place for P; head size 64 has 64 columns to spare (P_ALIAS false puts P there and hands the
+    // S buffer back as soon as it has been read), which measured 1 % slower.
     constexpr int NP = 2;
     constexpr bool P_ALIAS = true;
     constexpr int FA_STAGES = HD == 64 ? 3 : 2;
