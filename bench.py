@@ -236,7 +236,8 @@ def main(argv=None) -> int:
                 engine.cache.commit(rid, length)
             for g in engine.cache.groups:
                 if g.pool is not None:
-                    g.storage.normal_(0, 1)
+                    for tensor in g.storage.values():
+                        tensor.normal_(0, 1)
             return ids
         for rid in ids:
             toks = prompt(length)

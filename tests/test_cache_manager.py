@@ -38,9 +38,10 @@ def test_groups_by_need_and_units_by_entry():
     full, win = PagedKV(2, 16), PagedKV(2, 16, window=8)
     m = manager([full, win, full, None, 0, SlotState((3,))], storage=True)
     assert len(m.groups) == 3
-    assert m.groups[0].storage.shape == (2, 2, 11, 2, 4, 16)         # two units, pages 0..10
-    assert m.groups[1].storage.shape == (1, 2, 11, 2, 4, 16)
-    assert m.groups[2].storage.shape == (1, 3, 3)
+    assert m.groups[0].storage["keys"].shape == (2, 11, 2, 4, 16)     # two units, pages 0..10
+    assert sorted(m.groups[0].storage) == ["keys", "values"]
+    assert m.groups[1].storage["values"].shape == (1, 11, 2, 4, 16)
+    assert m.groups[2].storage["state"].shape == (1, 4, 3)            # three slots and the row nobody owns
     assert m._unit_of_entry[4] == m._unit_of_entry[0] and 3 not in m._unit_of_entry
     with pytest.raises(ValueError):
         manager([None, 0])
@@ -91,8 +92,9 @@ def test_a_window_gives_pages_back_as_it_moves():
         length += n
         m.commit("a", length)
         m.audit()
-        # the windowed group holds only pages that positions >= length - 6 + 1 touch
-        first_needed = max(0, length - 6 + 1) // 4
+        # the windowed group holds only pages that positions >= length - 6 + 1 touch, and what one
+        # token taken back (a step that ran ahead) would touch again
+        first_needed = max(0, length - m.ROLLBACK_SLACK - 6 + 1) // 4
         row = m.table_rows(1, [m.slot("a")])[0]
         assert all(p == 0 for p in row[:first_needed]) and all(p != 0 for p in row[first_needed:-(-length // 4)])
         assert m.groups[1].pool.held_count == -(-length // 4) - first_needed
@@ -147,6 +149,63 @@ def test_random_orders_of_requests(seed):
 def test_slot_state_is_zeroed_at_admission():
     m = manager([SlotState((2, 2))], storage=True)
     slot = m.admit("a")
-    m.groups[0].storage[0, slot] += 5
+    m.groups[0].storage["state"][0, slot] += 5
     m.release("a")
-    assert m.admit("b") == slot and float(m.groups[0].storage[0, slot].abs().sum()) == 0
+    assert m.admit("b") == slot and float(m.groups[0].storage["state"][0, slot].abs().sum()) == 0
+
+
+def test_a_request_kind_of_the_callers_own_describes_its_storage():
+    """The manager asks the request what to store and how to show it: one tensor per token here, in a dtype of
+    its own, beside keys and values and a per-request state."""
+    from dataclasses import dataclass
+
+    from tt_transformers_b200.parts import CacheRequest
+
+    @dataclass(frozen=True)
+    class Latent(CacheRequest):
+        width: int
+        paged = True
+
+        def storage(self, page_size):
+            return {"latent": ((page_size, self.width), torch.float64)}
+
+        def view(self, tensors, *, block_table, page_size, **_):
+            return ("latent view", tensors["latent"], block_table, page_size)
+
+    m = manager([Latent(5), PagedKV(1, 8), Latent(5), SlotState((2,), dtype=torch.int32)], storage=True)
+    assert [type(g.request).__name__ for g in m.groups] == ["Latent", "PagedKV", "SlotState"]
+    assert m.groups[0].storage["latent"].shape == (2, 11, 4, 5) and m.groups[0].storage["latent"].dtype == torch.float64
+    assert m.groups[2].storage["state"].dtype == torch.int32
+    m.admit("a")
+    m.reserve("a", 9)
+    m.commit("a", 9)
+    m.audit()
+
+    class Batch:
+        block_tables = {0: "table 0", 1: "table 1"}
+        seg_slot, seg_slot_list = "slots", [0]
+
+    kind, tensor, table, page = m.view(2, Batch)
+    assert kind == "latent view" and tensor.shape == (11, 4, 5) and table == "table 0" and page == 4
+    assert tensor.data_ptr() == m.groups[0].storage["latent"][1].data_ptr()
+    m.release("a")
+    assert m.free_pages() == 10
+
+
+def test_one_token_can_be_taken_back_behind_a_window():
+    m = manager([PagedKV(1, 8, window=4)], num_pages=6)
+    m.admit("a")
+    length = 0
+    for n in (7, 1, 1, 1, 1, 1):
+        m.reserve("a", length + n)
+        length += n
+        m.commit("a", length)
+    held = m.groups[0].pool.held_count
+    m.rollback("a", length - 1)                 # the step that ran ahead is not wanted after all
+    m.audit()
+    # every page that a query at position length - 1 reads (keys > length - 1 - 4) is still there
+    row = m.table_rows(0, [m.slot("a")])[0]
+    assert all(row[p // 4] != 0 for p in range(length - 1 - 4 + 1, length - 1))
+    assert m.groups[0].pool.held_count <= held
+    with pytest.raises(RuntimeError):
+        m.rollback("a", length - 3)

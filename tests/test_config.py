@@ -84,8 +84,8 @@ def test_registry():
     assert "LlamaForCausalLM" in known_architectures()
     arch = get_architecture("LlamaForCausalLM")
     spec = arch.model_spec(arch.load_config(TINY_B))
-    assert len(spec.layers) == 3 and spec.head_name == "lm_head.weight" and spec.vocab_size == 384
-    assert arch.model_spec(arch.load_config(TINY_A)).head_name is None
+    assert len(spec.layers) == 3 and spec.head.params["weight_name"] == "lm_head.weight" and spec.vocab_size == 384
+    assert arch.model_spec(arch.load_config(TINY_A)).head.params["weight_name"] is None
     with pytest.raises(UnknownArchitecture, match="LlamaForCausalLM"):
         get_architecture("NoSuchModelForCausalLM")
     assert architecture_of(TINY_A) == "LlamaForCausalLM"

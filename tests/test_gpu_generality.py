@@ -12,7 +12,8 @@ import plain_llama
 from tt_transformers_b200 import register_architecture, register_part
 from tt_transformers_b200.config import EngineConfig
 from tt_transformers_b200.engine.step import build_engine
-from tt_transformers_b200.parts import LayerCall, LayerSpec, Mixer, ModelSpec, PartSpec, SlotState, TensorSpec
+from tt_transformers_b200.parts import (Block, CacheRequest, LayerCall, LayerSpec, Mixer, ModelSpec, PartSpec, SlotState,
+                                        TensorSpec)
 from tt_transformers_b200.weights import write_model_folder
 
 pytestmark = pytest.mark.gpu
@@ -69,10 +70,10 @@ def toy_model_spec(cfg):
         norm2=PartSpec("rmsnorm", dict(width=cfg.width, eps=cfg.eps, weight_name=f"toy.{i}.norm2")),
         feed_forward=PartSpec("swiglu", dict(width=cfg.width, inter=cfg.inter, prefix=f"toy.{i}.ff.")),
     ) for i in range(cfg.layers))
-    return ModelSpec(vocab_size=cfg.vocab, width=cfg.width, embedding_name="toy.embed", layers=layers,
+    return ModelSpec(vocab_size=cfg.vocab, width=cfg.width, embedding=PartSpec("table", dict(vocab=cfg.vocab, width=cfg.width, weight_name="toy.embed")), layers=layers,
                      order=tuple(LayerCall(i) for i in range(cfg.layers)),
                      final_norm=PartSpec("rmsnorm", dict(width=cfg.width, eps=cfg.eps, weight_name="toy.norm")),
-                     head_name="toy.head")
+                     head=PartSpec("linear", dict(vocab=cfg.vocab, width=cfg.width, weight_name="toy.head")))
 
 
 def toy_plain_forward(cfg, w, tokens):
@@ -136,10 +137,10 @@ def order_model_spec(cfg):
         norm2=PartSpec("rmsnorm", dict(width=cfg.width, eps=cfg.eps, weight_name=f"l.{i}.n2")),
         feed_forward=PartSpec("swiglu", dict(width=cfg.width, inter=cfg.inter, prefix=f"l.{i}.ff.")),
     ) for i, window in enumerate(cfg.windows))
-    return ModelSpec(vocab_size=cfg.vocab, width=cfg.width, embedding_name="emb", layers=layers,
+    return ModelSpec(vocab_size=cfg.vocab, width=cfg.width, embedding=PartSpec("table", dict(vocab=cfg.vocab, width=cfg.width, weight_name="emb")), layers=layers,
                      order=tuple(LayerCall(l, c) for l, c in cfg.order),
                      final_norm=PartSpec("rmsnorm", dict(width=cfg.width, eps=cfg.eps, weight_name="norm")),
-                     head_name=None)
+                     head=PartSpec("linear", dict(vocab=cfg.vocab, width=cfg.width, weight_name=None)))
 
 
 def order_plain_forward(cfg, w, tokens):
@@ -189,7 +190,8 @@ def test_layer_order_shared_caches_and_windows(tmp_path, head_dim):
             kinds = [(type(g.request).__name__, g.request.window, len(g.units)) for g in engine.cache.groups]
             assert kinds == [("PagedKV", None, 2), ("PagedKV", 24, 2)]       # entry 3 owns no unit: it reads entry 0's
             for g in engine.cache.groups:
-                g.storage.fill_(float("nan"))        # a read of a slot that was never written would show
+                for tensor in g.storage.values():
+                    tensor.fill_(float("nan"))       # a read of a slot that was never written would show
             got = helpers.run_steps(engine, steps)
             engine.cache.audit()
             for rid in ref:
@@ -277,10 +279,11 @@ def routed_model_spec(cfg):
         feed_forward=PartSpec("toy_routed", dict(width=cfg["width"], inter=cfg["inter"], experts=cfg["experts"],
                                                  prefix=f"m.{i}.moe.")),
     ) for i in range(cfg["layers"]))
-    return ModelSpec(vocab_size=cfg["vocab"], width=cfg["width"], embedding_name="emb", layers=layers,
+    return ModelSpec(vocab_size=cfg["vocab"], width=cfg["width"],
+                     embedding=PartSpec("table", dict(vocab=cfg["vocab"], width=cfg["width"], weight_name="emb")), layers=layers,
                      order=tuple(LayerCall(i) for i in range(cfg["layers"])),
                      final_norm=PartSpec("rmsnorm", dict(width=cfg["width"], eps=1e-5, weight_name="norm")),
-                     head_name="head",
+                     head=PartSpec("linear", dict(vocab=cfg["vocab"], width=cfg["width"], weight_name="head")),
                      input_position=PartSpec("toy_learned", dict(width=cfg["width"], max_positions=cfg["positions"],
                                                                  weight_name="pos")))
 
@@ -324,3 +327,145 @@ def test_a_routed_feed_forward_and_a_learned_position_encoding(tmp_path):
         got = helpers.run_steps(engine, steps)
         for rid in ref:
             assert helpers.relative_error(got[rid], ref[rid]) < 1e-4, rid
+
+
+# ---------------------------------------------------------------------------- a whole toy architecture out of kinds the package has not
+@dataclass(frozen=True)
+class LatentPages(CacheRequest):
+    """One tensor per token instead of keys and values: a latent vector, from which the mixer makes both.
+    A page holds page_size latents."""
+
+    latent: int
+    window: object = None
+    paged = True
+
+    def storage(self, page_size):
+        return {"latent": ((page_size, self.latent), None)}
+
+    def view(self, tensors, *, block_table, page_size, **_):
+        return {"latent": tensors["latent"], "block_table": block_table, "page_size": page_size}
+
+
+class LatentAttention(Mixer):
+    """Single-head causal attention whose cache holds c_t = Wc h_t only; keys Wk c and values Wv c are made
+    from the cached latents of the request at every step. Plain torch operations."""
+
+    def __init__(self, width, latent, prefix, position=None):
+        self.width, self.latent, self.prefix = width, latent, prefix
+
+    def tensor_specs(self):
+        p = self.prefix
+        return [TensorSpec(p + "q", (self.latent, self.width)), TensorSpec(p + "c", (self.latent, self.width)),
+                TensorSpec(p + "k", (self.latent, self.latent)), TensorSpec(p + "v", (self.width, self.latent))]
+
+    def bind(self, tensors, runtime):
+        super().bind(tensors, runtime)
+        self.w = {n: runtime.matrix(tensors[self.prefix + n]) for n in "qckv"}
+
+    def cache_request(self):
+        return LatentPages(self.latent)
+
+    def forward(self, x, batch, cache, write_cache=True):
+        P, pages, table = cache["page_size"], cache["latent"], cache["block_table"]
+        c = (x.float() @ self.w["c"].float().t()).to(x.dtype)
+        if write_cache:
+            pos = batch.positions.long()
+            pages[table[batch.seg_of_token.long(), pos // P].long(), pos % P] = c
+        q = x.float() @ self.w["q"].float().t()
+        out = torch.empty_like(x)
+        start = 0
+        for r, (n, pos0) in enumerate(zip(batch.seg_lens, batch.seg_pos0_list)):
+            ctx = pos0 + n
+            held = pages[table[r, :-(-ctx // P)].long()].reshape(-1, self.latent)[:ctx].float()
+            keys, values = held @ self.w["k"].float().t(), held @ self.w["v"].float().t()
+            scores = q[start:start + n] @ keys.t() * self.latent ** -0.5
+            visible = torch.arange(ctx, device=x.device)[None, :] <= torch.arange(pos0, ctx, device=x.device)[:, None]
+            probs = torch.softmax(scores.masked_fill(~visible, float("-inf")), dim=-1)
+            out[start:start + n] = (probs @ values).to(x.dtype)
+            start += n
+        return out
+
+
+class SandwichBlock(Block):
+    """Norms before AND after each sub-layer: x += post1(mixer(norm1(x))); x += post2(ff(norm2(x)))."""
+
+    slots = {"norm1": "norm", "mixer": "mixer", "post1": "norm", "norm2": "norm", "feed_forward": "feed_forward",
+             "post2": "norm"}
+
+    def __init__(self, norm1, mixer, post1, norm2, feed_forward, post2):
+        self.norm1, self.mixer, self.post1 = norm1, mixer, post1
+        self.norm2, self.feed_forward, self.post2 = norm2, feed_forward, post2
+
+    def forward(self, x, delta, batch, cache, write_cache=True):
+        h = self.norm1.forward_add(x, delta)
+        mixed = self.post1.forward_add(self.mixer.forward(h, batch, cache, write_cache).float(), None)
+        h = self.norm2.forward_add(x, mixed)
+        return x, self.post2.forward_add(self.feed_forward.forward(h, batch).float(), None)
+
+
+def latent_model_spec(cfg):
+    W, V = cfg["width"], cfg["vocab"]
+    norm = lambda name: PartSpec("rmsnorm", dict(width=W, eps=cfg["eps"], weight_name=name))  # noqa: E731
+    layers = tuple(LayerSpec(
+        block="toy_sandwich",
+        norm1=norm(f"t.{i}.n1"), mixer=PartSpec("toy_latent", dict(width=W, latent=cfg["latent"], prefix=f"t.{i}.mix.")),
+        post1=norm(f"t.{i}.p1"), norm2=norm(f"t.{i}.n2"),
+        feed_forward=PartSpec("swiglu", dict(width=W, inter=cfg["inter"], prefix=f"t.{i}.ff.")), post2=norm(f"t.{i}.p2"),
+    ) for i in range(cfg["layers"]))
+    return ModelSpec(vocab_size=V, width=W,
+                     embedding=PartSpec("table", dict(vocab=V, width=W, weight_name="emb", scale=cfg["embed_scale"])),
+                     layers=layers, order=tuple(LayerCall(i) for i in range(cfg["layers"])), final_norm=norm("norm"),
+                     head=PartSpec("linear", dict(vocab=V, width=W, weight_name=None, logit_cap=cfg["logit_cap"])))
+
+
+def latent_plain_forward(cfg, w, tokens, layers=None):
+    T, L = len(tokens), cfg["latent"]
+    x = w["emb"][torch.as_tensor(tokens)] * cfg["embed_scale"]
+    visible = torch.arange(T)[None, :] <= torch.arange(T)[:, None]
+    for i in range(cfg["layers"] if layers is None else layers):
+        p = f"t.{i}."
+        h = plain_llama.rms_norm(x, w[p + "n1"], cfg["eps"])
+        c = h @ w[p + "mix.c"].T
+        scores = (h @ w[p + "mix.q"].T) @ (c @ w[p + "mix.k"].T).T * L ** -0.5
+        mixed = torch.softmax(scores.masked_fill(~visible, float("-inf")), dim=-1) @ (c @ w[p + "mix.v"].T)
+        x = x + plain_llama.rms_norm(mixed, w[p + "p1"], cfg["eps"])
+        h = plain_llama.rms_norm(x, w[p + "n2"], cfg["eps"])
+        x = x + plain_llama.rms_norm(plain_llama.swiglu(h, w, p + "ff."), w[p + "p2"], cfg["eps"])
+    logits = plain_llama.rms_norm(x, w["norm"], cfg["eps"]) @ w["emb"].T
+    return cfg["logit_cap"] * torch.tanh(logits / cfg["logit_cap"])
+
+
+def test_a_toy_architecture_with_scaled_embedding_capped_head_post_norms_and_a_latent_cache(tmp_path):
+    """Nothing under the package changes for: an embedding with a scale, a head with a cap on its logits, a block
+    kind with six parts, and a cache request that stores one tensor per token."""
+    register_part("mixer", "toy_latent", LatentAttention)
+    register_part("block", "toy_sandwich", SandwichBlock)
+    register_architecture("ToyLatentForTests", lambda d: d, latent_model_spec)
+    cfg = {"architectures": ["ToyLatentForTests"], "width": 56, "layers": 3, "vocab": 150, "inter": 88, "latent": 24,
+           "eps": 1e-5, "embed_scale": 56 ** 0.5, "logit_cap": 6.0}
+    folder = write_model_folder(str(tmp_path / "latent"), cfg, seed=21, std=0.15, norm_std=0.1, dtype=torch.float32)
+    _, w = plain_llama.read_model_folder(folder)
+    requests = {f"r{i}": helpers.random_tokens(150, n, 60 + i) for i, n in enumerate((61, 18, 40, 7, 33))}
+    ref = {rid: latent_plain_forward(cfg, w, toks) for rid, toks in requests.items()}
+    assert max(float(r.abs().max()) for r in ref.values()) > 3.0          # the cap bends these logits (tanh(0.5) = 0.46)
+    for dtype, tol in (("float32", 1e-4), ("bfloat16", 5e-2)):
+        for make_steps in (helpers.steps_whole, helpers.steps_decode_tail, helpers.steps_portions, helpers.steps_mixed):
+            steps = make_steps(requests)
+            pages = -(-helpers.max_live_tokens(requests, steps, rounding=8) // 8)
+            engine = build_engine(folder, EngineConfig(dtype=dtype, page_size=8, num_pages=pages, max_batch_size=4,
+                                                       max_seq_len=64, device="cuda:0"))
+            (group,) = engine.cache.groups
+            assert list(group.storage) == ["latent"] and group.storage["latent"].shape == (3, pages + 1, 8, 24)
+            group.storage["latent"].fill_(float("nan"))
+            got = helpers.run_steps(engine, steps)
+            engine.cache.audit()
+            assert engine.cache.free_pages() == pages
+            for rid in ref:
+                assert helpers.relative_error(got[rid], ref[rid]) < tol, (dtype, make_steps.__name__, rid)
+            engine.close()
+    # the model cut to its first two layer-order entries, through the ModelSpec (no architecture-specific code)
+    engine = build_engine(folder, EngineConfig(dtype="float32", page_size=8, max_batch_size=2, max_seq_len=64,
+                                               device="cuda:0"), n_layers=2)
+    got = helpers.run_steps(engine, helpers.steps_whole({"r1": requests["r1"]}))
+    assert helpers.relative_error(got["r1"], latent_plain_forward(cfg, w, requests["r1"], layers=2)) < 1e-4
+    engine.close()

@@ -82,7 +82,8 @@ def test_attention_part_with_its_cache(dtype, tol, heads, kv_heads, head_dim, wi
                                                           prefix="a.", position=position, window=window)))
     part.bind(w, rt)
     cache = CacheManager([part.cache_request()], page, 40, 2, 160, rt.device, dtype)
-    cache.groups[0].storage.fill_(float("nan"))
+    for tensor in cache.groups[0].storage.values():
+        tensor.fill_(float("nan"))
     xs = {"a": torch.randn(70, width, generator=g).to(dtype), "b": torch.randn(45, width, generator=g).to(dtype)}
     config = {"num_attention_heads": heads, "num_key_value_heads": kv_heads, "head_dim": head_dim, "hidden_size": width}
     inv_freq = plain_llama.rope_inverse_frequencies(head_dim, 10000.0, None)

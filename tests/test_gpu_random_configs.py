@@ -61,7 +61,8 @@ def test_random_configuration_and_trace(tmp_path, seed):
             engine = build_engine(folder, EngineConfig(dtype=dtype, page_size=page, num_pages=pages, max_batch_size=4,
                                                        max_seq_len=256, device="cuda:0"))
             for g in engine.cache.groups:
-                g.storage.fill_(float("nan"))
+                for tensor in g.storage.values():
+                    tensor.fill_(float("nan"))
             got = helpers.run_steps(engine, steps)
             engine.cache.audit()
             assert engine.cache.free_pages() == engine.cache.num_pages

@@ -24,8 +24,12 @@ class TorchKernels:
         pass
 
     # ------------------------------------------------------------------ elementwise
-    def embedding(self, table, token_ids):
-        return table[token_ids.long()].to(torch.float32)
+    def embedding(self, table, token_ids, scale=1.0):
+        return table[token_ids.long()].to(torch.float32) * scale
+
+    def softcap(self, logits, cap):
+        logits.copy_(cap * torch.tanh(logits / cap))
+        return logits
 
     def add_rmsnorm(self, residual, delta, weight, eps, out_dtype):
         if delta is not None:

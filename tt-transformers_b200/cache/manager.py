@@ -1,13 +1,16 @@
 """The cache manager.
 
-Layers that ask the same thing of the cache form a group: all keys (PagedKV without a
-window), a window of them (PagedKV with one), or a tensor of fixed size per request
-(SlotState). Each paged group has its own page pool, its own device storage
-[units, 2, pages + 1, kv_heads, page_size, head_dim] and, per live request, its own list of
-pages (the block table row). Pages are given back when the request ends, and, in a
-windowed group, as soon as the window has passed them; given-back pages are handed out
-again first. Every live request also owns a slot, which indexes the fixed-size state
-tensors [units, max_slots, ...] of SlotState groups (zeroed at admission).
+Layers that ask the same thing of the cache form a group: all keys (a paged request without
+a window), a window of them (one with a window), or tensors of fixed size per request. A
+request (parts.base.CacheRequest) says by itself which tensors it needs per page or per
+live request, in which dtype, and how a mixer sees them; the manager knows no request kind
+by name. Each paged group has its own page pool, its own device storage
+{name: [units, pages + 1, *page shape]} and, per live request, its own list of pages (the
+block table row). Pages are given back when the request ends, and, in a windowed group, as
+soon as the window has passed them; given-back pages are handed out again first. Every
+live request also owns a slot, which indexes the fixed-size state tensors {name: [units,
+max_slots + 1, ...]} of the other groups (zeroed at admission; the last row belongs to no
+request and takes what padded rows of a captured step write).
 
 The reference keeps per-layer key and value tensors [num_blocks, kv_heads, block_size,
 head_dim] and takes block tables from its caller
@@ -23,7 +26,7 @@ from typing import Dict, List, Optional
 import numpy as np
 import torch
 
-from ..parts.base import PagedKV, PagedKVView, SlotState, SlotStateView
+from ..parts.base import CacheRequest
 from .pages import PagePool
 
 
@@ -42,10 +45,10 @@ class OutOfSlots(RuntimeError):
 @dataclass
 class _Group:
     index: int
-    request: object                       # PagedKV or SlotState
+    request: CacheRequest
     units: List[int] = field(default_factory=list)     # layer-order entries that own a unit here
-    pool: Optional[PagePool] = None
-    storage: Optional[torch.Tensor] = None
+    pool: Optional[PagePool] = None                     # paged groups only
+    storage: Optional[Dict[str, torch.Tensor]] = None   # name -> [units, pages + 1 | max_slots + 1, *shape]
     table: Optional[np.ndarray] = None    # int32 [max_slots, table_width]: the block table of every slot
 
 
@@ -58,10 +61,14 @@ class _Live:
 
 
 class CacheManager:
+    ROLLBACK_SLACK = 1        # tokens by which a committed step may be taken back (the engine looks one step ahead)
+
     def __init__(self, cache_requests, page_size: int, num_pages: int, max_slots: int, max_seq_len: int,
                  device, dtype: torch.dtype, allocate_storage: bool = True):
-        """cache_requests: per entry of the layer order a PagedKV, a SlotState, None, or the
-        index of the entry whose unit it reads (as DecoderModel.cache_requests() gives)."""
+        """cache_requests: per entry of the layer order a CacheRequest (PagedKV, SlotState or a kind of
+        the caller's own), None, or the index of the entry whose unit it reads (as
+        DecoderModel.cache_requests() gives). `dtype`: the compute dtype, for tensors whose request
+        names none."""
         self.page_size, self.num_pages, self.max_slots = int(page_size), int(num_pages), int(max_slots)
         self.max_seq_len = int(max_seq_len)
         self.table_width = -(-self.max_seq_len // self.page_size)
@@ -72,8 +79,8 @@ class CacheManager:
         for entry, req in enumerate(cache_requests):
             if req is None or isinstance(req, int):
                 continue
-            if not isinstance(req, (PagedKV, SlotState)):
-                raise TypeError(f"layer-order entry {entry}: unknown cache request {req!r}")
+            if not isinstance(req, CacheRequest):
+                raise TypeError(f"layer-order entry {entry}: {req!r} is no CacheRequest")
             if req not in by_request:
                 by_request[req] = _Group(index=len(self.groups), request=req)
                 self.groups.append(by_request[req])
@@ -85,16 +92,15 @@ class CacheManager:
                 if req not in self._unit_of_entry:
                     raise ValueError(f"layer-order entry {entry} reads the cache of entry {req}, which has none")
                 self._unit_of_entry[entry] = self._unit_of_entry[req]
+        self.scratch_slot = self.max_slots                     # a state row that no request owns
         for g in self.groups:
-            if isinstance(g.request, PagedKV):
+            if g.request.paged:
                 g.pool = PagePool(self.num_pages)
                 g.table = np.zeros((self.max_slots, self.table_width), dtype=np.int32)
-                if allocate_storage:
-                    g.storage = torch.zeros(len(g.units), 2, self.num_pages + 1, g.request.num_kv_heads,
-                                            self.page_size, g.request.head_dim, dtype=dtype, device=device)
-            elif allocate_storage:
-                g.storage = torch.zeros(len(g.units), self.max_slots, *g.request.shape,
-                                        dtype=torch.float32, device=device)
+            if allocate_storage:
+                rows = self.num_pages + 1 if g.request.paged else self.max_slots + 1
+                g.storage = {name: torch.zeros(len(g.units), rows, *shape, dtype=dt or dtype, device=device)
+                             for name, (shape, dt) in g.request.storage(self.page_size).items()}
         self._free_slots = list(range(self.max_slots - 1, -1, -1))
         self._live: Dict[object, _Live] = {}
 
@@ -133,7 +139,8 @@ class CacheManager:
                 live.pages[g.index] = []
                 g.table[slot, :] = 0
             elif g.storage is not None:
-                g.storage[:, slot].zero_()
+                for tensor in g.storage.values():
+                    tensor[:, slot].zero_()
         self._live[request_id] = live
         return slot
 
@@ -206,8 +213,9 @@ class CacheManager:
         for g in self.groups:
             if g.pool is None or g.request.window is None:
                 continue
-            # the next query sits at position >= new_length and reads keys > position - window
-            first_needed = max(0, new_length - g.request.window + 1)
+            # the next query sits at position >= new_length and reads keys > position - window; a step
+            # taken back (rollback) moves the request's end back by up to ROLLBACK_SLACK positions
+            first_needed = max(0, new_length - self.ROLLBACK_SLACK - g.request.window + 1)
             dead = first_needed // self.page_size            # pages wholly below first_needed
             row = live.pages[g.index]
             freed = [p for p in row[:dead] if p != 0]
@@ -222,13 +230,14 @@ class CacheManager:
 
     def rollback(self, request_id, length: int) -> None:
         """Take back a step that was committed ahead of time and then not used: the request holds
-        `length` tokens again, pages beyond are given back. Not possible once a window has freed
-        pages on the way (has_windows())."""
+        `length` tokens again, pages beyond are given back. With windowed groups at most
+        ROLLBACK_SLACK tokens can be taken back: that far behind its window a request keeps its pages."""
         live = self._live[request_id]
         if length > live.length:
             raise ValueError("rollback goes backwards only")
-        if self.has_windows():
-            raise RuntimeError("a cache with windowed groups cannot roll back")
+        if self.has_windows() and live.length - length > self.ROLLBACK_SLACK:
+            raise RuntimeError(f"a cache with windowed groups can take back {self.ROLLBACK_SLACK} token(s), "
+                               f"not {live.length - length}")
         live.length = length
         self.trim(request_id)
 
@@ -256,11 +265,10 @@ class CacheManager:
             return None
         gi, unit = self._unit_of_entry[entry]
         g = self.groups[gi]
+        tensors = {name: tensor[unit] for name, tensor in g.storage.items()}
         if g.pool is not None:
-            return PagedKVView(keys=g.storage[unit, 0], values=g.storage[unit, 1],
-                               block_table=batch.block_tables[gi], page_size=self.page_size,
-                               window=g.request.window)
-        return SlotStateView(state=g.storage[unit], slots=batch.seg_slot, slot_list=batch.seg_slot_list)
+            return g.request.view(tensors, block_table=batch.block_tables[gi], page_size=self.page_size)
+        return g.request.view(tensors, slots=batch.seg_slot, slot_list=batch.seg_slot_list)
 
     # ------------------------------------------------------------------ invariants (tests)
     def audit(self) -> None:

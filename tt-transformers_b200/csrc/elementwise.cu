@@ -6,7 +6,7 @@
 // ---------------------------------------------------------------- embedding: out[t, :] = table[ids[t], :] as float32
 template <typename T>
 __global__ void embedding_kernel(const T* __restrict__ table, const int* __restrict__ ids, float* __restrict__ out,
-                                 int width, int vocab, int* __restrict__ status) {
+                                 int width, int vocab, float scale, int* __restrict__ status) {
     pdl_wait();
     pdl_launch_dependents();
     const int t = blockIdx.x;
@@ -22,23 +22,28 @@ __global__ void embedding_kernel(const T* __restrict__ table, const int* __restr
         for (int c = threadIdx.x * 8; c < width; c += blockDim.x * 8) {
             float v[8];
             load8(row + c, v);
+            if (scale != 1.f) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] *= scale;
+            }
             store8(dst + c, v);
         }
     } else {
-        for (int c = threadIdx.x; c < width; c += blockDim.x) dst[c] = to_float(row[c]);
+        for (int c = threadIdx.x; c < width; c += blockDim.x) dst[c] = to_float(row[c]) * scale;
     }
 }
 
+// scale: every embedded row is multiplied by it in float32 (1 for none).
 TTB_EXPORT int ttb_embedding(const void* table, int dtype, const int* ids, float* out, int tokens, int width,
-                             int vocab, int* status, cudaStream_t stream) {
+                             int vocab, float scale, int* status, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
     if (!table || !ids || !out || !status) return TTB_ERR_ARGUMENT;
     if (!aligned16(table) || !aligned16(out)) return TTB_ERR_ARGUMENT;
     const int threads = 128;
     if (dtype == TTB_DTYPE_BF16)
-        ttb_launch(embedding_kernel<__nv_bfloat16>, tokens, threads, 0, stream, (const __nv_bfloat16*)table, ids, out, width, vocab, status);
+        ttb_launch(embedding_kernel<__nv_bfloat16>, tokens, threads, 0, stream, (const __nv_bfloat16*)table, ids, out, width, vocab, scale, status);
     else if (dtype == TTB_DTYPE_F32)
-        ttb_launch(embedding_kernel<float>, tokens, threads, 0, stream, (const float*)table, ids, out, width, vocab, status);
+        ttb_launch(embedding_kernel<float>, tokens, threads, 0, stream, (const float*)table, ids, out, width, vocab, scale, status);
     else
         return TTB_ERR_UNSUPPORTED;
     return ttb_launch_status();
@@ -245,5 +250,27 @@ TTB_EXPORT int ttb_gather_rows(const void* src, const int* rows, void* dst, int 
         ttb_launch(gather_rows_kernel<uint16_t>, count, threads, 0, stream, (const uint16_t*)src, rows, (uint16_t*)dst, row_bytes / 2);
     else
         return TTB_ERR_UNSUPPORTED;
+    return ttb_launch_status();
+}
+
+// ---------------------------------------------------------------- x = cap * tanh(x / cap), float32, in place
+// A capped head: logits are squashed into (-cap, cap). Rows are `stride` floats apart.
+__global__ void softcap_kernel(float* __restrict__ x, int cols, int stride, float cap) {
+    pdl_wait();
+    pdl_launch_dependents();
+    float* row = x + (size_t)blockIdx.y * stride;
+    const float inv = 1.f / cap;
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += gridDim.x * blockDim.x)
+        row[c] = cap * tanhf(row[c] * inv);
+}
+
+TTB_EXPORT int ttb_softcap(float* x, int rows, int cols, int stride, float cap, cudaStream_t stream) {
+    if (rows == 0 || cols == 0) return TTB_OK;
+    if (!x || !(cap > 0.f) || stride < cols) return TTB_ERR_ARGUMENT;
+    if (rows > 65535) return TTB_ERR_UNSUPPORTED;
+    const int threads = 256;
+    int bx = (cols + threads - 1) / threads;
+    if (bx > 64) bx = 64;
+    ttb_launch(softcap_kernel, dim3(bx, rows), threads, 0, stream, x, cols, stride, cap);
     return ttb_launch_status();
 }

@@ -209,7 +209,7 @@ class LLM:
         """After this step every request of the plan decodes, nobody can join, nobody ends by
         length, and pages are plentiful: the next step is known but for its token ids."""
         engine, sched = self.engine, self._scheduler
-        if not (self.look_ahead and engine.can_feed_back()) or engine.cache.has_windows() or sched.waiting:
+        if not (self.look_ahead and engine.can_feed_back()) or sched.waiting:
             return False
         if len(plan) != len(sched.running) or not all(e.sample for e in plan):
             return False

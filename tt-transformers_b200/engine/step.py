@@ -136,7 +136,7 @@ class Engine:
             raise ValueError(f"a token id lies outside the vocabulary of {self.vocab_size}")
         seg_lens_all = seg_lens + [1] * pad
         pos0_all = seg_pos0 + [0] * pad
-        slot_all = seg_slot + [0] * pad
+        slot_all = seg_slot + [cache.scratch_slot] * pad      # padded rows own no request's state
         buf[o_tok:o_tok + T - pad] = tokens
         buf[o_tok + T - pad:o_tok + T] = 0
         lens = np.asarray(seg_lens_all, dtype=np.int32)
@@ -272,7 +272,7 @@ class Engine:
         for rid in self.cache.live_requests():
             self.cache.release(rid)
         for g in self.cache.groups:
-            g.storage = None
+            g.storage = None                     # the pages and the state tensors go
         self.graphs = None
 
 
@@ -289,9 +289,10 @@ def build_engine(model_folder: str = None, engine_config: EngineConfig = None, *
         raise ValueError("give a model folder, or config_dict and tensors")
     arch = get_architecture(architecture_of(config_dict))
     cfg = arch.load_config(config_dict)
+    spec = arch.model_spec(cfg)
     if n_layers is not None:
-        cfg = cfg.with_layers(n_layers)
-    model = DecoderModel(arch.model_spec(cfg))
+        spec = spec.first_entries(n_layers)       # the model cut short, whatever the architecture
+    model = DecoderModel(spec)
     specs = model.tensor_specs()
     if model_folder is not None:
         tensors = read_safetensors(model_folder, wanted=[s.name for s in specs] if n_layers is not None else None)

@@ -86,7 +86,7 @@ class CudaKernels:
                      "ttb_gemv_mma", "ttb_gemv_mma_fused", "ttb_gemv_mma_parts", "ttb_argmax", "ttb_attention_decode_merges_in_kernel", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm",
                      "ttb_gemm_tcgen05", "ttb_paged_attention_tcgen05", "ttb_attention_tcgen05_supports",
                      "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge", "ttb_gemv_qkv_rope",
-                     "ttb_gemm_skinny_tcgen05", "ttb_gemm_skinny_tcgen05_rows"):
+                     "ttb_gemm_skinny_tcgen05", "ttb_gemm_skinny_tcgen05_rows", "ttb_softcap"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -162,12 +162,21 @@ class CudaKernels:
             raise EngineDeviceError(what)
 
     # ------------------------------------------------------------------ elementwise
-    def embedding(self, table: torch.Tensor, token_ids: torch.Tensor) -> torch.Tensor:
+    def embedding(self, table: torch.Tensor, token_ids: torch.Tensor, scale: float = 1.0) -> torch.Tensor:
         tokens, (vocab, width) = token_ids.shape[0], table.shape
         out = torch.empty(tokens, width, dtype=torch.float32, device=self.device)
         self._check(self.lib.ttb_embedding(self._p(table), _dtype_code(table.dtype), self._p(token_ids), self._p(out),
-                                           tokens, width, vocab, self._p(self.status), self._stream()), "embedding")
+                                           tokens, width, vocab, ctypes.c_float(scale), self._p(self.status),
+                                           self._stream()), "embedding")
         return out
+
+    def softcap(self, logits: torch.Tensor, cap: float) -> torch.Tensor:
+        """logits = cap * tanh(logits / cap), float32, in place."""
+        if logits.dtype != torch.float32 or logits.dim() != 2 or logits.stride(1) != 1:
+            raise KernelError("softcap: logits must be float32 [rows, columns], contiguous along the columns")
+        self._check(self.lib.ttb_softcap(self._p(logits), logits.shape[0], logits.shape[1], logits.stride(0),
+                                         ctypes.c_float(cap), self._stream()), "softcap")
+        return logits
 
     def add_rmsnorm(self, residual: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Tensor, eps: float,
                     out_dtype: torch.dtype) -> torch.Tensor:

@@ -39,11 +39,13 @@ def model_spec(cfg: LlamaConfig) -> ModelSpec:
     return ModelSpec(
         vocab_size=cfg.vocab_size,
         width=cfg.hidden_size,
-        embedding_name="model.embed_tokens.weight",
+        embedding=PartSpec("table", dict(vocab=cfg.vocab_size, width=cfg.hidden_size,
+                                         weight_name="model.embed_tokens.weight")),
         layers=tuple(layers),
         order=tuple(LayerCall(i) for i in range(cfg.num_hidden_layers)),
         final_norm=PartSpec("rmsnorm", dict(width=cfg.hidden_size, eps=cfg.rms_norm_eps, weight_name="model.norm.weight")),
-        head_name=None if cfg.tie_word_embeddings else "lm_head.weight",
+        head=PartSpec("linear", dict(vocab=cfg.vocab_size, width=cfg.hidden_size,
+                                     weight_name=None if cfg.tie_word_embeddings else "lm_head.weight")),
         max_positions=cfg.max_position_embeddings,
     )
 

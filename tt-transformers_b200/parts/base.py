@@ -29,22 +29,65 @@ class TensorSpec:
 
 
 # ----------------------------------------------------------------------------- what a mixer asks of the cache
+class CacheRequest:
+    """What one layer-order entry asks of the cache manager. A request says by itself what is stored
+    and how a mixer sees it, so the manager knows no kind of request by name:
+
+    `paged` True: storage per token, in pages handed out through a block table per request;
+    `storage(page_size)` gives {name: (shape of ONE page, dtype or None for the compute dtype)}, and the
+    manager keeps each tensor as [units, pages + 1, *shape] (page 0 is the scratch page). `window`
+    None keeps every position; a number lets the manager take back pages that lie wholly more than
+    `window` positions behind the request's end.
+    `paged` False: storage of fixed size per live request; `storage(page_size)` gives {name: (shape
+    of ONE request's state, dtype)}, kept as [units, slots + 1, *shape] and zeroed when a request is
+    admitted (the last row belongs to nobody: padded rows of captured steps point there).
+
+    `view(tensors, ...)` wraps one unit's tensors for the mixer. Requests that compare equal share a
+    group (one pool, one block table per request). Subclasses are frozen dataclasses."""
+
+    paged = True
+    window = None
+
+    def storage(self, page_size: int):
+        raise NotImplementedError
+
+    def view(self, tensors, **step):
+        raise NotImplementedError
+
+
 @dataclass(frozen=True)
-class PagedKV:
+class PagedKV(CacheRequest):
     """Keys and values in pages. `window` None keeps all keys; a number keeps only
     the last `window` positions readable, and pages behind it are given back."""
 
     num_kv_heads: int
     head_dim: int
     window: Optional[int] = None
+    paged = True
+
+    def storage(self, page_size: int):
+        page = (self.num_kv_heads, page_size, self.head_dim)     # one KV head's page is contiguous
+        return {"keys": (page, None), "values": (page, None)}
+
+    def view(self, tensors, *, block_table, page_size, **_):
+        return PagedKVView(keys=tensors["keys"], values=tensors["values"], block_table=block_table,
+                           page_size=page_size, window=self.window)
 
 
 @dataclass(frozen=True)
-class SlotState:
-    """A tensor of fixed shape per live request (float32), zeroed when the request
-    is admitted. Mixers with a running state of their own use this."""
+class SlotState(CacheRequest):
+    """A tensor of fixed shape per live request, zeroed when the request is admitted. Mixers with a
+    running state of their own use this."""
 
     shape: Tuple[int, ...]
+    dtype: torch.dtype = torch.float32
+    paged = False
+
+    def storage(self, page_size: int):
+        return {"state": (tuple(self.shape), self.dtype)}
+
+    def view(self, tensors, *, slots, slot_list, **_):
+        return SlotStateView(state=tensors["state"], slots=slots, slot_list=slot_list)
 
 
 @dataclass
@@ -60,7 +103,7 @@ class PagedKVView:
 
 @dataclass
 class SlotStateView:
-    state: torch.Tensor         # [max_slots, *shape] float32
+    state: torch.Tensor         # [max_slots + 1, *shape]
     slots: torch.Tensor         # int32 [segments] on the device
     slot_list: List[int]        # the same on the host
 
@@ -207,18 +250,73 @@ class PositionEncoding(Part):
         return None
 
 
+class TokenEmbedding(Part):
+    """forward(token_ids int32 [T]) -> float32 [T, width], the start of the residual stream. A head that
+    is tied to the embedding reads its `table` ([vocab, width], compute dtype) after bind."""
+
+    def forward(self, token_ids):
+        raise NotImplementedError
+
+
+class OutputHead(Part):
+    """forward(h [N, width], compute dtype) -> float32 logits [N, vocab]. A head with `tied` True has no
+    weight of its own: the model calls tie(embedding) before bind."""
+
+    tied = False
+
+    def tie(self, embedding: TokenEmbedding) -> None:
+        raise NotImplementedError
+
+    def forward(self, h):
+        raise NotImplementedError
+
+
+class Block:
+    """How the parts of one layer are arranged. `slots` names the parts a block kind is built from and
+    the category each is looked up in; a LayerSpec gives a PartSpec for every name, the model builds
+    them and hands them to the block's constructor as keyword arguments. forward(x, delta, batch,
+    cache, write_cache) -> (x, delta): x is the float32 residual stream (updated in place), delta a
+    sub-layer output that is still to be added (or None). `mixer` is the part whose cache request
+    the entry's cache unit serves and that receives the layer's position encoding."""
+
+    slots: Dict[str, str] = {"norm1": "norm", "mixer": "mixer", "norm2": "norm", "feed_forward": "feed_forward"}
+    takes_next_norm = False
+
+    def parts(self):
+        return [getattr(self, name) for name in self.slots]
+
+    def cache_request(self):
+        return self.mixer.cache_request()
+
+    def graph_safe(self) -> bool:
+        """True if the forward of every mixer and feed-forward just launches kernels on the current stream,
+        with shapes fixed by the batch's shape."""
+        return all(getattr(getattr(self, name), "graph_safe", False)
+                   for name, category in self.slots.items() if category in ("mixer", "feed_forward"))
+
+    def forward(self, x, delta, batch, cache, write_cache=True):
+        raise NotImplementedError
+
+
 # ----------------------------------------------------------------------------- registries
 _REGISTRIES: Dict[str, Dict[str, Callable]] = {
-    "mixer": {}, "feed_forward": {}, "norm": {}, "position": {}, "block": {},
+    "mixer": {}, "feed_forward": {}, "norm": {}, "position": {}, "block": {}, "embedding": {}, "head": {},
 }
 
 
 def register_part(category: str, kind: str, factory: Callable) -> None:
     """Make `factory(**params)` available as `kind` in `category` (mixer,
-    feed_forward, norm, position, block). Registering a kind again replaces it."""
+    feed_forward, norm, position, block, embedding, head). Registering a kind again replaces it."""
     if category not in _REGISTRIES:
         raise KeyError(f"unknown part category {category!r}; known: {sorted(_REGISTRIES)}")
     _REGISTRIES[category][kind] = factory
+
+
+def block_factory(kind: str) -> Callable:
+    table = _REGISTRIES["block"]
+    if kind not in table:
+        raise KeyError(f"no block of kind {kind!r} is registered; known: {sorted(table)}")
+    return table[kind]
 
 
 def build_part(category: str, spec: "PartSpec"):

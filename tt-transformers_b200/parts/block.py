@@ -15,7 +15,7 @@ tensors only, as before.
 
 from __future__ import annotations
 
-from .base import ADDED, DeferredNorm, register_part
+from .base import ADDED, Block, DeferredNorm, register_part
 
 
 def _normed(norm, consumer, x, delta):
@@ -33,14 +33,12 @@ def _following(norm, consumer):
     return None
 
 
-class PreNormBlock:
+class PreNormBlock(Block):
+    slots = {"norm1": "norm", "mixer": "mixer", "norm2": "norm", "feed_forward": "feed_forward"}
+    takes_next_norm = True
+
     def __init__(self, norm1, mixer, norm2, feed_forward):
         self.norm1, self.mixer, self.norm2, self.feed_forward = norm1, mixer, norm2, feed_forward
-
-    def parts(self):
-        return [self.norm1, self.mixer, self.norm2, self.feed_forward]
-
-    takes_next_norm = True
 
     def forward(self, x, delta, batch, cache, write_cache=True, next_norm=None):
         """x: float32 residual, updated in place; delta: pending sub-layer output, None, or ADDED

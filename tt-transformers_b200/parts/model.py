@@ -12,23 +12,43 @@ the j-th call instead. A layer may be named by several calls (shared weights).
 
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass, replace
 from typing import Dict, List, Optional
 
 import torch
 
-from .base import ADDED, DeferredNorm, PartSpec, Runtime, StepBatch, TensorSpec, build_part
-from .embedding import Embedding, Head
+from .base import ADDED, Block, DeferredNorm, PartSpec, Runtime, StepBatch, TensorSpec, build_part, block_factory
 
 
-@dataclass(frozen=True)
+def _block_graph_safe(block) -> bool:
+    safe = getattr(block, "graph_safe", None)
+    if callable(safe):
+        return bool(safe())
+    return all(getattr(p, "graph_safe", False) for p in (block.mixer, block.feed_forward))
+
+
 class LayerSpec:
-    mixer: PartSpec
-    feed_forward: PartSpec
-    norm1: PartSpec
-    norm2: PartSpec
-    position: Optional[PartSpec] = None      # handed to the mixer as `position`
-    block: str = "pre_norm"
+    """One layer as data: the block kind, a PartSpec for every part that block kind is built from
+    (by the names in its `slots`: norm1, mixer, norm2, feed_forward for `pre_norm`; a block kind with
+    more parts, say norms after its sub-layers, names more), and the position encoding handed to
+    the layer's mixer as `position`."""
+
+    __slots__ = ("block", "position", "parts")
+
+    def __init__(self, block: str = "pre_norm", position: Optional[PartSpec] = None, **parts: PartSpec):
+        for name, spec in parts.items():
+            if not isinstance(spec, PartSpec):
+                raise TypeError(f"LayerSpec: part {name!r} must be a PartSpec, got {type(spec).__name__}")
+        self.block, self.position, self.parts = block, position, dict(parts)
+
+    def __getattr__(self, name):                 # spec.mixer, spec.norm1, ... read like fields
+        parts = object.__getattribute__(self, "parts")
+        if name in parts:
+            return parts[name]
+        raise AttributeError(name)
+
+    def __repr__(self):
+        return f"LayerSpec(block={self.block!r}, position={self.position!r}, parts={self.parts!r})"
 
 
 @dataclass(frozen=True)
@@ -41,39 +61,55 @@ class LayerCall:
 class ModelSpec:
     vocab_size: int
     width: int
-    embedding_name: str
+    embedding: PartSpec                      # category "embedding"
     layers: tuple                            # of LayerSpec
     order: tuple                             # of LayerCall
     final_norm: PartSpec
-    head_name: Optional[str]                 # None: tied to the embedding
+    head: PartSpec                           # category "head"
     input_position: Optional[PartSpec] = None  # a position encoding applied to the embedded tokens
     max_positions: int = 1 << 30
+
+    def first_entries(self, count: int) -> "ModelSpec":
+        """The same model cut to the first `count` entries of its layer order (for runs that want fewer
+        layers than the checkpoint has). Layers that no remaining entry names are dropped."""
+        if not 1 <= count <= len(self.order):
+            raise ValueError(f"the layer order has {len(self.order)} entries; cannot keep {count}")
+        order = self.order[:count]
+        used = sorted({call.layer for call in order})
+        renumber = {old: new for new, old in enumerate(used)}
+        return replace(self, layers=tuple(self.layers[i] for i in used),
+                       order=tuple(LayerCall(renumber[c.layer], c.cache_of) for c in order))
 
 
 class DecoderModel:
     def __init__(self, spec: ModelSpec):
         self.spec = spec
-        self.embedding = Embedding(spec.vocab_size, spec.width, spec.embedding_name)
-        self.head = Head(spec.vocab_size, spec.width, spec.head_name,
-                         tied_to=self.embedding if spec.head_name is None else None)
+        self.embedding = build_part("embedding", spec.embedding)
+        self.head = build_part("head", spec.head)
+        if getattr(self.head, "tied", False):
+            self.head.tie(self.embedding)
         self.final_norm = build_part("norm", spec.final_norm)
         self.input_position = build_part("position", spec.input_position) if spec.input_position else None
         self.layers = []
         positions: Dict[PartSpec, object] = {}
-        for ls in spec.layers:
+        for number, ls in enumerate(spec.layers):
             position = None
             if ls.position is not None:
                 if ls.position not in positions:          # layers with the same encoding share one object
                     positions[ls.position] = build_part("position", ls.position)
                 position = positions[ls.position]
-            mixer_params = dict(ls.mixer.params)
-            if position is not None:
-                mixer_params["position"] = position
-            mixer = build_part("mixer", PartSpec(ls.mixer.kind, mixer_params))
-            block = build_part("block", PartSpec(ls.block, dict(
-                norm1=build_part("norm", ls.norm1), mixer=mixer,
-                norm2=build_part("norm", ls.norm2), feed_forward=build_part("feed_forward", ls.feed_forward))))
-            self.layers.append(block)
+            factory = block_factory(ls.block)
+            slots = getattr(factory, "slots", Block.slots)
+            if set(ls.parts) != set(slots):
+                raise ValueError(f"layer {number}: block kind {ls.block!r} is built from {sorted(slots)}, "
+                                 f"the layer names {sorted(ls.parts)}")
+            built = {}
+            for name, category in slots.items():
+                part_spec = ls.parts[name]
+                if category == "mixer" and position is not None:
+                    part_spec = PartSpec(part_spec.kind, dict(part_spec.params, position=position))
+                built[name] = build_part(category, part_spec)
+            self.layers.append(factory(**built))
         self.positions = list(positions.values())
         for i, call in enumerate(spec.order):
             if not 0 <= call.layer < len(self.layers):
@@ -109,7 +145,7 @@ class DecoderModel:
         """True if every mixer and feed-forward says that its forward only launches kernels
         on the current stream with shapes fixed by the batch's shape (no host reads, no
         per-step host tables), so that a decode step may be captured and replayed."""
-        return all(getattr(p, "graph_safe", False) for b in self.layers for p in (b.mixer, b.feed_forward))
+        return all(_block_graph_safe(b) for b in self.layers)
 
     # ------------------------------------------------------------------ cache needs
     def cache_requests(self):
@@ -120,7 +156,7 @@ class DecoderModel:
             if call.cache_of is not None:
                 out.append(call.cache_of)
             else:
-                out.append(self.layers[call.layer].mixer.cache_request())
+                out.append(self.layers[call.layer].cache_request())
         return out
 
     # ------------------------------------------------------------------ one step
