@@ -6,7 +6,8 @@ were run once, on small inputs, to anchor the plain implementation:
   - the Llama-3 frequency scaling, src/tt_transformers/models/llama3_8b/hf_generator.py:88-103
     (the module imports the accelerator library at the top, so a stand-in object is put in
     sys.modules for the import; the function itself uses only torch and math);
-  - the host sampler _select, src/tt_transformers/models/hf_generation.py:125-148;
+  - the host sampler _select, src/tt_transformers/models/hf_generation.py:125-148 (its choices where they
+    are deterministic, and, for random settings, the set of tokens it may draw and their probabilities);
   - the checkpoint-row permutation reverse_permute, src/tt_transformers/models/llama32_1b/weight_utils.py:23-25,
     with the pair-swap matrix of src/tt_transformers/tensor_utils.py:91-112, to show that rotating
     interleaved pairs of permuted rows equals rotating (i, i + d/2) of the checkpoint's rows.
@@ -54,6 +55,24 @@ def main(reference_root):
                                                  top_k=1, top_p=1.0, active=active)
     out["select_top_p_small"] = hf_generation._select(logits, batch_size=6, vocab_size=50, do_sample=True,
                                                       temperature=0.7, top_k=0, top_p=1e-4, active=active)
+
+    # Which tokens _select may draw, for settings where sampling is random: the probabilities it hands to
+    # torch.multinomial are caught on the way (the function itself runs unchanged); a token is allowed where
+    # its probability is positive. Logits: 400 values spread so that no cut falls within rounding of a token.
+    wide = torch.randn(3, 400, generator=gen) * 2.5
+    out["allowed_logits"] = wide
+    out["allowed"] = []
+    real_multinomial = torch.multinomial
+    for temperature, top_k, top_p in ((1.0, 0, 0.9), (0.8, 100, 1.0), (1.3, 50, 0.8), (1.0, 0, 0.5), (0.7, 200, 0.95)):
+        caught = []
+        torch.multinomial = lambda probs, num_samples, **kw: (caught.append(probs.clone()), real_multinomial(probs, num_samples, **kw))[1]
+        try:
+            hf_generation._select(wide, batch_size=3, vocab_size=400, do_sample=True, temperature=temperature,
+                                  top_k=top_k, top_p=top_p, active=torch.ones(3, dtype=torch.bool))
+        finally:
+            torch.multinomial = real_multinomial
+        out["allowed"].append(dict(temperature=temperature, top_k=top_k, top_p=top_p, mask=caught[0] > 0,
+                                   probs=caught[0]))
 
     from tt_transformers.models.llama32_1b.weight_utils import reverse_permute
     from tt_transformers.tensor_utils import get_rot_transformation_mat

@@ -186,6 +186,23 @@ def greedy(config, w, prompt, steps):
     return seq[len(prompt):]
 
 
+def host_allowed(row, top_k, top_p):
+    """Which tokens of one row of (temperature-scaled) scores may be drawn: a boolean mask.
+    src/tt_transformers/models/hf_generation.py:138-146."""
+    allowed = torch.ones_like(row, dtype=torch.bool)
+    if top_k:
+        kth = torch.sort(row, descending=True).values[min(top_k, row.numel()) - 1]
+        allowed &= row >= kth
+    if top_p < 1.0:
+        masked = torch.where(allowed, row, torch.full_like(row, float("-inf")))
+        order = torch.argsort(masked)  # ascending: the tail comes first
+        tail_mass = torch.cumsum(torch.softmax(masked, dim=-1)[order], dim=-1)
+        drop = tail_mass <= 1.0 - top_p
+        drop[-1] = False
+        allowed[order[drop]] = False
+    return allowed
+
+
 def host_select(scores, do_sample, temperature, top_k, top_p, generator=None):
     """Host sampler: which tokens may be drawn, and the draw.
 
@@ -200,17 +217,7 @@ def host_select(scores, do_sample, temperature, top_k, top_p, generator=None):
         return torch.argmax(scores, dim=-1)
     picks = []
     for row in scores / temperature:
-        allowed = torch.ones_like(row, dtype=torch.bool)
-        if top_k:
-            kth = torch.sort(row, descending=True).values[min(top_k, row.numel()) - 1]
-            allowed &= row >= kth
-        if top_p < 1.0:
-            masked = torch.where(allowed, row, torch.full_like(row, float("-inf")))
-            order = torch.argsort(masked)  # ascending: the tail comes first
-            tail_mass = torch.cumsum(torch.softmax(masked, dim=-1)[order], dim=-1)
-            drop = tail_mass <= 1.0 - top_p
-            drop[-1] = False
-            allowed[order[drop]] = False
+        allowed = host_allowed(row, top_k, top_p)
         probs = torch.softmax(torch.where(allowed, row, torch.full_like(row, float("-inf"))), dim=-1)
         picks.append(torch.multinomial(probs, 1, generator=generator)[0])
     return torch.stack(picks)

@@ -49,6 +49,17 @@ def test_temperature_sampling_is_reproducible_and_independent_of_the_batch(tiny_
     out = llm.generate(torch.tensor([prompts[0]]), max_new_tokens=5, do_sample=True, temperature=0.8, top_k=20, top_p=0.9, seed=3)
     again = llm.generate(torch.tensor([prompts[0]]), max_new_tokens=5, do_sample=True, temperature=0.8, top_k=20, top_p=0.9, seed=3)
     assert torch.equal(out, again) and out.shape == (1, 10)
+    # the reference's host sampler takes any top_k, and top_p without top_k cuts over the whole vocabulary
+    # (src/tt_transformers/models/hf_generation.py:138-146): so does generate(), and so do requests
+    for top_k, top_p in ((0, 0.9), (100, 1.0), (300, 0.5)):
+        a = llm.generate([prompts[1]], max_new_tokens=6, do_sample=True, temperature=1.1, top_k=top_k, top_p=top_p, seed=9)
+        b = llm.generate([prompts[1]], max_new_tokens=6, do_sample=True, temperature=1.1, top_k=top_k, top_p=top_p, seed=9)
+        assert a == b and len(a[0]) == 6
+    wide = llm.generate([prompts[1]], max_new_tokens=12, do_sample=True, temperature=5.0, top_k=0, top_p=1.0, seed=9)
+    tight = llm.generate([prompts[1]], max_new_tokens=12, do_sample=True, temperature=5.0, top_k=0, top_p=1e-6, seed=9)
+    greedy = llm.generate([prompts[1]], max_new_tokens=12)
+    assert tight == greedy and wide != greedy         # a top_p that keeps the best token alone is greedy decoding
+    llm.cleanup()
 
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16"])

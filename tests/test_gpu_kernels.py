@@ -214,6 +214,37 @@ def test_partial_rotation_and_no_rotation(kernels, twin, dtype):
         assert torch.equal(view.values, view2.values)
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_rotation_of_neighbouring_pairs(kernels, twin, dtype):
+    """`interleaved`: pair (2i, 2i + 1) instead of (i, i + d/2). Against the twin, and against what the reference's
+    own pair-swap matrix gives on rows in its interleaved order (tests/golden/make_golden.py)."""
+    import os
+
+    for heads, kv_heads, head_dim, rotary_dim in ((4, 2, 32, 32), (3, 1, 64, 64), (2, 2, 48, 16)):
+        qkv, batch, view = make_paged_case(dtype, heads, kv_heads, head_dim, 8, [(3, 9), (20, 1)], seed=6)
+        inv_freq = (1.0 / (10000.0 ** (torch.arange(0, rotary_dim, 2).float() / rotary_dim))).cuda()
+        qkv2 = qkv.clone()
+        view2 = SimpleNamespace(keys=view.keys.clone(), values=view.values.clone(), block_table=view.block_table,
+                                page_size=8, window=None)
+        kernels.rope_kv_write(qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, interleaved=True)
+        twin.rope_kv_write(qkv2, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view2, interleaved=True)
+        close(qkv[:, :heads * head_dim], qkv2[:, :heads * head_dim], dtype)
+        close(view.keys, view2.keys, dtype)
+        assert torch.equal(view.values, view2.values)
+    if dtype != torch.float32:
+        return
+    golden = torch.load(os.path.join(os.path.dirname(__file__), "golden", "reference_parts.pt"))
+    heads, hd = golden["rope_heads"], golden["rope_head_dim"]
+    q = (golden["rope_x"] @ golden["rope_w"].T).view(3, heads, hd)           # the checkpoint's row order
+    meta = torch.stack([q[..., :hd // 2], q[..., hd // 2:]], dim=-1).flatten(-2)   # the reference's interleaved order
+    qkv = torch.cat([meta.reshape(3, heads * hd), torch.zeros(3, 2 * hd)], 1).cuda().contiguous()
+    batch = SimpleNamespace(positions=golden["rope_pos"].to(torch.int32).cuda(),
+                            seg_of_token=torch.zeros(3, dtype=torch.int32, device="cuda"))
+    kernels.rope_kv_write(qkv, batch, golden["rope_inv_freq"].cuda(), hd, heads, 1, hd, None, write_kv=False,
+                          interleaved=True)
+    assert torch.allclose(qkv[:, :heads * hd].cpu().view(3, heads, hd), golden["rope_rotated_meta"], atol=1e-5)
+
+
 def test_attention_finds_a_far_key(kernels):
     """One key among hundreds is made to stand out; the output must be its value."""
     heads, kv_heads, head_dim, page_size = 2, 1, 64, 16
@@ -328,7 +359,9 @@ def test_sample(kernels, twin, vocab, rows):
     seeds = torch.arange(rows, device="cuda", dtype=torch.int64) * 7919 + 1
     for counter in range(4):
         counters = torch.full((rows,), counter, device="cuda", dtype=torch.int32)
-        for top_k, top_p in ((0, 1.0), (5, 1.0), (40, 0.7), (1, 1.0), (64, 0.2)):
+        for top_k, top_p in ((0, 1.0), (5, 1.0), (40, 0.7), (1, 1.0), (64, 0.2), (0, 0.9), (100, 1.0), (90, 0.6), (0, 0.3)):
+            if top_k > vocab:
+                continue
             k = torch.full((rows,), top_k, device="cuda", dtype=torch.int32)
             p = torch.full((rows,), top_p, device="cuda")
             got = kernels.sample(logits, temperature, k, p, seeds, counters).cpu()
@@ -338,6 +371,33 @@ def test_sample(kernels, twin, vocab, rows):
             assert agree >= 0.9, (top_k, top_p, got.tolist(), ref.tolist())
     for s, c in ((0, 0), (1, 5), (2 ** 40 + 3, 77)):
         assert abs(kernels.uniform(s, c) - twin.uniform(s, c)) < 1e-7
+
+
+def test_sample_draws_exactly_from_the_sets_the_references_host_sampler_allows(kernels):
+    """2,000 draws per setting on fixed logits: every drawn token is one the reference's _select may draw
+    (src/tt_transformers/models/hf_generation.py:138-146; the sets were taken from that function), every allowed
+    token of some weight is drawn, and the frequencies follow its probabilities. Settings: top_p over the whole
+    vocabulary, top_k beyond the kernel's candidate list, both together, and the candidate-list path."""
+    import os
+
+    golden = torch.load(os.path.join(os.path.dirname(__file__), "golden", "reference_parts.pt"))
+    logits, draws = golden["allowed_logits"], 2000
+    settings = {(c["top_k"], c["top_p"]) for c in golden["allowed"]}
+    assert {(0, 0.9), (100, 1.0), (50, 0.8)} <= settings
+    for case in golden["allowed"]:
+        for row in range(logits.shape[0]):
+            rows = logits[row][None].repeat(draws, 1).cuda()
+            picks = kernels.sample(rows, torch.full((draws,), case["temperature"], device="cuda"),
+                                   torch.full((draws,), case["top_k"], dtype=torch.int32, device="cuda"),
+                                   torch.full((draws,), case["top_p"], device="cuda"),
+                                   torch.full((draws,), 4242 + row, dtype=torch.int64, device="cuda"),
+                                   torch.arange(draws, dtype=torch.int32, device="cuda")).cpu().long()
+            freq = torch.bincount(picks, minlength=logits.shape[1]).float() / draws
+            allowed, probs = case["mask"][row], case["probs"][row]
+            what = (case["temperature"], case["top_k"], case["top_p"], row)
+            assert not bool(((freq > 0) & ~allowed).any()), what              # nothing outside the set
+            assert bool((freq > 0)[probs >= 0.006].all()), what               # (1 - 0.006)^2000 = 6e-6
+            assert float((freq - probs).abs().sum()) / 2 < 0.08, what         # total variation
 
 
 def test_sample_distribution(kernels):

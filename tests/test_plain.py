@@ -52,6 +52,20 @@ def test_host_sampler_equals_the_references_where_it_is_deterministic():
     assert torch.equal(plain_llama.host_select(logits, True, 0.7, 0, 1e-4), GOLDEN["select_top_p_small"])
 
 
+def test_host_sampler_allows_the_tokens_the_reference_allows():
+    """For random settings: the set of tokens that may be drawn, and their probabilities, as the reference's
+    _select handed them to its draw."""
+    logits = GOLDEN["allowed_logits"]
+    assert len(GOLDEN["allowed"]) >= 5
+    for case in GOLDEN["allowed"]:
+        for row in range(logits.shape[0]):
+            scaled = logits[row] / case["temperature"]
+            mask = plain_llama.host_allowed(scaled, case["top_k"], case["top_p"])
+            assert torch.equal(mask, case["mask"][row]), (case["top_k"], case["top_p"], row)
+            probs = torch.softmax(torch.where(mask, scaled, torch.full_like(scaled, float("-inf"))), dim=-1)
+            assert torch.allclose(probs, case["probs"][row], atol=1e-6)
+
+
 def test_host_sampler_respects_its_cuts():
     gen = torch.Generator().manual_seed(0)
     logits = torch.tensor([[5.0, 4.0, 3.0, 2.0, 1.0, 0.0]]).repeat(300, 1)
@@ -87,6 +101,30 @@ def test_rotation_keeps_lengths_and_depends_on_distance_only():
         kk = plain_llama.rope_rotate(k, torch.tensor([p]), f)
         dots.append(float((qq * kk).sum()))
     assert max(dots) - min(dots) < 1e-4
+
+
+def test_rms_norm_equals_torchs_and_swiglu_the_references_expression():
+    """The reference's module tests take torch.nn.RMSNorm(dim, eps) as what its norm must equal
+    (tests/modules/rmsnorm/test_rmsnorm_1d.py:744-748) and the expression (silu(x @ w1) * (x @ w3)) @ w2 as what
+    its feed-forward must equal (tests/modules/mlp/test_mlp_1d.py:675-676, weights [in, out] there)."""
+    g = torch.Generator().manual_seed(3)
+    for width, eps in ((64, 1e-5), (96, 1e-6), (80, 1e-2)):
+        x = torch.randn(7, width, generator=g) * 3
+        norm = torch.nn.RMSNorm(width, eps=eps)
+        with torch.no_grad():
+            norm.weight.copy_(1 + 0.3 * torch.randn(width, generator=g))
+            want = norm(x)
+        assert torch.allclose(plain_llama.rms_norm(x, norm.weight.detach(), eps), want, atol=1e-6, rtol=1e-5)
+        assert torch.allclose(plain_llama.rms_norm(x, norm.weight.detach(), eps),
+                              torch.nn.functional.rms_norm(x, (width,), norm.weight.detach(), eps), atol=1e-6, rtol=1e-5)
+    width, inter = 48, 112
+    x = torch.randn(5, width, generator=g)
+    w1, w3 = torch.randn(width, inter, generator=g) * 0.2, torch.randn(width, inter, generator=g) * 0.2
+    w2 = torch.randn(inter, width, generator=g) * 0.2
+    want = (torch.nn.functional.silu(x @ w1) * (x @ w3)) @ w2
+    weights = {"gate_proj.weight": w1.T.contiguous(), "up_proj.weight": w3.T.contiguous(),
+               "down_proj.weight": w2.T.contiguous()}
+    assert torch.allclose(plain_llama.swiglu(x, weights, ""), want, atol=1e-6)
 
 
 def test_rms_norm_and_swiglu_by_hand():
@@ -133,3 +171,24 @@ def test_tied_and_untied_heads():
     w2["lm_head.weight"] = torch.zeros_like(w["model.embed_tokens.weight"])
     assert torch.equal(plain_llama.forward(TINY_A, w2, [1, 2, 3]), logits)          # tied: lm_head is not read
     assert float(plain_llama.forward(dict(TINY_A, tie_word_embeddings=False), w2, [1, 2, 3]).abs().max()) == 0
+
+
+def test_the_kernel_twins_sampler_draws_from_the_references_allowed_sets():
+    """tests/torch_kernels.py states the device sampler's rules in plain torch; its draws stay within the sets the
+    reference's _select allows, for top_p over the whole vocabulary and top_k beyond the kernel's candidate list."""
+    from torch_kernels import TorchKernels
+
+    twin = TorchKernels()
+    logits = GOLDEN["allowed_logits"]
+    draws = 200
+    for case in GOLDEN["allowed"]:
+        for row in range(logits.shape[0]):
+            rows = logits[row][None].repeat(draws, 1)
+            picks = twin.sample(rows, torch.full((draws,), case["temperature"]),
+                                torch.full((draws,), case["top_k"], dtype=torch.int32), torch.full((draws,), case["top_p"]),
+                                torch.full((draws,), 99 + row, dtype=torch.int64), torch.arange(draws, dtype=torch.int32))
+            drawn = torch.zeros(logits.shape[1], dtype=torch.bool)
+            drawn[picks.long()] = True
+            allowed, probs = case["mask"][row], case["probs"][row]
+            assert not bool((drawn & ~allowed).any()), (case["top_k"], case["top_p"], row)
+            assert bool(drawn[probs >= 0.08].all())

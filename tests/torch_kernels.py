@@ -56,11 +56,19 @@ class TorchKernels:
         return None          # the twin has no fused form: the caller runs projection, rotation and write one by one
 
     # ------------------------------------------------------------------ attention
-    def rope_kv_write(self, qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True):
+    def rope_kv_write(self, qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True,
+                      interleaved=False):
         T = qkv.shape[0]
         x = qkv.view(T, heads + 2 * kv_heads, head_dim)
         n_rot = heads + kv_heads
-        if rotary_dim:
+        if rotary_dim and interleaved:
+            angles = batch.positions.to(torch.float32)[:, None] * inv_freq[None, :]
+            cos, sin = torch.cos(angles)[:, None, :], torch.sin(angles)[:, None, :]
+            a = x[:, :n_rot, 0:rotary_dim:2].float().clone()
+            b = x[:, :n_rot, 1:rotary_dim:2].float().clone()
+            x[:, :n_rot, 0:rotary_dim:2] = (a * cos - b * sin).to(qkv.dtype)
+            x[:, :n_rot, 1:rotary_dim:2] = (b * cos + a * sin).to(qkv.dtype)
+        elif rotary_dim:
             half = rotary_dim // 2
             angles = batch.positions.to(torch.float32)[:, None] * inv_freq[None, :]
             cos, sin = torch.cos(angles)[:, None, :], torch.sin(angles)[:, None, :]
@@ -128,13 +136,29 @@ class TorchKernels:
             k = int(top_k[r]) if top_k is not None else 0
             p_limit = float(top_p[r]) if top_p is not None else 1.0
             probs = torch.exp((l - l[best]) / temp)
-            if k <= 0:
+            if k <= 0 or k > self.max_top_k:
+                # cuts as thresholds on the value: below the k-th largest logit, then the low tail that holds at
+                # most 1 - top_p of what is left; logits equal to a threshold stay; the draw walks the ids in order
+                keep = torch.ones(vocab, dtype=torch.bool)
+                if 0 < k < vocab:
+                    keep &= l >= torch.sort(l, descending=True).values[k - 1]
+                if p_limit < 1.0:
+                    masked = torch.where(keep, probs.double(), torch.zeros((), dtype=torch.float64))
+                    limit = (1.0 - p_limit) * float(masked.sum())
+                    values, order = torch.sort(l)                        # ascending
+                    mass = torch.cumsum(masked[order], 0)
+                    first = torch.searchsorted(values, values, right=False)   # where each value's equals begin
+                    below = torch.where(first > 0, mass[(first - 1).clamp(min=0)], torch.zeros((), dtype=torch.float64))
+                    fits = (below <= limit) & keep[order]
+                    t = values[int(fits.nonzero().max())]                # the largest value whose lower tail fits
+                    keep &= l >= torch.minimum(t, l[best])
+                probs = torch.where(keep, probs, torch.zeros(()))
                 cdf = torch.cumsum(probs.double(), 0)
                 target = u * float(cdf[-1])
                 pick = int(torch.searchsorted(cdf, torch.tensor(target, dtype=torch.float64), right=True))
                 out[r] = min(pick, vocab - 1)
                 continue
-            k = min(k, vocab, self.max_top_k)
+            k = min(k, vocab)
             order = sorted(range(vocab), key=lambda i: (-float(l[i]), i))[:k]
             cand = probs[order].double()
             keep = k

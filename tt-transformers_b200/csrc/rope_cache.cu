@@ -3,8 +3,10 @@
 // rotation itself are float32; accurate sincosf (no fast-math).
 //
 // qkv row layout: [ heads * head_dim | kv_heads * head_dim | kv_heads * head_dim ].
-// Rotation pairs element i with element i + rotary_dim/2 of each head, for i < rotary_dim/2;
-// elements from rotary_dim on are left as they are.
+// Rotation pairs element i with element i + rotary_dim/2 of each head, for i < rotary_dim/2
+// (the checkpoint's row order), or, with `interleaved`, element 2i with element 2i + 1 (the
+// order of models whose projections were trained on neighbouring pairs); elements from
+// rotary_dim on are left as they are.
 // Page layout: [num_pages, kv_heads, page_size, head_dim].
 #include "common.cuh"
 
@@ -14,7 +16,7 @@ __global__ void rope_kv_write_kernel(T* __restrict__ qkv, const int* __restrict_
                                      int rotary_dim, int heads, int kv_heads, int head_dim,
                                      T* __restrict__ key_pages, T* __restrict__ value_pages,
                                      const int* __restrict__ block_table, int table_width, int page_size,
-                                     int num_pages, int write_kv, int* __restrict__ status) {
+                                     int num_pages, int write_kv, int interleaved, int* __restrict__ status) {
     extern __shared__ float trig[];  // cos[rotary_dim/2], sin[rotary_dim/2]
     pdl_wait();
     pdl_launch_dependents();
@@ -81,15 +83,17 @@ __global__ void rope_kv_write_kernel(T* __restrict__ qkv, const int* __restrict_
             *reinterpret_cast<uint4*>(dst + i + half) = hi;
         }
     } else {
-    // queries: rotate in place
+    // queries: rotate in place. Pair i is (i, i + half_rot), or (2i, 2i + 1) when interleaved.
+    const int first = interleaved ? 2 : 1, apart = interleaved ? 1 : half_rot;
     for (int w = threadIdx.x; w < heads * half; w += blockDim.x) {
         const int h = w / half, i = w - h * half;
         if (i >= half_rot) continue;
         T* q = row + h * head_dim;
-        const float a = to_float(q[i]), b = to_float(q[i + half_rot]);
+        const int ia = first * i, ib = ia + apart;
+        const float a = to_float(q[ia]), b = to_float(q[ib]);
         const float c = trig[i], s = trig[half_rot + i];
-        q[i] = from_float<T>(a * c - b * s);
-        q[i + half_rot] = from_float<T>(b * c + a * s);
+        q[ia] = from_float<T>(a * c - b * s);
+        q[ib] = from_float<T>(b * c + a * s);
     }
     if (!write_kv) return;
 
@@ -114,10 +118,11 @@ __global__ void rope_kv_write_kernel(T* __restrict__ qkv, const int* __restrict_
         // keys: element i pairs with i + half_rot when i < half_rot; the rest is copied.
         // Work item i covers elements i and i + half, so that every element is written once.
         if (i < half_rot) {
-            const float a = to_float(k[i]), b = to_float(k[i + half_rot]);
+            const int ia = first * i, ib = ia + apart;
+            const float a = to_float(k[ia]), b = to_float(k[ib]);
             const float c = trig[i], s = trig[half_rot + i];
-            key_pages[dst + i] = from_float<T>(a * c - b * s);
-            key_pages[dst + i + half_rot] = from_float<T>(b * c + a * s);
+            key_pages[dst + ia] = from_float<T>(a * c - b * s);
+            key_pages[dst + ib] = from_float<T>(b * c + a * s);
         }
         value_pages[dst + i] = v[i];
         value_pages[dst + i + half] = v[i + half];
@@ -137,8 +142,8 @@ __global__ void rope_kv_write_kernel(T* __restrict__ qkv, const int* __restrict_
 TTB_EXPORT int ttb_rope_kv_write(void* qkv, int dtype, const int* positions, const int* seg_of_token,
                                  const float* inv_freq, int rotary_dim, int tokens, int heads, int kv_heads,
                                  int head_dim, void* key_pages, void* value_pages, const int* block_table,
-                                 int table_width, int page_size, int num_pages, int write_kv, int* status,
-                                 cudaStream_t stream) {
+                                 int table_width, int page_size, int num_pages, int write_kv, int interleaved,
+                                 int* status, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
     if (!qkv || !positions || !status) return TTB_ERR_ARGUMENT;
     if (write_kv && (!key_pages || !value_pages || !block_table || !seg_of_token)) return TTB_ERR_ARGUMENT;
@@ -148,26 +153,26 @@ TTB_EXPORT int ttb_rope_kv_write(void* qkv, int dtype, const int* positions, con
     const int threads = 256;
     const size_t smem = (size_t)(rotary_dim > 0 ? rotary_dim : 2) * sizeof(float);
     const int elem = dtype == TTB_DTYPE_BF16 ? 2 : 4;
-    const bool vec = rotary_dim == head_dim && head_dim % (32 / elem) == 0 && aligned16(qkv) &&
+    const bool vec = !interleaved && rotary_dim == head_dim && head_dim % (32 / elem) == 0 && aligned16(qkv) &&
                      (!write_kv || (aligned16(key_pages) && aligned16(value_pages)));
     if (vec && dtype == TTB_DTYPE_BF16)
         ttb_launch(rope_kv_write_kernel<__nv_bfloat16, true>, tokens, threads, smem, stream,
             (__nv_bfloat16*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
             (__nv_bfloat16*)key_pages, (__nv_bfloat16*)value_pages, block_table, table_width, page_size, num_pages,
-            write_kv, status);
+            write_kv, interleaved, status);
     else if (vec && dtype == TTB_DTYPE_F32)
         ttb_launch(rope_kv_write_kernel<float, true>, tokens, threads, smem, stream,
             (float*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
-            (float*)key_pages, (float*)value_pages, block_table, table_width, page_size, num_pages, write_kv, status);
+            (float*)key_pages, (float*)value_pages, block_table, table_width, page_size, num_pages, write_kv, interleaved, status);
     else if (dtype == TTB_DTYPE_BF16)
         ttb_launch(rope_kv_write_kernel<__nv_bfloat16, false>, tokens, threads, smem, stream,
             (__nv_bfloat16*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
             (__nv_bfloat16*)key_pages, (__nv_bfloat16*)value_pages, block_table, table_width, page_size, num_pages,
-            write_kv, status);
+            write_kv, interleaved, status);
     else if (dtype == TTB_DTYPE_F32)
         ttb_launch(rope_kv_write_kernel<float, false>, tokens, threads, smem, stream,
             (float*)qkv, positions, seg_of_token, inv_freq, rotary_dim, heads, kv_heads, head_dim,
-            (float*)key_pages, (float*)value_pages, block_table, table_width, page_size, num_pages, write_kv, status);
+            (float*)key_pages, (float*)value_pages, block_table, table_width, page_size, num_pages, write_kv, interleaved, status);
     else
         return TTB_ERR_UNSUPPORTED;
     return ttb_launch_status();

@@ -5,8 +5,14 @@
 //                             request's stream does not depend on its place in the batch.
 //   top_k in 1..SAMPLE_MAX_K  only the k largest logits take part (lowest id first among equal
 //                             ones); they are walked from the largest down.
-//   top_p < 1 (needs top_k)   of those, the low tail whose cumulative probability is <= 1 - top_p
+//   top_p < 1                 of those, the low tail whose cumulative probability is <= 1 - top_p
 //                             is left out; the largest always stays.
+//   top_k > SAMPLE_MAX_K, or top_p < 1 without top_k: the cuts are found as thresholds on the logit's
+//                             value, by bisection over its 32 bits (no sorting): first the value of
+//                             the k-th largest logit, everything below it is out; then the largest
+//                             value t such that the logits below t (of those still in) hold at most
+//                             1 - top_p of the probability, and everything below t is out. Logits
+//                             equal to a threshold all stay. The draw walks the vocabulary in id order.
 #include "common.cuh"
 
 #define SAMPLE_THREADS 1024
@@ -18,6 +24,12 @@ __host__ __device__ __forceinline__ float uniform_from(uint64_t seed, uint64_t c
     x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
     x = x ^ (x >> 31);
     return (float)(x >> 40) * (1.0f / 16777216.0f);
+}
+
+// float -> unsigned key with the same order (larger float, larger key)
+__device__ __forceinline__ uint32_t ordered_key(float f) {
+    const uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
 struct Best {
@@ -80,12 +92,52 @@ sample_kernel(const float* __restrict__ logits, int ld, int vocab, const float* 
     int k = top_k ? top_k[row] : 0;
     if (k > vocab) k = vocab;
 
-    if (k <= 0) {
-        // whole vocabulary: thread `tid` owns the contiguous ids [tid * chunk, (tid + 1) * chunk)
+    const float p_limit = top_p ? top_p[row] : 1.f;
+    if (k <= 0 || k > SAMPLE_MAX_K) {
+        // ---- the cuts as thresholds on the value (see the head of this file); cut = 0 keeps everything
+        uint32_t cut = 0;
+        const uint32_t top_key = ordered_key(top.value);
+        if (k > SAMPLE_MAX_K && k < vocab) {
+            // the key of the k-th largest logit: the largest key with at least k logits at or above it
+            uint32_t prefix = 0;
+            for (int bit = 31; bit >= 0; --bit) {
+                const uint32_t candidate = prefix | (1u << bit);
+                float count = 0.f;                       // exact in float up to 2^24 entries per row
+                for (int i = tid; i < vocab; i += SAMPLE_THREADS) count += ordered_key(l[i]) >= candidate ? 1.f : 0.f;
+                count = block_sum(count, sum_scratch);
+                if (count >= (float)k) prefix = candidate;
+            }
+            cut = prefix;
+        }
+        if (p_limit < 1.f) {
+            float kept = 0.f;
+            for (int i = tid; i < vocab; i += SAMPLE_THREADS)
+                if (ordered_key(l[i]) >= cut) kept += expf((l[i] - top.value) * inv_temp);
+            kept = block_sum(kept, sum_scratch);
+            const float limit = (1.f - p_limit) * kept;
+            // the largest key t with mass{cut <= key < t} <= limit; logits below t leave
+            uint32_t prefix = 0;
+            for (int bit = 31; bit >= 0; --bit) {
+                const uint32_t candidate = prefix | (1u << bit);
+                float below = 0.f;
+                if (candidate > cut) {
+                    for (int i = tid; i < vocab; i += SAMPLE_THREADS) {
+                        const uint32_t key = ordered_key(l[i]);
+                        if (key >= cut && key < candidate) below += expf((l[i] - top.value) * inv_temp);
+                    }
+                }
+                below = block_sum(below, sum_scratch);
+                if (below <= limit) prefix = candidate;
+            }
+            cut = prefix < top_key ? prefix : top_key;   // the largest logit always stays
+        }
+        // ---- the draw: thread `tid` owns the contiguous ids [tid * chunk, (tid + 1) * chunk)
         const int chunk = (vocab + SAMPLE_THREADS - 1) / SAMPLE_THREADS;
         const int begin = tid * chunk, end = min(begin + chunk, vocab);
         float s = 0.f;
-        for (int i = begin; i < end; ++i) s += expf((l[i] - top.value) * inv_temp);
+        for (int i = begin; i < end; ++i)
+            if (ordered_key(l[i]) >= cut) s += expf((l[i] - top.value) * inv_temp);
+        __syncthreads();
         chunk_sum[tid] = s;
         if (tid == 0) result = -1;
         __syncthreads();
@@ -107,6 +159,7 @@ sample_kernel(const float* __restrict__ logits, int ld, int vocab, const float* 
             float running = before;
             int pick = -1, last_positive = -1;
             for (int i = begin; i < end; ++i) {
+                if (ordered_key(l[i]) < cut) continue;
                 const float p = expf((l[i] - top.value) * inv_temp);
                 running += p;
                 if (p > 0.f) last_positive = i;
@@ -121,7 +174,6 @@ sample_kernel(const float* __restrict__ logits, int ld, int vocab, const float* 
     }
 
     // the k largest, one block-wide selection per candidate
-    if (k > SAMPLE_MAX_K) k = SAMPLE_MAX_K;
     Best previous = top;
     if (tid == 0) { cand_value[0] = top.value; cand_index[0] = top.index; }
     for (int c = 1; c < k; ++c) {
@@ -140,7 +192,6 @@ sample_kernel(const float* __restrict__ logits, int ld, int vocab, const float* 
         float total = 0.f;
         for (int c = 0; c < k; ++c) { prob[c] = expf((cand_value[c] - top.value) * inv_temp); total += prob[c]; }
         int keep = k;
-        const float p_limit = top_p ? top_p[row] : 1.f;
         if (p_limit < 1.f) {
             float tail = 0.f;
             for (int c = k - 1; c >= 1; --c) {

@@ -87,7 +87,7 @@ class LLM:
         as_tensor = isinstance(input_ids, torch.Tensor)
         prompts = self._prompts_from(input_ids, attention_mask)
         params = [SamplingParams(temperature=temperature if do_sample else 0.0,
-                                 top_k=min(top_k, self.sampler.max_top_k) if do_sample else 0,
+                                 top_k=top_k if do_sample else 0,
                                  top_p=top_p if do_sample else 1.0,
                                  seed=None if seed is None else int(seed) * 1000003 + row,   # rows draw from streams of their own
                                  max_new_tokens=max_new_tokens, eos_token_ids=tuple(eos), ignore_eos=ignore_eos)

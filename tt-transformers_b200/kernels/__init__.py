@@ -349,13 +349,14 @@ class CudaKernels:
             return out
         return self.swiglu(self.linear(x, w_gate_up))
 
-    def fused_qkv_rope(self, x, w_qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True):
+    def fused_qkv_rope(self, x, w_qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True,
+                       interleaved=False):
         """The QKV projection, the rotation and the cache write of a decode step in one kernel.
         Returns the rotated queries [M, heads * head_dim], or None where the fused kernel does not
         apply (then the caller runs the three steps one by one)."""
         M, K = x.shape
         norm = x if isinstance(x, DeferredNorm) else None
-        if norm is not None and not self.fuse_norm:
+        if (norm is not None and not self.fuse_norm) or interleaved:
             return None
         src = norm.xg if norm is not None else x
         if not (w_qkv.dtype == torch.bfloat16 and M <= 8 and K % 8 == 0 and src.stride(1) == 1
@@ -375,7 +376,10 @@ class CudaKernels:
         return q
 
     # ------------------------------------------------------------------ attention
-    def rope_kv_write(self, qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True):
+    def rope_kv_write(self, qkv, batch, inv_freq, rotary_dim, heads, kv_heads, head_dim, view, write_kv=True,
+                      interleaved=False):
+        """Rotate the queries and keys of qkv in place and write keys and values into their pages. Pairs are
+        (i, i + rotary_dim/2), or (2i, 2i + 1) with `interleaved`."""
         tokens = qkv.shape[0]
         if qkv.shape[1] != (heads + 2 * kv_heads) * head_dim or not qkv.is_contiguous():
             raise KernelError("rope_kv_write: qkv must be contiguous [tokens, (heads + 2 kv_heads) * head_dim]")
@@ -386,8 +390,8 @@ class CudaKernels:
             self._p(view.keys if view is not None else None), self._p(view.values if view is not None else None),
             self._p(view.block_table if view is not None else None),
             view.block_table.shape[1] if view is not None else 0, view.page_size if view is not None else 1,
-            num_pages, 1 if (write_kv and view is not None) else 0, self._p(self.status), self._stream()),
-            "rope_kv_write")
+            num_pages, 1 if (write_kv and view is not None) else 0, 1 if interleaved else 0, self._p(self.status),
+            self._stream()), "rope_kv_write")
 
     def paged_attention(self, qkv, batch, heads, kv_heads, head_dim, scale, view) -> torch.Tensor:
         tokens = qkv.shape[0]

@@ -56,13 +56,15 @@ class Attention(Mixer):
         k = self.runtime.kernels
         rotation = self.position.rotation() if self.position is not None else None
         inv_freq, rotary_dim = rotation if rotation is not None else (None, 0)
+        interleaved = bool(getattr(self.position, "interleaved", False))
         qkv = None
         if batch.max_seg_len == 1:          # a handful of decoded tokens: projection, rotation and cache write in one kernel
             qkv = k.fused_qkv_rope(x, self.w_qkv, batch, inv_freq, rotary_dim, self.heads, self.kv_heads, self.head_dim,
-                                   cache, write_cache)
+                                   cache, write_cache, interleaved=interleaved)
         if qkv is None:
             qkv = k.linear(x, self.w_qkv)
-            k.rope_kv_write(qkv, batch, inv_freq, rotary_dim, self.heads, self.kv_heads, self.head_dim, cache, write_cache)
+            k.rope_kv_write(qkv, batch, inv_freq, rotary_dim, self.heads, self.kv_heads, self.head_dim, cache, write_cache,
+                            interleaved=interleaved)
         mixed = k.paged_attention(qkv, batch, self.heads, self.kv_heads, self.head_dim, self.scale, cache)
         if residual is not None:
             # ADDED or a DeferredNorm where the product's epilogue takes the add, else the product itself

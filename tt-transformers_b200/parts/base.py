@@ -241,7 +241,10 @@ class PositionEncoding(Part):
     """How positions reach the model. `embed` may change the embedded tokens
     (absolute encodings); `rotation()` gives what a mixer needs to rotate queries
     and keys: (inverse frequencies float32 [rotary_dim/2] on the device,
-    rotary_dim), or None when nothing is rotated."""
+    rotary_dim), or None when nothing is rotated. `interleaved` says which elements
+    of a head form a rotated pair: (i, i + rotary_dim/2) when False, (2i, 2i + 1) when True."""
+
+    interleaved = False
 
     def embed(self, x, batch: StepBatch):
         return x

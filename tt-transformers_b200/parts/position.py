@@ -40,10 +40,15 @@ def rotary_inverse_frequencies(rotary_dim: int, theta: float, scaling: Optional[
 
 
 class Rotary(PositionEncoding):
-    def __init__(self, rotary_dim: int, theta: float, scaling: Optional[dict] = None):
+    """`interleaved` False pairs element i of a head with element i + rotary_dim/2 (the row order of the
+    checkpoints this engine reads); True pairs 2i with 2i + 1, the order on which the reference rotates after
+    permuting the checkpoint's rows (src/tt_transformers/models/llama32_1b/weight_utils.py:23-25)."""
+
+    def __init__(self, rotary_dim: int, theta: float, scaling: Optional[dict] = None, interleaved: bool = False):
         if rotary_dim % 2:
             raise ValueError(f"rotary_dim must be even, got {rotary_dim}")
         self.rotary_dim, self.theta, self.scaling = int(rotary_dim), float(theta), scaling
+        self.interleaved = bool(interleaved)
         self.inv_freq_host = rotary_inverse_frequencies(self.rotary_dim, self.theta, scaling)
 
     def bind(self, tensors, runtime):

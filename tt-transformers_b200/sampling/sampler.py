@@ -22,8 +22,10 @@ class Sampler:
         self.max_top_k = int(getattr(kernels, "max_top_k", 64))
 
     def validate(self, params: SamplingParams) -> None:
-        if params.temperature > 0 and params.top_k > self.max_top_k:
-            raise ValueError(f"top_k must be at most {self.max_top_k} on the device sampler, got {params.top_k}")
+        """Every combination of temperature, top_k and top_p is served: up to `max_top_k` candidates are
+        selected one by one, more (or top_p alone) by thresholds on the logit's value."""
+        if not isinstance(params, SamplingParams):
+            raise TypeError(f"sampling parameters must be SamplingParams, got {type(params).__name__}")
 
     def sample(self, logits: torch.Tensor, params: Sequence[SamplingParams], seeds: Sequence[int],
                counters: Sequence[int]) -> List[int]:
