@@ -120,3 +120,66 @@ def run_steps(engine, steps):
             engine.finish(rid)
     engine.kernels.check_status()
     return {rid: torch.stack(rows) for rid, rows in got.items()}
+
+
+def steps_many(requests, live, tail=44, seed=0, portion=(2, 40)):
+    """Many requests at a time: up to `live` are live; each runs its prompt part in portions beside the others'
+    decoded tokens and its last `tail` tokens one by one; nobody sits a step out, so that between admissions the
+    steps hold one token per request (the shape that is captured and replayed). When a request ends, the next
+    waiting one is admitted in the following step and takes over its pages."""
+    g = torch.Generator().manual_seed(seed)
+    waiting = list(requests)
+    at = {}
+    steps = []
+    while waiting or at:
+        while waiting and len(at) < live:
+            at[waiting.pop(0)] = 0
+        entries, end = [], []
+        for rid in list(at):
+            toks, i = requests[rid], at[rid]
+            head = max(1, len(toks) - tail)
+            if i >= head:
+                n = 1
+            else:
+                n = min(int(torch.randint(portion[0], portion[1] + 1, (1,), generator=g)), head - i)
+            entries.append({"id": rid, "tokens": toks[i:i + n], "want": [n - 1] if i + n >= head else []})
+            at[rid] = i + n
+            if at[rid] == len(toks):
+                end.append(rid)
+                del at[rid]
+        steps.append({"entries": entries, "end": end})
+    return steps
+
+
+def wanted_positions(steps):
+    """{id: [positions]} of the logits that run_steps collects for these steps, in order."""
+    at, out = {}, {}
+    for s in steps:
+        for e in s["entries"]:
+            base = at.get(e["id"], 0)
+            out.setdefault(e["id"], []).extend(base + w for w in e["want"])
+            at[e["id"]] = base + len(e["tokens"])
+    return out
+
+
+def error_stats(got, ref, margin=0.02):
+    """Over all requests: the largest and the mean |got - ref| relative to the largest |ref|, how often the best
+    token agrees, and how often it agrees on rows whose reference leads its runner-up by more than `margin`
+    times the largest |ref| (rows that rounding should not flip)."""
+    worst = mean = 0.0
+    rows = agree = clear = clear_agree = 0
+    for rid in ref:
+        g, r = got[rid].float().cpu(), ref[rid].float().cpu()
+        scale = float(r.abs().max())
+        diff = (g - r).abs()
+        worst = max(worst, float(diff.max()) / scale)
+        mean += float(diff.mean(dim=-1).sum()) / scale
+        same = g.argmax(-1) == r.argmax(-1)
+        top2 = r.topk(2, dim=-1).values
+        lead = (top2[:, 0] - top2[:, 1]) > margin * scale
+        rows += r.shape[0]
+        agree += int(same.sum())
+        clear += int(lead.sum())
+        clear_agree += int((same & lead).sum())
+    return {"max": worst, "mean": mean / rows, "top1": agree / rows, "clear_rows": clear,
+            "clear_top1": clear_agree / max(clear, 1)}

@@ -205,3 +205,16 @@ def test_the_real_layer_sizes_in_32_bit_and_bfloat16(tmp_path):
         engine.close()
         del engine
         torch.cuda.empty_cache()
+
+
+def test_token_match_at_full_depth():
+    """Llama 3.2 1B with all 16 layers, random weights, float32: the logits of two prompts against the plain
+    implementation in the four ways of cutting (the benchmark's token-match case)."""
+    from tt_transformers_b200.cli import measure
+
+    result = measure.run_token_match(measure.model_config("1b"), prompt_lengths=(80, 47))
+    print(result)
+    assert result["layers"] == 16 and set(result["modes"]) == {"whole", "decode_tail", "portions", "mixed"}
+    for mode, figures in result["modes"].items():
+        assert figures["max_relative_error"] <= 1e-4, (mode, figures)
+        assert figures["argmax_agreement"] == 1.0, (mode, figures)

@@ -1,5 +1,20 @@
-"""Accuracy and performance cases, named as in the reference's benchmark.
+"""Accuracy and performance cases.
 
+The engine's own cases (one JSON object out; `--json FILE` also writes it to a file):
+    --case prefill-2048     one prompt of 2,048 tokens in one step: tokens/s, share of the bf16 peak
+    --case decode-b1|b8|b64 decode steps at that batch, every request holding about --context tokens:
+                            tokens/s, tokens/s/user, share of the HBM peak that (weights + live cache) per step
+                            stands for; decode-b1 also reports the time to first token of a 128-token prompt
+    --case mixed-3b         32 requests, prompt lengths uniform in [128, 2048], 256 decoded tokens each, through
+                            the scheduler with its token budget (Llama 3.2 3B sizes unless --model says otherwise)
+    --case decode-8b-b64    64 requests with 4,096-token prompts, context limit 32,768, decode (Llama 3.1 8B sizes)
+    --case token-match      float32 logits against the plain implementation (tests/plain_llama.py) on the same
+                            random weights, all layers, in four ways of cutting the prompts into steps
+    --case all              every case above, one object holding them all
+    --model {1b,3b,8b}      layer sizes (random weights); --n-layers cuts the model short
+    --context N --steps K   context held while decoding, timed decode steps
+
+The reference's cases, by its names (examples/llama32_1b/benchmark.py:1100-1121):
     --case token-accuracy   teacher forcing: 512 prompt tokens, then 511 given tokens one per
                             step; how often the model's best token is the reference's best, and
                             among the reference's five best (examples/common/run_helpers.py:201-289).
@@ -31,6 +46,7 @@ import time
 import torch
 
 EXAMPLE_CASES = ("token-accuracy", "batch-1", "batch-32", "batch-32-ci", "eval-32")
+ENGINE_CASES = ("prefill-2048", "decode-b1", "decode-b8", "decode-b64", "mixed-3b", "decode-8b-b64", "token-match", "all")
 
 
 def _prompts(vocab, batch, seed=0, low=90, high=125):
@@ -101,15 +117,89 @@ def run_eval_32(llm, repeats=3, new_tokens=32):
     return {"repeats": repeats, "prompts": 32, "deterministic": same}
 
 
+def run_engine_case(case: str, model: str, context: int, steps: int, warmup: int, n_layers=None, fill="prefill") -> dict:
+    """One of the engine's own cases; every figure through tt_transformers_b200.cli.measure."""
+    from ..engine.llm import LLM
+    from . import measure
+
+    if case == "all":
+        out = {}
+        for each in ENGINE_CASES[:-1]:
+            out[each] = run_engine_case(each, model, context, steps, warmup, n_layers, fill)
+            torch.cuda.empty_cache()
+        return out
+    if case == "mixed-3b" and model is None:
+        model = "3b"
+    if case == "decode-8b-b64" and model is None:
+        model = "8b"
+    model = model or "1b"
+    cfg = measure.model_config(model)
+    layers = n_layers or cfg["num_hidden_layers"]
+    cfg = dict(cfg, num_hidden_layers=layers)
+    pk = measure.peaks()
+    out = {"case": case, "model": measure.MODEL_NAMES.get(model, model), "layers": layers,
+           "layers_full": measure.model_config(model)["num_hidden_layers"], "dtype": "bfloat16"}
+    if case == "token-match":
+        out.update(measure.run_token_match(cfg, layers=layers), dtype="float32")
+        return out
+    sampler = measure.ClockSampler()
+    try:
+        if case == "prefill-2048":
+            engine = measure.make_engine(cfg, max_batch=1, context=max(context or 4096, measure.PREFILL_TOKENS + measure.PAGE))
+            out.update(measure.measure_prefill(engine, cfg, layers, pk))
+        elif case in ("decode-b1", "decode-b8", "decode-b64"):
+            batch = int(case.split("-b")[1])
+            context = context or 8192
+            engine = measure.make_engine(cfg, max_batch=batch, context=context)
+            if batch == 1:
+                out["ttft"] = measure.measure_ttft(engine, cfg, 128)
+            out.update(measure.measure_decode(engine, cfg, layers, pk, batch, context, steps, warmup, sampler=sampler, how=fill))
+        elif case == "mixed-3b":
+            context = context or 8192
+            engine = measure.make_engine(cfg, max_batch=32, context=context, pool_tokens=32 * (2048 + 256 + measure.PAGE))
+            out.update(measure.run_mixed(LLM(engine), cfg, layers, pk, sampler=sampler), context=context)
+        elif case == "decode-8b-b64":
+            context = context or 32768
+            prompt = 4096
+            engine = measure.make_engine(cfg, max_batch=64, context=context,
+                                         pool_tokens=64 * (prompt + steps + warmup + 2 * measure.PAGE))
+            # every request holds `prompt` tokens when decoding starts
+            out.update(measure.measure_decode(engine, cfg, layers, pk, 64, prompt + steps + warmup + 1, steps, warmup,
+                                              sampler=sampler, how=fill), prompt_tokens=prompt, context_limit=context)
+        else:
+            raise SystemExit(f"unknown case {case!r}")
+        engine.close()
+    finally:
+        sampler.stop()
+    return out
+
+
 def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("--case", choices=EXAMPLE_CASES, default=EXAMPLE_CASES[0])
+    parser.add_argument("--case", choices=ENGINE_CASES + EXAMPLE_CASES, default=EXAMPLE_CASES[0])
     parser.add_argument("--optimizations", choices=("performance", "accuracy"), default="performance")
     parser.add_argument("--hf-model", default=None, help="model folder (default: $HF_MODEL, else --random)")
-    parser.add_argument("--random", default="llama-3.2-1b", help="named model with random weights")
+    parser.add_argument("--random", default="llama-3.2-1b", help="named model with random weights (the reference's cases)")
+    parser.add_argument("--model", choices=("1b", "3b", "8b"), default=None, help="layer sizes for the engine's own cases")
+    parser.add_argument("--context", type=int, default=None, help="tokens every request holds while decoding")
+    parser.add_argument("--steps", type=int, default=64, help="timed decode steps")
+    parser.add_argument("--warmup", type=int, default=8)
+    parser.add_argument("--fill", default="prefill", choices=("prefill", "synthetic"))
+    parser.add_argument("--json", default=None, metavar="FILE", help="also write the result object to FILE")
     parser.add_argument("--n-layers", type=int, default=None)
     args = parser.parse_args(argv)
     from .common import load
+
+    if args.case in ENGINE_CASES:
+        result = run_engine_case(args.case, args.model, args.context, args.steps, max(args.warmup, 3), args.n_layers, args.fill)
+        text = json.dumps(result)
+        print(text)
+        if args.json:
+            with open(args.json, "w") as f:
+                f.write(text + "\n")
+        if args.case == "token-match" and not (result["max_relative_error"] <= 1e-4 and result["argmax_agreement"] == 1.0):
+            raise SystemExit(1)
+        return
 
     hf_model = args.hf_model or os.environ.get("HF_MODEL")
     dtype = "bfloat16" if args.optimizations == "performance" else "float32"
@@ -128,7 +218,11 @@ def main(argv=None):
         result = run_perf(llm, batch, steps)
         llm.cleanup()
     result.update(case=args.case, optimizations=args.optimizations, model=hf_model or f"random:{args.random}")
-    print(json.dumps(result))
+    text = json.dumps(result)
+    print(text)
+    if args.json:
+        with open(args.json, "w") as f:
+            f.write(text + "\n")
     if args.case == "eval-32" and not result["deterministic"]:
         raise SystemExit(1)
 
