@@ -147,8 +147,9 @@ def test_the_first_tokens_of_a_sequence(tiny_folders, dtype, tol):
             assert helpers.relative_error(one_by_one[rid], ref[rid]) < tol
 
 
+@pytest.mark.parametrize("eager", [False, True])
 @pytest.mark.parametrize("dtype,tol", [("float32", 1e-4), ("bfloat16", 4e-2)])
-def test_trace_run_as_a_program(tiny_folders, tmp_path, dtype, tol):
+def test_trace_run_as_a_program(tiny_folders, tmp_path, dtype, tol, eager):
     requests = {f"r{i}": helpers.random_tokens(384, n, 30 + i) for i, n in enumerate((40, 90, 17, 64, 33))}
     ref = helpers.plain_logits(tiny_folders["B"], requests)
     steps = helpers.steps_mixed(requests)
@@ -156,7 +157,8 @@ def test_trace_run_as_a_program(tiny_folders, tmp_path, dtype, tol):
     out = tmp_path / "out"
     proc = subprocess.run([sys.executable, os.path.join(ROOT, "bin", "trace_run"), "--model", tiny_folders["B"],
                            "--dtype", dtype, "--out", str(out), "--max-tokens",
-                           str(helpers.max_live_tokens(requests, steps))], input=lines, capture_output=True, text=True)
+                           str(helpers.max_live_tokens(requests, steps))] + (["--eager"] if eager else []),
+                          input=lines, capture_output=True, text=True)
     assert proc.returncode == 0, proc.stderr[-2000:]
     assert [l for l in proc.stdout.split("\n") if l.startswith("done")] == [f"done {i}" for i in range(len(steps))]
     got = {}

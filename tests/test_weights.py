@@ -51,6 +51,11 @@ def test_stored_precision(tmp_path):
     assert got["model.norm.weight"].dtype == torch.bfloat16               # 16-bit floats are kept as bfloat16
     assert got["model.layers.0.input_layernorm.weight"].dtype == torch.bfloat16
     assert got["extra.table"].dtype == torch.int32                        # integer tables
+    # for an engine that computes in float32, float16 keeps every bit of its mantissa
+    wide = read_safetensors(str(tmp_path / "m"), widen_float16=True)
+    assert wide["model.norm.weight"].dtype == torch.float32
+    assert torch.equal(wide["model.norm.weight"], tensors["model.norm.weight"].float())
+    assert wide["model.layers.0.input_layernorm.weight"].dtype == torch.bfloat16
 
 
 def test_one_error_lists_everything(tmp_path):

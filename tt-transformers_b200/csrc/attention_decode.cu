@@ -519,12 +519,12 @@ static int launch_attention_decode(const CUtensorMap& map_k, const CUtensorMap& 
     const size_t smem = 1024 + (stage_bytes > merge_bytes ? stage_bytes : merge_bytes) + (size_t)8 * NT * HD * 2 +
                         AD_TABLE_CACHE * sizeof(int) + 2 * STAGES * sizeof(uint64_t);
     auto kernel = attention_decode_kernel<HD, NT, STAGES>;
-    static bool configured = false;
-    if (!configured) {
+    static TtbOncePerDevice configured;
+    if (configured.pending()) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return (int)e;
         if (cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) cudaGetLastError();
-        configured = true;
+        configured.mark();
     }
     int page_shift = 0;
     while ((1 << page_shift) < page_size) ++page_shift;

@@ -434,11 +434,11 @@ static int launch_attention(const void* qkv, int q_row_stride, void* out, const 
     int page_shift = -1;
     for (int b = 0; b < 31; ++b)
         if (page_size == (1 << b)) page_shift = b;
-    static bool configured = false;
-    if (!configured) {
+    static TtbOncePerDevice configured;
+    if (configured.pending()) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return (int)e;
-        configured = true;
+        configured.mark();
     }
     dim3 grid(n_qtiles, kv_heads, num_splits);
     const float scale_log2 = scale * 1.4426950408889634f;

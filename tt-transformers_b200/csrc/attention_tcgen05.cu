@@ -523,11 +523,11 @@ static int launch_attention_tcgen05(const CUtensorMap& map_q, const CUtensorMap&
     constexpr int halves = HD / 64, stages = HD == 64 ? 3 : 2;
     const size_t smem = (size_t)halves * FA_ROWS_TILE + 2 * (size_t)stages * halves * FA_HALF_TILE + sizeof(FaBars) + 16 +
                         FA_TABLE * sizeof(int);
-    static bool configured = false;
-    if (!configured) {
+    static TtbOncePerDevice configured;
+    if (configured.pending()) {
         cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return (int)e;
-        configured = true;
+        configured.mark();
     }
     int page_shift = 0;
     while ((1 << page_shift) < page_size) ++page_shift;

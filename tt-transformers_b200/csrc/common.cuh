@@ -55,6 +55,21 @@ static inline int ttb_launch_status() {
     return e == cudaSuccess ? TTB_OK : (int)e;
 }
 
+// A kernel's attributes (its shared-memory limit, its cluster size) belong to a device: a launcher sets them
+// before its first launch on each device it is used on.
+#define TTB_MAX_DEVICES 64
+struct TtbOncePerDevice {
+    bool done[TTB_MAX_DEVICES] = {};
+    bool pending() const {
+        int d = 0;
+        return cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= TTB_MAX_DEVICES || !done[d];
+    }
+    void mark() {
+        int d = 0;
+        if (cudaGetDevice(&d) == cudaSuccess && d >= 0 && d < TTB_MAX_DEVICES) done[d] = true;
+    }
+};
+
 __device__ __forceinline__ float to_float(float v) { return v; }
 __device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
 template <typename T> __device__ __forceinline__ T from_float(float v);

@@ -328,12 +328,12 @@ static int sk_launch(const CUtensorMap& map_w, const CUtensorMap& map_x, void* C
                      int up_offset, int* error_flag, cudaStream_t stream) {
     auto kernel = gemm_skinny_tcgen05_kernel<NX, SWIGLU, TO>;
     const size_t stage_bytes = SK_W_BYTES + NX * SK_BK * 2;
-    static bool configured = false;
-    if (!configured) {
+    static TtbOncePerDevice configured;
+    if (configured.pending()) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)(1024 + SK_MAX_STAGES * stage_bytes + sizeof(SkBars) + 16));
         if (e != cudaSuccess) return (int)e;
-        configured = true;
+        configured.mark();
     }
     const int out_cols = SWIGLU ? SK_BW / 2 : SK_BW;
     const int tiles = (N + out_cols - 1) / out_cols;

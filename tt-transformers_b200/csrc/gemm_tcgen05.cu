@@ -357,11 +357,11 @@ template <bool SWIGLU, typename TO>
 static int tc_launch(const CUtensorMap& map_a, const CUtensorMap& map_w, void* C, int M, int N, int K, int ldc,
                      int up_offset, int* error_flag, cudaStream_t stream) {
     auto kernel = gemm_tcgen05_kernel<SWIGLU, TO>;
-    static bool configured = false;
-    if (!configured) {
+    static TtbOncePerDevice configured;
+    if (configured.pending()) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg::SMEM_BYTES);
         if (e != cudaSuccess) return (int)e;
-        configured = true;
+        configured.mark();
     }
     constexpr int out_cols = SWIGLU ? TcCfg::ACC_COLS / 2 : TcCfg::ACC_COLS;
     const int m_tiles = (M + TC_BM - 1) / TC_BM, n_tiles = (N + out_cols - 1) / out_cols;

@@ -318,12 +318,12 @@ static int gemv_mma_launch(const void* x, const void* w, void* out, int M, int N
     constexpr int GM_THREADS = GM_WARPS * 32;
     const size_t smem = (size_t)GM_WARPS * RG * NB * 32 * sizeof(float4) + (NORM ? (size_t)GM_THREADS * sizeof(float) : 0);
     auto kernel = gemv_mma_kernel<NB, RG, MODE, GM_WARPS, TO, NORM, ACCUM>;
-    static bool configured = false;
-    if (!configured && smem > 48 * 1024) {
+    static TtbOncePerDevice configured;
+    if (configured.pending() && smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return (int)e;
     }
-    configured = true;
+    configured.mark();
     GmRope none = {};
     GmFuse plain = {};
     const int blocks = (MODE == GM_ROPE) ? N / 16 : (N + rows - 1) / rows;

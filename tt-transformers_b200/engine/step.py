@@ -295,7 +295,8 @@ def build_engine(model_folder: str = None, engine_config: EngineConfig = None, *
     model = DecoderModel(spec)
     specs = model.tensor_specs()
     if model_folder is not None:
-        tensors = read_safetensors(model_folder, wanted=[s.name for s in specs] if n_layers is not None else None)
+        tensors = read_safetensors(model_folder, wanted=[s.name for s in specs] if n_layers is not None else None,
+                                   widen_float16=engine_config.dtype == "float32")
     if n_layers is not None:
         # a model cut to its first layers leaves the other layers' tensors unused on purpose
         check_tensors(tensors, specs, ignorable=lambda name: True)

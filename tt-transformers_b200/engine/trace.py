@@ -28,15 +28,16 @@ REQUEST_ROUNDING = 64   # each request's token count is rounded up to this for -
 
 
 def run_trace(model: str, dtype: str, out_dir: str, max_tokens: int, lines, log=sys.stdout, device="cuda:0",
-              kernels=None, page_size: int = 16) -> int:
-    """Replay the steps that `lines` yields. Returns the number of steps run."""
+              kernels=None, page_size: int = 16, cuda_graph: bool = True) -> int:
+    """Replay the steps that `lines` yields. Returns the number of steps run. Steps that bring one token
+    per request run as generation runs them: as replays of a captured step (cuda_graph False: eagerly)."""
     os.makedirs(out_dir, exist_ok=True)
     if REQUEST_ROUNDING % page_size:
         raise ValueError(f"page_size {page_size} must divide {REQUEST_ROUNDING}")
     num_pages = max(1, -(-max_tokens // page_size))
     config = EngineConfig(dtype=dtype, page_size=page_size, num_pages=num_pages, max_batch_size=MAX_LIVE,
                           max_seq_len=max(max_tokens, page_size), max_step_tokens=max(max_tokens, 1) * MAX_LIVE,
-                          max_chunk_tokens=max(max_tokens, 1), cuda_graph=False, device=device)
+                          max_chunk_tokens=max(max_tokens, 1), cuda_graph=cuda_graph, device=device)
     engine = build_engine(model, config, kernels=kernels)
     steps = 0
     for line in lines:

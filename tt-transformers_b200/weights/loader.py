@@ -4,7 +4,8 @@ The reference walks a loaded model object attribute by attribute
 (src/tt_transformers/models/llama32_1b/hf_generator.py:224-262); the attribute paths
 are the checkpoint's tensor names, which is what is read here, straight from the files.
 Floating-point tensors are kept in bfloat16 unless they are stored in 32-bit, which
-stays 32-bit; integer tables become int32. All problems of a checkpoint are reported
+stays 32-bit (float16, whose mantissa bfloat16 cannot hold, becomes float32 when the engine
+computes in float32, so that the 32-bit path loses nothing); integer tables become int32. All problems of a checkpoint are reported
 together, in one error.
 """
 
@@ -42,18 +43,19 @@ def _checkpoint_files(folder: str) -> List[str]:
     return files
 
 
-def _normalise(tensor: torch.Tensor) -> torch.Tensor:
-    if tensor.dtype in (torch.float32, torch.float64):
+def _normalise(tensor: torch.Tensor, widen_float16: bool = False) -> torch.Tensor:
+    if tensor.dtype in (torch.float32, torch.float64) or (widen_float16 and tensor.dtype == torch.float16):
         return tensor.to(torch.float32)          # stored in 32-bit (or wider): stays 32-bit
     if tensor.dtype in _FLOAT or tensor.dtype.is_floating_point:
         return tensor.to(torch.bfloat16)
     return tensor.to(torch.int32)                 # integer tables
 
 
-def read_safetensors(folder: str, wanted: Iterable[str] = None) -> Dict[str, torch.Tensor]:
+def read_safetensors(folder: str, wanted: Iterable[str] = None, widen_float16: bool = False) -> Dict[str, torch.Tensor]:
     """name -> tensor on the CPU. With `wanted`, tensors of other names are listed
     (as zero-size placeholders are not needed, only their names and shapes are kept
-    under the key '__unread__') instead of being read."""
+    under the key '__unread__') instead of being read. widen_float16: float16 tensors become
+    float32 instead of bfloat16 (for an engine that computes in float32)."""
     wanted = set(wanted) if wanted is not None else None
     tensors: Dict[str, torch.Tensor] = {}
     unread: Dict[str, tuple] = {}
@@ -63,7 +65,7 @@ def read_safetensors(folder: str, wanted: Iterable[str] = None) -> Dict[str, tor
         with safe_open(path, framework="pt", device="cpu") as f:
             for name in f.keys():
                 if wanted is None or name in wanted:
-                    tensors[name] = _normalise(f.get_tensor(name))
+                    tensors[name] = _normalise(f.get_tensor(name), widen_float16)
                 else:
                     unread[name] = tuple(f.get_slice(name).get_shape())
     tensors["__unread__"] = unread
