@@ -170,3 +170,50 @@ def test_many_live_requests_through_captured_steps(tmp_path_factory, tiny_folder
     else:
         assert stats["mean"] <= BF16_MEAN and stats["clear_top1"] >= BF16_CLEAR_TOP1 and stats["clear_rows"] > 50, stats
     engine.close()
+
+
+# ---------------------------------------------------------------------------- captured prompt steps
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+@pytest.mark.parametrize("name,lengths,page", [("D", (2, 31, 32, 33, 100, 128, 257, 512), 16), ("B", (3, 17, 64, 150), 8),
+                                               ("E", (40, 129), 8)])
+def test_short_prompts_as_replays_of_a_captured_step(tiny_folders, dtype, name, lengths, page):
+    """A lone request's first portion, wanting its last logits, runs as a replay of the step captured for its length
+    bucket: the rest of the bucket is a segment on the scratch page (filled with NaN here: nothing of it may reach
+    the real rows). The prompt's last logits and three decoded positions against the plain implementation."""
+    from tt_transformers_b200.config import EngineConfig
+    from tt_transformers_b200.engine.step import build_engine
+
+    requests = {f"s{n}": helpers.random_tokens(CONFIGS[name]["vocab_size"], n + 3, 900 + n) for n in lengths}
+    ref = helpers.plain_logits(tiny_folders[name], requests)
+    engine = build_engine(tiny_folders[name], EngineConfig(dtype=dtype, page_size=page, max_batch_size=2,
+                                                           max_seq_len=1024 if name == "D" else 256, device="cuda:0"))
+    assert engine.prompt_graphs is not None
+    for g in engine.cache.groups:
+        for tensor in g.storage.values():
+            tensor.fill_(float("nan"))
+    steps = []
+    for n in lengths:
+        toks = requests[f"s{n}"]
+        steps.append({"entries": [{"id": f"s{n}", "tokens": toks[:n], "want": [n - 1]}], "end": []})
+        for i in range(n, n + 3):
+            steps.append({"entries": [{"id": f"s{n}", "tokens": [toks[i]], "want": [0]}], "end": [f"s{n}"] if i == n + 2 else []})
+    got = helpers.run_steps(engine, steps)
+    assert engine.prompt_graphs.replays == len(lengths)
+    assert len(engine.prompt_graphs._graphs) == len({engine.prompt_graphs._bucket(n) for n in lengths})
+    check(got, {rid: ref[rid][len(requests[rid]) - 4:] for rid in requests}, dtype)
+    # a portion that wants no logits runs the same way and returns none; one that wants several runs eagerly
+    before = engine.prompt_graphs.replays
+    assert engine.step([helpers_entry("x", requests[f"s{lengths[-1]}"][:lengths[0] + 7], [])]).shape[0] == 0
+    assert engine.prompt_graphs.replays == before + 1
+    engine.finish("x")
+    assert engine.step([helpers_entry("y", requests[f"s{lengths[-1]}"][:9], [0, 8])]).shape[0] == 2
+    assert engine.prompt_graphs.replays == before + 1
+    engine.finish("y")
+    engine.cache.audit()
+    engine.close()
+
+
+def helpers_entry(rid, tokens, want):
+    from tt_transformers_b200.engine.step import StepEntry
+
+    return StepEntry(rid, tokens, want)

@@ -23,6 +23,9 @@ class TorchKernels:
     def check_status(self):
         pass
 
+    def attention_tables(self, seg_lens, seg_pos0, rep, fixed_tokens=0):
+        return {}            # the twin's attention walks the segments by itself
+
     # ------------------------------------------------------------------ elementwise
     def embedding(self, table, token_ids, scale=1.0):
         return table[token_ids.long()].to(torch.float32) * scale

@@ -117,3 +117,100 @@ class DecodeGraphs:
         if len(want) == rows:
             return logits[:rows]
         return logits[torch.tensor(want, dtype=torch.long, device=logits.device)] if want else logits[:0]
+
+
+class PromptGraphs:
+    """Captured prompt steps for short prompts, the counterpart of the reference's traced prefill per length
+    bucket (src/tt_transformers/llm_runtime/trace_compiler.py:314-541; buckets:
+    src/tt_transformers/llm_runtime/prefill/plan.py:448-453).
+
+    A step that brings the first tokens of ONE request (nothing cached yet, at least two tokens, at most the
+    largest bucket) and wants the logits of at most one place is padded to the next bucket: the rest of the
+    bucket is a second segment at position 0 whose block table points at the scratch page, so what it writes
+    and reads is nobody's. The step's metadata, with the query-tile lists of its mixers, is copied into a
+    persistent buffer and the graph captured for that bucket is replayed: about 150 launches of the host
+    become one. What such a step computes for its real tokens is what the eager step computes: the same
+    kernels on the same rows (rows of a matrix product do not depend on one another)."""
+
+    BUCKETS = (32, 64, 128, 256, 512)
+
+    def __init__(self, engine):
+        self._engine = weakref.ref(engine)
+        limit = min(engine.config.max_step_tokens, engine.config.max_chunk_tokens, engine.max_seq_len)
+        self.sizes = [b for b in self.BUCKETS if b <= limit]
+        self._graphs: Dict[int, tuple] = {}
+        self.replays = 0
+
+    @property
+    def engine(self):
+        return self._engine()
+
+    def takes(self, entries) -> bool:
+        if len(entries) != 1 or not self.sizes:
+            return False
+        e = entries[0]
+        return (2 <= len(e.tokens) <= self.sizes[-1] and len(e.want) <= 1
+                and self.engine.cache.length(e.request_id) == 0)
+
+    def _bucket(self, tokens: int) -> int:
+        for s in self.sizes:
+            if s >= tokens:
+                return s
+        raise ValueError(f"{tokens} tokens exceed the largest captured prompt step")
+
+    def _fill(self, entries, size):
+        eng = self.engine
+        entry = entries[0]
+        if not entry.want:              # the graph always computes one row of logits; nobody reads it then
+            entry = type(entry)(entry.request_id, entry.tokens, [0])
+        host, layout, lists = eng._fill_host([entry], table_width=eng.cache.table_width, pad_tokens_to=size)
+        # everything a kernel's launch depends on is the bucket's, not the prompt's
+        lists = dict(lists, max_context=size, seg_lens=[size, 0], wants_every_row=False)
+        return host, layout, lists
+
+    def _capture(self, size: int, entries) -> tuple:
+        eng = self.engine
+        host, layout, lists = self._fill(entries, size)
+        static = torch.empty(layout["total"], dtype=torch.int32, device=eng.runtime.device)
+        static.copy_(host, non_blocking=True)
+        eng._record_staging()
+        batch = eng._batch_from(static, layout, lists)
+        tables = dict(batch.extras)                           # device views into `static`: refreshed with it
+        side = torch.cuda.Stream(device=eng.runtime.device)
+        side.wait_stream(torch.cuda.current_stream(eng.runtime.device))
+        with torch.cuda.stream(side):                         # warm up outside the capture
+            eng.model.forward(batch, eng.cache)
+        torch.cuda.current_stream(eng.runtime.device).wait_stream(side)
+        torch.cuda.synchronize(eng.runtime.device)
+        graph = torch.cuda.CUDAGraph()
+        before = eng.kernels.launches
+        batch.extras.clear()
+        batch.extras.update(tables)                           # what the warm-up derived on the host is derived again
+        gc_was_on = gc.isenabled()
+        gc.disable()                  # no collection (of engines used before, with CUDA objects) while capturing
+        try:
+            pool = eng.graphs.pool if eng.graphs is not None else None
+            with torch.cuda.graph(graph, pool=pool):
+                logits = eng.model.forward(batch, eng.cache)
+        finally:
+            if gc_was_on:
+                gc.enable()
+        if eng.graphs is not None and eng.graphs.pool is None:
+            eng.graphs.pool = graph.pool()
+        return graph, static, layout, logits, eng.kernels.launches - before
+
+    def run(self, entries) -> torch.Tensor:
+        eng = self.engine
+        size = self._bucket(len(entries[0].tokens))
+        if size not in self._graphs:
+            self._graphs[size] = self._capture(size, entries)
+        graph, static, layout, logits, kernels_in_graph = self._graphs[size]
+        host, new_layout, _ = self._fill(entries, size)
+        assert new_layout["total"] == layout["total"] and new_layout["extras"] == layout["extras"]
+        static.copy_(host, non_blocking=True)
+        eng.h2d_bytes += 4 * host.numel()
+        eng._record_staging()
+        graph.replay()
+        eng.kernels.launches += kernels_in_graph
+        self.replays += 1
+        return logits if entries[0].want else logits[:0]

@@ -55,10 +55,11 @@ class Engine:
         self._staging_turn = 0
         self.h2d_bytes = 0                  # bytes of step inputs copied from the host so far
         self.steps_run = 0
-        self.graphs = None
+        self.graphs = self.prompt_graphs = None
         if config.cuda_graph and runtime.device.type == "cuda" and model.graph_safe():
-            from .graph import DecodeGraphs
+            from .graph import DecodeGraphs, PromptGraphs
             self.graphs = DecodeGraphs(self)
+            self.prompt_graphs = PromptGraphs(self)
 
     # ------------------------------------------------------------------ requests
     def admit(self, request_id) -> None:
@@ -97,17 +98,23 @@ class Engine:
         return dev
 
     def _fill_host(self, entries: List[StepEntry], pad_to: int = 0, table_width: Optional[int] = None,
-                   want_all: bool = False):
+                   want_all: bool = False, pad_tokens_to: int = 0):
         """The step's metadata as one packed int32 host buffer. With pad_to, segments of one
         token at position 0 on the scratch page are appended until there are pad_to segments
-        (a captured decode step has a fixed number of rows). Returns (host, layout, lists)."""
+        (a captured decode step has a fixed number of rows); with pad_tokens_to, one segment that
+        brings the step to that many tokens (a captured prompt step has a fixed number of tokens
+        in two segments; an entry that fills it alone is followed by a segment of no tokens).
+        Returns (host, layout, lists)."""
         cache = self.cache
         seg_lens = [len(e.tokens) for e in entries]
         seg_pos0 = [cache.length(e.request_id) for e in entries]
         seg_slot = [cache.slot(e.request_id) for e in entries]
         real = len(entries)
-        pad = max(0, pad_to - real)
-        T, R = sum(seg_lens) + pad, real + pad
+        pad_lens = [1] * max(0, pad_to - real)
+        if pad_tokens_to:
+            pad_lens = [pad_tokens_to - sum(seg_lens)]
+        pad, pad_tokens = len(pad_lens), sum(pad_lens)
+        T, R = sum(seg_lens) + pad_tokens, real + pad
         want_rows, base = [], 0
         for e, n in zip(entries, seg_lens):
             for w in e.want:
@@ -128,17 +135,23 @@ class Engine:
         o_slot = o_p0 + _round4(R)
         o_want = o_slot + _round4(R)
         o_tab = o_want + _round4(max(N, 1))
-        total = o_tab + len(groups) * _round4(R * W)
-        host = self._stage(total)
-        buf = host.numpy()
-        tokens = np.fromiter((t for e in entries for t in e.tokens), dtype=np.int64, count=T - pad)
-        if tokens.size and (tokens.min() < 0 or tokens.max() >= self.vocab_size):
-            raise ValueError(f"a token id lies outside the vocabulary of {self.vocab_size}")
-        seg_lens_all = seg_lens + [1] * pad
+        seg_lens_all = seg_lens + pad_lens
         pos0_all = seg_pos0 + [0] * pad
         slot_all = seg_slot + [cache.scratch_slot] * pad      # padded rows own no request's state
-        buf[o_tok:o_tok + T - pad] = tokens
-        buf[o_tok + T - pad:o_tok + T] = 0
+        # small tables that the mixers' kernels derive from the step's shape travel in the same copy
+        step_tables = self.model.step_tables(seg_lens_all, pos0_all, pad_tokens_to)
+        o_extra, extras = o_tab + len(groups) * _round4(R * W), []
+        for key, table in step_tables.items():
+            extras.append((key, o_extra, tuple(table.shape)))
+            o_extra += _round4(table.size)
+        total = o_extra
+        host = self._stage(total)
+        buf = host.numpy()
+        tokens = np.fromiter((t for e in entries for t in e.tokens), dtype=np.int64, count=T - pad_tokens)
+        if tokens.size and (tokens.min() < 0 or tokens.max() >= self.vocab_size):
+            raise ValueError(f"a token id lies outside the vocabulary of {self.vocab_size}")
+        buf[o_tok:o_tok + T - pad_tokens] = tokens
+        buf[o_tok + T - pad_tokens:o_tok + T] = 0
         lens = np.asarray(seg_lens_all, dtype=np.int32)
         cu = np.zeros(R + 1, dtype=np.int32)
         np.cumsum(lens, out=cu[1:])
@@ -154,8 +167,10 @@ class Engine:
             start = o_tab + i * _round4(R * W)
             buf[start:start + real * W] = cache.table_rows(g, seg_slot, W).reshape(-1)
             buf[start + real * W:start + R * W] = 0
+        for (key, start, shape), table in zip(extras, step_tables.values()):
+            buf[start:start + table.size] = table.reshape(-1)
         layout = dict(T=T, R=R, N=N, W=W, o_tok=o_tok, o_pos=o_pos, o_seg=o_seg, o_cu=o_cu, o_p0=o_p0, o_slot=o_slot,
-                      o_want=o_want, o_tab=o_tab, total=total, groups=groups)
+                      o_want=o_want, o_tab=o_tab, total=total, groups=groups, extras=extras)
         lists = dict(seg_lens=seg_lens_all, seg_pos0=pos0_all, seg_slot=slot_all, max_context=max_context,
                      wants_every_row=want_rows == list(range(T)))
         return host, layout, lists
@@ -176,6 +191,9 @@ class Engine:
         for i, g in enumerate(L["groups"]):
             start = L["o_tab"] + i * _round4(R * W)
             batch.block_tables[g] = dev[start:start + R * W].view(R, W)
+        for key, start, shape in L.get("extras", ()):
+            count = int(np.prod(shape))
+            batch.extras[key] = dev[start:start + count].view(*shape)
         return batch
 
     def build_batch(self, entries: List[StepEntry], table_width: Optional[int] = None) -> StepBatch:
@@ -228,6 +246,8 @@ class Engine:
             raise ValueError("token_feedback needs a captured decode step: one token per request, cuda_graph on")
         if self.graphs is not None and total == len(entries):
             logits = self.graphs.run(entries, token_feedback)   # one token per request: replay a captured step
+        elif self.prompt_graphs is not None and self.prompt_graphs.takes(entries):
+            logits = self.prompt_graphs.run(entries)            # a short first portion of one request: likewise
         else:
             batch = self.build_batch(entries)
             logits = self.model.forward(batch, self.cache)
@@ -273,7 +293,7 @@ class Engine:
             self.cache.release(rid)
         for g in self.cache.groups:
             g.storage = None                     # the pages and the state tensors go
-        self.graphs = None
+        self.graphs = self.prompt_graphs = None
 
 
 def build_engine(model_folder: str = None, engine_config: EngineConfig = None, *, config_dict: dict = None,

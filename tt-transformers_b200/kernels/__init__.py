@@ -409,6 +409,30 @@ class CudaKernels:
             int(view.window or 0), view.keys.shape[0], self._p(self.status), self._stream()), "paged_attention")
         return out
 
+    def attention_tables(self, seg_lens, seg_pos0, rep: int, fixed_tokens: int = 0):
+        """The query-tile lists of a step as host tables, for the step's one metadata copy: {key: int32 array
+        [2, tiles]} with the segment and the first token of every tile, the tile that sees most keys first (the
+        longest blocks start first). One table per tile height a kernel may use; none for a step that the decode
+        shape takes. fixed_tokens: the step always holds this many tokens in at most two segments (a captured
+        prompt step): the table gets the length that any such step fits in, filled up with repeats of its last
+        tile (a tile computed twice writes the same values twice)."""
+        import numpy as np
+
+        if max(seg_lens) * rep <= 16:
+            return {}
+        out = {}
+        for rows in {int(self.lib.ttb_attention_tcgen05_tile_rows()), int(self.lib.ttb_attention_mma_tile_rows(0))}:
+            per_tile = max(1, rows // rep)
+            tiles = []
+            for r, (n, pos0) in enumerate(zip(seg_lens, seg_pos0)):
+                for t in range(0, n, per_tile):
+                    tiles.append((-(pos0 + min(n, t + per_tile)), r, t))
+            tiles.sort()
+            if fixed_tokens:
+                tiles += [tiles[-1]] * (fixed_tokens // per_tile + 2 - len(tiles))
+            out[("attention_tiles", per_tile)] = np.array([[t[1] for t in tiles], [t[2] for t in tiles]], dtype=np.int32)
+        return out
+
     def _attention_plan(self, batch, rep: int, kv_heads: int, head_dim: int, big_tiles: bool = False):
         """How the step's segments are cut into query tiles, and into how many key splits:
         derived once per step and geometry, reused by every layer. big_tiles: the 128-row
@@ -424,15 +448,12 @@ class CudaKernels:
         if decode_shape:
             seg, tok0, n_tiles = None, None, batch.num_segments
         else:
-            tiles = []
-            for r, (n, pos0) in enumerate(zip(batch.seg_lens, batch.seg_pos0_list)):
-                for t in range(0, n, tokens_per_tile):
-                    tiles.append((-(pos0 + min(n, t + tokens_per_tile)), r, t))
-            tiles.sort()                      # the tile that sees most keys first: the longest blocks start first
-            seg_list, tok_list = [t[1] for t in tiles], [t[2] for t in tiles]
-            n_tiles = len(seg_list)
-            both = torch.tensor([seg_list, tok_list], dtype=torch.int32, pin_memory=True).to(self.device, non_blocking=True)
-            seg, tok0 = both[0], both[1]
+            both = batch.extras.get(("attention_tiles", tokens_per_tile))      # came with the step's metadata
+            if both is None:                  # a batch put together by hand: a copy of its own
+                table = self.attention_tables(batch.seg_lens, batch.seg_pos0_list, rep)[("attention_tiles", tokens_per_tile)]
+                both = torch.from_numpy(table).pin_memory().to(self.device, non_blocking=True)
+                batch.extras[("attention_tiles", tokens_per_tile)] = both
+            seg, tok0, n_tiles = both[0], both[1], both.shape[1]
         # Key splits: with fewer blocks than fit the GPU at once, as many splits as fill it in one
         # wave (chunks of at least 256 keys); with more, a few waves of chunks of at least 2,048 keys.
         blocks = n_tiles * kv_heads

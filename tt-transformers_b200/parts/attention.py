@@ -52,6 +52,14 @@ class Attention(Mixer):
     fuses_norm = True
     fuses_residual = True
 
+    def step_tables_signature(self):
+        return ("attention", self.heads // self.kv_heads)
+
+    def step_tables(self, seg_lens, seg_pos0, fixed_tokens=0):
+        """The query-tile lists that the attention kernels want for this step, as host tables: they travel with
+        the step's metadata in its one copy to the device and reach forward() in batch.extras."""
+        return self.runtime.kernels.attention_tables(seg_lens, seg_pos0, self.heads // self.kv_heads, fixed_tokens)
+
     def forward(self, x, batch, cache, write_cache=True, residual=None, next_norm=None):
         k = self.runtime.kernels
         rotation = self.position.rotation() if self.position is not None else None

@@ -216,6 +216,12 @@ class Mixer(Part):
     def forward(self, x, batch: StepBatch, cache, write_cache: bool = True):
         raise NotImplementedError
 
+    # Optional: step_tables(seg_lens, seg_pos0, fixed_tokens=0) -> {key: int32 numpy array}: small tables that the
+    # mixer's kernels derive from the step's shape on the host. They are packed into the step's metadata (one copy
+    # to the device) and handed back as device tensors in batch.extras[key]. step_tables_signature() -> hashable:
+    # mixers with equal signatures want the same tables (asked once per step). A kernel table without
+    # `attention_tables` (a stand-in on the CPU) may return {} from it.
+
 
 class FeedForward(Part):
     """forward(x [T, width], batch) -> [T, width], each token by itself."""

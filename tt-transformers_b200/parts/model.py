@@ -147,6 +147,21 @@ class DecoderModel:
         per-step host tables), so that a decode step may be captured and replayed."""
         return all(_block_graph_safe(b) for b in self.layers)
 
+    def step_tables(self, seg_lens, seg_pos0, fixed_tokens: int = 0) -> Dict[object, object]:
+        """Host tables that the mixers want for a step of this shape (Mixer.step_tables), each asked once."""
+        if not hasattr(self, "_planners"):
+            planners = {}
+            for block in self.layers:
+                for part in block.parts():
+                    if hasattr(part, "step_tables"):
+                        sign = part.step_tables_signature() if hasattr(part, "step_tables_signature") else id(part)
+                        planners.setdefault(sign, part)
+            self._planners = list(planners.values())
+        tables = {}
+        for part in self._planners:
+            tables.update(part.step_tables(seg_lens, seg_pos0, fixed_tokens))
+        return tables
+
     # ------------------------------------------------------------------ cache needs
     def cache_requests(self):
         """For every entry of the layer order: what its cache unit must be (PagedKV,
