@@ -102,3 +102,26 @@ def test_engine_config():
     for bad in (dict(dtype="float16"), dict(page_size=0), dict(num_pages=0), dict(max_step_tokens=-1)):
         with pytest.raises(ConfigError):
             EngineConfig(**bad)
+
+
+def test_engine_config_options():
+    from tt_transformers_b200.config import EngineConfig
+    from tt_transformers_b200.config.base import ConfigError
+
+    c = EngineConfig(graph_batch_sizes=[1, 2, 6], gpu_memory_fraction=0.5, admission="conservative")
+    assert c.graph_batch_sizes == (1, 2, 6)
+    for bad in (dict(graph_batch_sizes=(4, 2)), dict(graph_batch_sizes=()), dict(gpu_memory_fraction=0.0),
+                dict(gpu_memory_fraction=1.5), dict(admission="greedy")):
+        with pytest.raises(ConfigError):
+            EngineConfig(**bad)
+
+
+def test_bytes_per_page():
+    import torch
+
+    from tt_transformers_b200.cache import CacheManager
+    from tt_transformers_b200.parts import PagedKV, SlotState
+
+    requests = [PagedKV(2, 16), PagedKV(2, 16), None, 0, PagedKV(1, 8, window=4), SlotState((3,))]
+    # two units of K and V pages of 2 x 4 x 16 bfloat16, one unit of 1 x 4 x 8
+    assert CacheManager.bytes_per_page(requests, 4, torch.bfloat16) == 2 * 2 * (2 * 4 * 16) * 2 + 2 * (4 * 8) * 2

@@ -220,3 +220,30 @@ def test_token_match_at_full_depth():
     for mode, figures in result["modes"].items():
         assert figures["max_relative_error"] <= 1e-4, (mode, figures)
         assert figures["argmax_agreement"] == 1.0, (mode, figures)
+
+
+def test_engine_options_memory_share_graph_sizes_and_conservative_admission(tiny_folders):
+    """The cache sized by a share of the device's memory, decode steps captured at chosen batch sizes, and requests
+    admitted only when everything they may hold fits: the same tokens as with the defaults."""
+    from tt_transformers_b200 import from_pretrained
+
+    prompts = [helpers.random_tokens(512, n, 300 + n) for n in (12, 40, 7, 25, 18)]
+    plain = from_pretrained(tiny_folders["D"], dtype="float32", max_batch_size=4, max_seq_len=256)
+    expect = plain.generate(prompts, max_new_tokens=12)
+    plain.cleanup()
+    llm = from_pretrained(tiny_folders["D"], dtype="float32", max_batch_size=64, max_seq_len=4096, gpu_memory_fraction=1.0)
+    assert llm.engine.cache.num_pages == 64 * 256           # capped by what every slot at full length needs
+    free, total = torch.cuda.mem_get_info()
+    share = (total - free + (64 << 20)) / total             # what is in use now and 64 MiB more
+    small = from_pretrained(tiny_folders["D"], dtype="float32", max_batch_size=64, max_seq_len=4096,
+                            gpu_memory_fraction=share, graph_batch_sizes=(1, 3), admission="conservative")
+    assert 500 < small.engine.cache.num_pages < 8000, small.engine.cache.num_pages     # 16 KiB a page: about 4,000
+    assert small.engine.graphs.sizes == [1, 3, 64]
+    got = small.generate(prompts, max_new_tokens=12)
+    assert got == expect
+    assert 64 in small.engine.graphs._graphs and set(small.engine.graphs._graphs) <= {1, 3, 64}
+    alone = small.generate(prompts[:3], max_new_tokens=5)               # three rows: the captured size 3
+    assert alone == [e[:5] for e in expect[:3]] and 3 in small.engine.graphs._graphs
+    assert small.last_stats["preemptions"] == 0
+    small.cleanup()
+    llm.cleanup()

@@ -136,3 +136,48 @@ def test_seeds_follow_arrival_unless_given():
     b = sched.add("b", [1], params())
     c = sched.add("c", [1], params(seed=5))
     assert a.seed != b.seed and c.seed == 5
+
+
+def test_conservative_admission_reserves_everything_up_front_and_never_gives_way():
+    """The reference's generate() reserves prompt + max_new_tokens pages before any work
+    (src/tt_transformers/models/hf_generation.py:337-343): with admission='conservative' a request starts only
+    when all that fits, holds it until it ends, and so never gives way or runs out of pages."""
+    cache = CacheManager([PagedKV(1, 8)], 4, 10, 3, 64, torch.device("cpu"), torch.float32, allocate_storage=False)
+    sched = Scheduler(cache, 16, 8, 64, admission="conservative")
+    a = sched.add("a", list(range(10)), params(n=10))       # 20 tokens: 5 pages
+    b = sched.add("b", list(range(6)), params(n=10))        # 16 tokens: 4 pages
+    c = sched.add("c", list(range(3)), params(n=6))         # 9 tokens: 3 pages; only one page is left beside a and b
+    plan, _ = run_step(cache, sched)
+    assert [(e.request.request_id, e.count) for e in plan] == [("a", 8), ("b", 6)]
+    assert cache.free_pages() == 1 and [r.request_id for r in sched.waiting] == ["c"]
+    steps = 0
+    while sched.has_work():
+        plan, _ = run_step(cache, sched)
+        steps += 1
+        if cache.is_live("a"):
+            assert cache.free_pages() <= 1 or not cache.is_live("b")     # what is held stays held
+        assert steps < 60
+    assert sched.preemptions == 0
+    assert [r.finish_reason for r in (a, b, c)] == ["length"] * 3 and len(c.output) == 6
+    assert cache.free_pages() == 10
+    # the same load admitted eagerly starts all three at once
+    cache2, eager = make(num_pages=10, slots=3)
+    for r in (a, b, c):
+        eager.add(r.request_id, r.prompt, r.params)
+    plan, _ = run_step(cache2, eager)
+    assert [e.request.request_id for e in plan] == ["a", "b", "c"]
+
+
+def test_held_pages_survive_a_step_taken_back():
+    cache = CacheManager([PagedKV(1, 8)], 4, 10, 2, 64, torch.device("cpu"), torch.float32, allocate_storage=False)
+    cache.admit("a")
+    cache.reserve("a", 17, hold=True)
+    assert cache.free_pages() == 5
+    cache.commit("a", 6)
+    cache.reserve("a", 7)
+    cache.commit("a", 7)
+    cache.rollback("a", 6)                      # gives back what lies beyond 6 tokens, but not what is held
+    assert cache.free_pages() == 5 and cache.room("a") == 5 * 4 + 20 - 6
+    cache.audit()
+    cache.release("a")
+    assert cache.free_pages() == 10

@@ -58,6 +58,7 @@ class _Live:
     length: int = 0                                           # tokens whose keys are cached
     pages: Dict[int, List[int]] = field(default_factory=dict)  # group -> page of every page index (0: none)
     reserved_to: int = 0                                      # pages cover positions < reserved_to
+    held_to: int = 0                                          # pages below this position stay even when unused (trim)
 
 
 class CacheManager:
@@ -161,10 +162,33 @@ class CacheManager:
         want = -(-new_length // self.page_size)
         return max(0, want - have)
 
-    def reserve(self, request_id, new_length: int) -> None:
+    @staticmethod
+    def bytes_per_page(cache_requests, page_size: int, dtype: torch.dtype) -> int:
+        """Device bytes that one more page costs, over all paged groups (every group has the same number of pages)."""
+        total, seen = 0, {}
+        for req in cache_requests:
+            if isinstance(req, CacheRequest) and req.paged:
+                seen[req] = seen.get(req, 0) + 1
+        for req, units in seen.items():
+            for shape, dt in req.storage(page_size).values():
+                count = 1
+                for n in shape:
+                    count *= n
+                total += units * count * torch.empty(0, dtype=dt or dtype).element_size()
+        return total
+
+    def reserve(self, request_id, new_length: int, hold: bool = False) -> None:
         """Make sure pages cover positions below new_length, in every paged group, or take
-        nothing and raise OutOfPages."""
+        nothing and raise OutOfPages. hold: the pages stay with the request until it ends, also
+        while it holds fewer tokens (an admission that reserves everything up front)."""
         live = self._live[request_id]
+        if hold:
+            self._reserve(live, request_id, new_length)
+            live.held_to = max(live.held_to, new_length)
+            return
+        self._reserve(live, request_id, new_length)
+
+    def _reserve(self, live, request_id, new_length: int) -> None:
         if new_length > self.max_seq_len:
             raise ValueError(f"request {request_id!r} would hold {new_length} tokens; the limit is {self.max_seq_len}")
         have = -(-live.reserved_to // self.page_size)
@@ -192,7 +216,8 @@ class CacheManager:
         """Give back pages that were reserved beyond what the request holds (a step that
         was reserved for but did not run)."""
         live = self._live[request_id]
-        keep = -(-live.length // self.page_size)
+        floor = max(live.length, live.held_to)
+        keep = -(-floor // self.page_size)
         for g in self.groups:
             if g.pool is None:
                 continue
@@ -202,7 +227,7 @@ class CacheManager:
                 g.pool.free(extra)
             del row[keep:]
             g.table[live.slot, keep:] = 0
-        live.reserved_to = live.length
+        live.reserved_to = floor
 
     def commit(self, request_id, new_length: int) -> None:
         """The request now holds new_length tokens. Pages that a window has passed are freed."""

@@ -24,11 +24,15 @@ OWN_ARGMAX = "own argmax"        # token_feedback value: the tokens are the argm
 class DecodeGraphs:
     def __init__(self, engine):
         self._engine = weakref.ref(engine)       # no cycle with the engine: both go when the last user lets go
-        sizes, b = [], 1
-        while b < engine.config.max_batch_size:
-            sizes.append(b)
-            b *= 2
-        sizes.append(engine.config.max_batch_size)
+        limit = engine.config.max_batch_size
+        if engine.config.graph_batch_sizes:
+            sizes = [b for b in engine.config.graph_batch_sizes if b < limit]
+        else:
+            sizes, b = [], 1
+            while b < limit:
+                sizes.append(b)
+                b *= 2
+        sizes.append(limit)                       # every batch the engine admits fits a captured size
         self.sizes = sizes
         self._graphs: Dict[int, tuple] = {}
         self.replays = 0

@@ -131,7 +131,7 @@ class LLM:
             raise ValueError(f"request requires {need} KV pages; the cache has {engine.cache.num_pages}")
         if self._scheduler is None:
             self._scheduler = Scheduler(engine.cache, engine.config.max_step_tokens, engine.config.max_chunk_tokens,
-                                        engine.max_seq_len)
+                                        engine.max_seq_len, admission=engine.config.admission)
         self._next_id += 1
         return self._scheduler.add(self._next_id, prompt, params)
 
@@ -271,13 +271,16 @@ def _load_tokenizer(folder: str):
 def from_pretrained(model: str, *, max_batch_size: int = 32, max_seq_len: int = 4096, n_layers: Optional[int] = None,
                     dtype: str = "bfloat16", page_size: int = 16, num_pages: Optional[int] = None,
                     max_step_tokens: int = 2048, max_chunk_tokens: int = 2048, cuda_graph: bool = True,
+                    gpu_memory_fraction: Optional[float] = None, graph_batch_sizes=None, admission: str = "eager",
                     device: str = "cuda:0", kernels=None) -> LLM:
     """Load the model folder `model` (config.json + safetensors; the class is chosen by
     config.json) and return an LLM ready to generate."""
     dtype = {"bf16": "bfloat16", "fp32": "float32", torch.bfloat16: "bfloat16", torch.float32: "float32"}.get(dtype, dtype)
     config = EngineConfig(dtype=dtype, page_size=page_size, num_pages=num_pages, max_batch_size=max_batch_size,
                           max_seq_len=max_seq_len, max_step_tokens=max_step_tokens,
-                          max_chunk_tokens=max_chunk_tokens, cuda_graph=cuda_graph, device=device)
+                          max_chunk_tokens=max_chunk_tokens, cuda_graph=cuda_graph, device=device,
+                          gpu_memory_fraction=gpu_memory_fraction, admission=admission,
+                          graph_batch_sizes=tuple(graph_batch_sizes) if graph_batch_sizes else None)
     engine = build_engine(model, config, kernels=kernels, n_layers=n_layers)
     cfg = engine.model_config
     return LLM(engine, eos_token_ids=getattr(cfg, "eos_token_ids", ()), tokenizer=_load_tokenizer(model))

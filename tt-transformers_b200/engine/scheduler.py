@@ -12,6 +12,11 @@ where it was, as draws depend on the token index only). A request that runs alon
 still cannot get a page is finished with reason "out_of_pages"; no other request is
 affected.
 
+With admission "conservative" a request is admitted only when pages for its whole prompt and
+all the tokens it may produce are free, and takes them all at once, as the reference's
+generate() does: such a request never gives way and never runs out of pages; fewer requests
+run side by side.
+
 The reference has no scheduler of its own: generate() runs a static batch and reserves
 prompt + max_new_tokens pages up front, failing before any work if they do not suffice
 (src/tt_transformers/models/hf_generation.py:337-348); serving leaves scheduling to the
@@ -78,8 +83,11 @@ class PlannedEntry:
 
 
 class Scheduler:
-    def __init__(self, cache: CacheManager, max_step_tokens: int, max_chunk_tokens: int, max_seq_len: int):
-        self.cache = cache
+    def __init__(self, cache: CacheManager, max_step_tokens: int, max_chunk_tokens: int, max_seq_len: int,
+                 admission: str = "eager"):
+        if admission not in ("eager", "conservative"):
+            raise ValueError(f"admission must be 'eager' or 'conservative', got {admission!r}")
+        self.cache, self.admission = cache, admission
         self.max_step_tokens, self.max_chunk_tokens, self.max_seq_len = max_step_tokens, max_chunk_tokens, max_seq_len
         self.waiting: Deque[Request] = deque()
         self.running: List[Request] = []          # in order of admission
@@ -173,6 +181,17 @@ class Scheduler:
                 break
             if req.preemptions and self.running and self.cache.room() < pending + 1:
                 break      # one that gave way comes back when all it has fits beside the others, not to give way again
+            if self.admission == "conservative":
+                whole = min(len(req.prompt) + req.params.max_new_tokens, self.max_seq_len)
+                if self.cache.room() < whole:
+                    break  # it waits until everything it may ever hold fits
+                self.waiting.popleft()
+                self.cache.admit(req.request_id)
+                self.cache.reserve(req.request_id, whole, hold=True)
+                self.running.append(req)
+                plan.append(PlannedEntry(req, 0, count, sample=count == pending))
+                budget -= count
+                continue
             self.waiting.popleft()
             self.cache.admit(req.request_id)
             self.cache.reserve(req.request_id, fit)

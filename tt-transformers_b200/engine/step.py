@@ -47,7 +47,21 @@ class Engine:
         self.kernels = runtime.kernels
         self.vocab_size = model.spec.vocab_size
         self.max_seq_len = min(config.max_seq_len, model.spec.max_positions)
-        self.cache = CacheManager(model.cache_requests(), config.page_size, config.resolved_num_pages(),
+        requests = model.cache_requests()
+        num_pages = config.resolved_num_pages()
+        if config.num_pages is None and config.gpu_memory_fraction is not None and runtime.device.type == "cuda":
+            # as many pages as fit beside what the device already holds (the weights), up to that share of its
+            # memory; never more than every slot at full length needs
+            free, total = torch.cuda.mem_get_info(runtime.device)
+            budget = int(config.gpu_memory_fraction * total) - (total - free)
+            per_page = CacheManager.bytes_per_page(requests, config.page_size, runtime.dtype)
+            if per_page:
+                fit = budget // per_page - 1                      # the scratch page
+                if fit < 1:
+                    raise ValueError(f"gpu_memory_fraction {config.gpu_memory_fraction} leaves no room for a cache page "
+                                     f"({(total - free) >> 20} MiB of {total >> 20} MiB are in use)")
+                num_pages = min(num_pages, int(fit))
+        self.cache = CacheManager(requests, config.page_size, num_pages,
                                   config.max_batch_size, self.max_seq_len, runtime.device, runtime.dtype)
         self._pinned = runtime.device.type == "cuda"
         self._staging = [None, None]          # two host buffers in turn, each with the event of its last copy
