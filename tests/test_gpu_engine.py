@@ -160,7 +160,7 @@ def test_many_live_requests_through_captured_steps(tmp_path_factory, tiny_folder
     got = helpers.run_steps(engine, steps)
     engine.cache.audit()
     assert engine.cache.free_pages() == pages
-    buckets = sorted(engine.graphs._graphs)
+    buckets = engine.graphs.captured_sizes()
     assert engine.graphs.replays >= 44 and max(buckets) >= min(64, 1 << (live - 1).bit_length()), buckets
     stats = helpers.error_stats(got, ref)
     print(f"\\n{name} live={live} {dtype}: {stats} buckets={buckets} replays={engine.graphs.replays}")

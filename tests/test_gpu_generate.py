@@ -116,6 +116,7 @@ def test_long_decoding(tiny_folders, dtype, tol):
     ref = helpers.plain_logits(tiny_folders["D"], requests)
     engine = build_engine(tiny_folders["D"], EngineConfig(dtype=dtype, page_size=16, num_pages=48, max_batch_size=2,
                                                           max_seq_len=448, device="cuda:0"))
+    engine.graphs.MIN_CONTEXT_BUCKET = 64        # the contexts grow through the buckets 64, 128, 256 and 448
     steps = [{"entries": [{"id": "a", "tokens": requests["a"][:20], "want": [19]},
                           {"id": "b", "tokens": requests["b"][:3], "want": [2]}], "end": []}]
     for i in range(400):
@@ -125,6 +126,7 @@ def test_long_decoding(tiny_folders, dtype, tol):
         steps.append({"entries": entries, "end": ["b"] if 3 + i == 299 else []})
     got = helpers.run_steps(engine, steps)
     assert engine.graphs is not None and engine.graphs.replays >= 399
+    assert sorted({bucket for _, bucket in engine.graphs._graphs}) == [64, 128, 256, 448]
     assert helpers.relative_error(got["a"], ref["a"][19:]) < tol
     assert helpers.relative_error(got["b"], ref["b"][2:]) < tol
 
@@ -241,9 +243,37 @@ def test_engine_options_memory_share_graph_sizes_and_conservative_admission(tiny
     assert small.engine.graphs.sizes == [1, 3, 64]
     got = small.generate(prompts, max_new_tokens=12)
     assert got == expect
-    assert 64 in small.engine.graphs._graphs and set(small.engine.graphs._graphs) <= {1, 3, 64}
+    assert 64 in small.engine.graphs.captured_sizes() and set(small.engine.graphs.captured_sizes()) <= {1, 3, 64}
     alone = small.generate(prompts[:3], max_new_tokens=5)               # three rows: the captured size 3
-    assert alone == [e[:5] for e in expect[:3]] and 3 in small.engine.graphs._graphs
+    assert alone == [e[:5] for e in expect[:3]] and 3 in small.engine.graphs.captured_sizes()
     assert small.last_stats["preemptions"] == 0
     small.cleanup()
+    llm.cleanup()
+
+
+def test_greedy_decoding_on_the_device_across_context_buckets(tiny_folders):
+    """Decode steps are captured per batch size and context bucket. A greedy loop that feeds every step's own
+    argmax to the next one on the device keeps doing so when the contexts grow into the next bucket (another graph
+    with buffers of its own): the tokens equal the plain implementation's."""
+    from tt_transformers_b200 import from_pretrained
+
+    import plain_llama
+
+    config, weights = plain_llama.read_model_folder(tiny_folders["D"])
+    prompts = [helpers.random_tokens(512, n, 640 + n) for n in (11, 27)]
+    expect = [plain_llama.greedy(config, weights, p, 60) for p in prompts]
+    llm = from_pretrained(tiny_folders["D"], dtype="float32", page_size=16, max_batch_size=2, max_seq_len=256)
+    llm.engine.graphs.MIN_CONTEXT_BUCKET = 16
+    assert llm.generate(prompts, max_new_tokens=60) == expect
+    buckets = sorted({bucket for _, bucket in llm.engine.graphs._graphs})
+    assert buckets == [32, 64, 128], buckets
+    # and through the engine's own decode loop, from the prompts' last tokens on
+    engine = llm.engine
+    from tt_transformers_b200.engine.step import StepEntry
+    firsts = []
+    for i, p in enumerate(prompts):
+        logits = engine.step([StepEntry(f"g{i}", p, [len(p) - 1])])
+        firsts.append(int(engine.kernels.sample(logits)[0]))
+    rest = engine.decode_steps(["g0", "g1"], firsts, 59)
+    assert [[firsts[i]] + [row[i] for row in rest] for i in range(2)] == expect
     llm.cleanup()

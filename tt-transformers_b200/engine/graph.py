@@ -7,6 +7,12 @@ in which every request brings exactly one token is padded to the next captured b
 (padding rows sit at position 0 and write to the scratch page), its metadata is copied into
 a persistent device buffer, and the graph captured for that size is replayed. The logits
 live in a buffer that the next replay of the same size overwrites.
+
+A graph is captured per batch size AND per context bucket (the longest context in the step,
+rounded up to a power of two): what a launch fixes for good (how many key splits the decode
+attention uses, how wide the block tables are) then fits the contexts that are live, not the
+longest one the engine admits. The reference keys its decode traces by lane batch and
+page-table width in the same way (decode.py:949-961).
 """
 
 from __future__ import annotations
@@ -34,10 +40,10 @@ class DecodeGraphs:
                 b *= 2
         sizes.append(limit)                       # every batch the engine admits fits a captured size
         self.sizes = sizes
-        self._graphs: Dict[int, tuple] = {}
+        self._graphs: Dict[tuple, tuple] = {}          # (batch size, context bucket) -> captured step
         self.replays = 0
         self.pool = None
-        self._last_size = None
+        self._last_key = None
         self.greedy = None
 
     @property
@@ -50,14 +56,28 @@ class DecodeGraphs:
                 return s
         raise ValueError(f"{rows} requests exceed the engine's max_batch_size")
 
-    def _capture(self, size: int, entries) -> tuple:
+    MIN_CONTEXT_BUCKET = 1024
+
+    def _context_bucket(self, entries) -> int:
+        """The longest context of the step (its new token included), rounded up to a power of two."""
         eng = self.engine
-        W = eng.cache.table_width
+        longest = max(eng.cache.length(e.request_id) for e in entries) + 1
+        bucket = self.MIN_CONTEXT_BUCKET
+        while bucket < longest:
+            bucket *= 2
+        return min(bucket, eng.max_seq_len)
+
+    def captured_sizes(self):
+        return sorted({size for size, _ in self._graphs})
+
+    def _capture(self, size: int, bucket: int, entries) -> tuple:
+        eng = self.engine
+        W = -(-bucket // eng.cache.page_size)
         host, layout, lists = eng._fill_host(entries, pad_to=size, table_width=W, want_all=True)
         static = torch.empty(layout["total"], dtype=torch.int32, device=eng.runtime.device)
         static.copy_(host, non_blocking=True)
         eng._record_staging()
-        lists = dict(lists, max_context=eng.max_seq_len)      # key splits are sized for the longest context
+        lists = dict(lists, max_context=bucket)               # key splits are sized for the bucket's longest context
         batch = eng._batch_from(static, layout, lists)
         side = torch.cuda.Stream(device=eng.runtime.device)
         side.wait_stream(torch.cuda.current_stream(eng.runtime.device))
@@ -95,17 +115,20 @@ class DecodeGraphs:
         eng = self.engine
         rows = len(entries)
         size = self._bucket(rows)
-        if size not in self._graphs:
-            self._graphs[size] = self._capture(size, entries)
-        graph, static, layout, logits, kernels_in_graph, greedy = self._graphs[size]
-        host, new_layout, _ = eng._fill_host(entries, pad_to=size, table_width=eng.cache.table_width, want_all=True)
+        key = (size, self._context_bucket(entries))
+        if key not in self._graphs:
+            self._graphs[key] = self._capture(size, key[1], entries)
+        graph, static, layout, logits, kernels_in_graph, greedy = self._graphs[key]
+        host, new_layout, _ = eng._fill_host(entries, pad_to=size, table_width=layout["W"], want_all=True)
         assert new_layout["total"] == layout["total"]
         if isinstance(token_feedback, str) and token_feedback == OWN_ARGMAX:
-            if self._last_size != size:
+            if self._last_key is None or self._last_key[0] != size:
                 raise ValueError("OWN_ARGMAX needs the step before to have been a replay of the same captured size")
             first = layout["o_pos"]                     # everything but the token ids, which the replay before left in place
             static[first:].copy_(host[first:], non_blocking=True)
             eng.h2d_bytes += 4 * (host.numel() - first)
+            if self._last_key != key:                   # the context grew into the next bucket: another graph's buffer
+                static[layout["o_tok"]:layout["o_tok"] + size].copy_(self._graphs[self._last_key][5])
         else:
             static.copy_(host, non_blocking=True)
             eng.h2d_bytes += 4 * host.numel()
@@ -113,8 +136,8 @@ class DecodeGraphs:
         if torch.is_tensor(token_feedback):
             static[layout["o_tok"]:layout["o_tok"] + rows].copy_(token_feedback[:rows])
         graph.replay()
-        self._last_size = size
-        self.greedy = greedy[:rows]                     # overwritten by the next replay of this size
+        self._last_key = key
+        self.greedy = greedy[:rows]                     # overwritten by the next replay of this graph
         eng.kernels.launches += kernels_in_graph
         self.replays += 1
         want = [i for i, e in enumerate(entries) if len(e.want)]
