@@ -11,6 +11,9 @@ The engine's own cases (one JSON object out; `--json FILE` also writes it to a f
     --case token-match      float32 logits against the plain implementation (tests/plain_llama.py) on the same
                             random weights, all layers, in four ways of cutting the prompts into steps
     --case all              every case above, one object holding them all
+    --case decode-sweep     decode steps over batch sizes 1, 8, 32, 64 and contexts 2,048, 8,192, 32,768 under ONE engine
+                            whose context limit is 32,768 (cache filled with random numbers; combinations whose cache
+                            exceeds 90 GB left out): step time and share of the HBM peak for each
     --model {1b,3b,8b}      layer sizes (random weights); --n-layers cuts the model short
     --context N --steps K   context held while decoding, timed decode steps
 
@@ -47,6 +50,7 @@ import torch
 
 EXAMPLE_CASES = ("token-accuracy", "batch-1", "batch-32", "batch-32-ci", "eval-32")
 ENGINE_CASES = ("prefill-2048", "decode-b1", "decode-b8", "decode-b64", "mixed-3b", "decode-8b-b64", "token-match", "all")
+EXTRA_CASES = ("decode-sweep",)
 
 
 def _prompts(vocab, batch, seed=0, low=90, high=125):
@@ -122,6 +126,23 @@ def run_engine_case(case: str, model: str, context: int, steps: int, warmup: int
     from ..engine.llm import LLM
     from . import measure
 
+    if case == "decode-sweep":
+        from . import measure as m
+
+        cfg = m.model_config(model or "1b")
+        layers = n_layers or cfg["num_hidden_layers"]
+        cfg = dict(cfg, num_hidden_layers=layers)
+        per_token = m.cache_bytes_per_token(cfg, layers)
+        grid = [(b, c) for c in (2048, 8192, 32768) for b in (1, 8, 32, 64) if b * c * per_token < 90e9]
+        engine = m.make_engine(cfg, max_batch=64, context=32768 + 64, pool_tokens=max(b * (c + 64) for b, c in grid))
+        rows = []
+        for b, c in grid:
+            r = m.measure_decode(engine, cfg, layers, m.peaks(), b, c, steps, warmup, how="synthetic")
+            rows.append({"batch": b, "context": c, "ms_per_step": r["ms_per_step"], "tokens_per_s": r["tokens_per_s"],
+                         "gb_per_step": round(r["roofline"]["bytes_per_step"] / 1e9, 2), "frac": r["roofline"]["frac"]})
+        engine.close()
+        return {"case": case, "model": m.MODEL_NAMES.get(model or "1b"), "layers": layers, "context_limit": 32768 + 64,
+                "peaks": m.peaks()["source"], "rows": rows}
     if case == "all":
         out = {}
         for each in ENGINE_CASES[:-1]:
@@ -176,7 +197,7 @@ def run_engine_case(case: str, model: str, context: int, steps: int, warmup: int
 
 def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("--case", choices=ENGINE_CASES + EXAMPLE_CASES, default=EXAMPLE_CASES[0])
+    parser.add_argument("--case", choices=ENGINE_CASES + EXTRA_CASES + EXAMPLE_CASES, default=EXAMPLE_CASES[0])
     parser.add_argument("--optimizations", choices=("performance", "accuracy"), default="performance")
     parser.add_argument("--hf-model", default=None, help="model folder (default: $HF_MODEL, else --random)")
     parser.add_argument("--random", default="llama-3.2-1b", help="named model with random weights (the reference's cases)")
@@ -190,7 +211,7 @@ def main(argv=None):
     args = parser.parse_args(argv)
     from .common import load
 
-    if args.case in ENGINE_CASES:
+    if args.case in ENGINE_CASES + EXTRA_CASES:
         result = run_engine_case(args.case, args.model, args.context, args.steps, max(args.warmup, 3), args.n_layers, args.fill)
         text = json.dumps(result)
         print(text)
