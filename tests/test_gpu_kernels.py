@@ -347,6 +347,44 @@ def test_prompt_attention_ignores_slots_that_hold_nothing(kernels, twin, case):
     kernels.check_status()
 
 
+@pytest.mark.parametrize("case", [
+    (8, 2, 64, 16, [(0, 200), (70, 33), (500, 40)]),
+    (32, 8, 64, 16, [(0, 700), (3000, 300), (17, 1), (255, 2)]),      # long blocks, a block of one row group
+    (8, 8, 64, 8, [(0, 513), (100, 257)]),                             # one head per KV head: 256 tokens a block
+    (6, 2, 64, 32, [(0, 90), (1000, 170)]),                            # three heads per KV head: 85 tokens a block
+    (24, 8, 128, 16, [(0, 130), (700, 50), (64, 64)]),
+    (32, 8, 128, 16, [(0, 300), (2100, 140)]),
+    (16, 1, 128, 64, [(0, 40), (500, 33)]),                            # sixteen heads per KV head, pages of 64
+    (8, 2, 64, 256, [(0, 300), (200, 100)]),                           # pages larger than a key tile
+])
+def test_prompt_attention_with_key_splits(kernels, twin, case):
+    """The tcgen05 attention kernel against plain attention, with the number of key splits the host would choose
+    and with 2, 3 and 5 (partial results and the merge kernel); long blocks, blocks of a single row group, heads
+    per KV head that do not divide a tile; every cache slot that no query may see holds NaN."""
+    heads, kv_heads, head_dim, page_size, segments = case
+    dtype = torch.bfloat16
+    qkv, batch, view = make_paged_case(dtype, heads, kv_heads, head_dim, page_size, segments, None, seed=12)
+    visible = torch.zeros(view.keys.shape[0], page_size, dtype=torch.bool)
+    for r, (p, n) in enumerate(segments):
+        for key in range(p + n):
+            visible[int(view.block_table[r, key // page_size]), key % page_size] = True
+    ref = twin.paged_attention(qkv.float(), batch, heads, kv_heads, head_dim, 0.25,
+                               SimpleNamespace(keys=view.keys.float(), values=view.values.float(),
+                                               block_table=view.block_table, page_size=page_size, window=None))
+    hidden = (~visible).cuda()[:, None, :, None].expand_as(view.keys)
+    view.keys[hidden] = float("nan")
+    view.values[hidden] = float("nan")
+    for splits in (None, 2, 3, 5):
+        batch.extras.clear()
+        if splits is not None:
+            plan = kernels._attention_plan(batch, heads // kv_heads, kv_heads, head_dim, big_tiles=True)
+            batch.extras[("attention_plan", heads // kv_heads, kv_heads, head_dim, True)] = plan[:4] + (splits,)
+        got = kernels.paged_attention(qkv, batch, heads, kv_heads, head_dim, 0.25, view)
+        assert not torch.isnan(got.float()).any(), splits
+        close(got, ref, dtype)
+        kernels.check_status()
+
+
 @pytest.mark.parametrize("vocab,rows", [(384, 5), (128256, 3), (1000, 64), (33, 2)])
 def test_sample(kernels, twin, vocab, rows):
     g = torch.Generator(device="cuda").manual_seed(4)

@@ -256,6 +256,11 @@ def measure_decode(engine, cfg: dict, layers: int, pk: dict, batch: int, context
     prompts = prompts or Prompts(cfg["vocab_size"])
     start = context - steps - warmup - 1
     ids = fill_requests(engine, cfg, batch, start, prompts, how)
+    if how == "prefill":
+        # Filling the cache is a burst of tensor-core work that leaves the board at its power cap with lowered
+        # clocks; decoding does not keep it there. Let the clocks settle so that the timed steps measure decoding.
+        torch.cuda.synchronize()
+        time.sleep(0.5)
     tokens = engine.decode_steps(ids, [1] * batch, warmup)[-1]
     before = engine.kernels.launches
     clocks = {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}

@@ -2,7 +2,7 @@
 //
 // A block owns 128 query rows: 128 / (heads per KV head) tokens of one segment times the query heads of
 // one KV head, token-major, so all rows share the keys and values that are loaded. Per tile of 64 keys:
-//   producer (warp 0, one thread)   TMA loads of whole cache pages (cp.async.bulk.tensor, 128-byte swizzle,
+//   producer (warp 0, a lane per copy)  TMA loads of whole cache pages (cp.async.bulk.tensor, 128-byte swizzle,
 //                                   no multicast) into a ring of K and V stages; the page ids of the
 //                                   block's key range are first copied from the block table to shared memory
 //   first product (warp 1, one thread)   S = Q K^T by tcgen05.mma into one of two S buffers in tensor memory, as
@@ -147,7 +147,7 @@ struct FaBars {
 };
 
 template <int HD>
-__global__ void __launch_bounds__(FA_THREADS)
+__global__ void __launch_bounds__(FA_THREADS, 2)
 attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                          const __grid_constant__ CUtensorMap map_v, __nv_bfloat16* __restrict__ out,
                          const int* __restrict__ cu_seqlens, const int* __restrict__ seg_pos0,
@@ -244,35 +244,42 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
     const uint32_t tmem_o = tmem_base + 2 * FA_BN;
 
     if (warp == 0) {
-        // ------------------------------------------------------------------ producer
-        if (lane == 0 && num_tiles > 0) {
-            fa_expect_tx(fa_smem(&bars->q_full), (uint32_t)(HALVES * rep * tokens_per_tile * 128));      // whole boxes, whatever lies outside
-            for (int h = 0; h < HALVES; ++h)
-                fa_tma_4d(fa_smem(q_tile) + h * FA_ROWS_TILE, &map_q, 0, h, g * rep, seg_start + tok0, fa_smem(&bars->q_full));
+        // ------------------------------------------------------------------ producer: one copy per lane
+        if (num_tiles > 0) {
+            if (lane == 0) {
+                fa_expect_tx(fa_smem(&bars->q_full), (uint32_t)(HALVES * rep * tokens_per_tile * 128));      // whole boxes, whatever lies outside
+                for (int h = 0; h < HALVES; ++h)
+                    fa_tma_4d(fa_smem(q_tile) + h * FA_ROWS_TILE, &map_q, 0, h, g * rep, seg_start + tok0, fa_smem(&bars->q_full));
+            }
             const int box_rows = min(page_size, FA_BN);            // a copy brings a page, or 64 rows of a larger one
             const int boxes_per_tile = FA_BN / box_rows;
             for (int j = 0; j < num_tiles; ++j) {
                 const int s = j % FA_STAGES;
-                if (j >= FA_STAGES && !fa_wait(fa_smem(&bars->kv_empty[s]), ((j / FA_STAGES) - 1) & 1)) {
-                    atomicExch(error_flag, 11);
-                    break;
+                if (j >= FA_STAGES) {
+                    bool freed = true;
+                    if (lane == 0) freed = fa_wait(fa_smem(&bars->kv_empty[s]), ((j / FA_STAGES) - 1) & 1);
+                    freed = __shfl_sync(0xffffffffu, freed, 0);
+                    if (!freed) {
+                        if (lane == 0) atomicExch(error_flag, 11);
+                        break;
+                    }
                 }
                 const int key0 = k_begin + j * FA_BN;
                 const int boxes = min(boxes_per_tile, ((k_end - key0) + box_rows - 1) / box_rows);
                 const uint32_t bar = fa_smem(&bars->kv_full[s]);
-                fa_expect_tx(bar, (uint32_t)boxes * box_rows * HD * 2 * 2);
-                for (int pg = 0; pg < boxes; ++pg) {
+                if (lane == 0) fa_expect_tx(bar, (uint32_t)boxes * box_rows * HD * 2 * 2);
+                __syncwarp();
+                // a lane brings one box: keys or values, one half of the head, one page (or 64 rows of a larger one)
+                for (int c = lane; c < 2 * HALVES * boxes; c += 32) {
+                    const int which = c & 1, h = (c >> 1) % HALVES, pg = (c >> 1) / HALVES;
                     const int key = key0 + pg * box_rows;
                     const int page_index = key >> page_shift;
                     const int rel = page_index - page_base;
                     int page = rel < FA_TABLE ? page_cache[rel] : table[page_index];
                     if ((unsigned)page >= (unsigned)num_pages) page = 0;
                     const int row = (page * kv_heads + g) * page_size + (key & (page_size - 1));
-                    for (int h = 0; h < HALVES; ++h) {
-                        const uint32_t off = (uint32_t)(s * FA_TILE_BYTES + h * FA_HALF_TILE + pg * box_rows * 128);
-                        fa_tma_2d(fa_smem(k_stage) + off, &map_k, h * 64, row, bar);
-                        fa_tma_2d(fa_smem(v_stage) + off, &map_v, h * 64, row, bar);
-                    }
+                    const uint32_t off = (uint32_t)(s * FA_TILE_BYTES + h * FA_HALF_TILE + pg * box_rows * 128);
+                    fa_tma_2d(fa_smem(which ? v_stage : k_stage) + off, which ? &map_v : &map_k, h * 64, row, bar);
                 }
             }
         }

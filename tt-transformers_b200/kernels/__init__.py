@@ -442,8 +442,10 @@ class CudaKernels:
         if plan is not None:
             return plan
         decode_shape = batch.max_seg_len * rep <= 16 and not big_tiles
-        rows = (int(self.lib.ttb_attention_tcgen05_tile_rows()) if big_tiles
-                else int(self.lib.ttb_attention_mma_tile_rows(1 if decode_shape else 0)))
+        if big_tiles:
+            rows = int(self.lib.ttb_attention_tcgen05_tile_rows())
+        else:
+            rows = int(self.lib.ttb_attention_mma_tile_rows(1 if decode_shape else 0))
         tokens_per_tile = max(1, rows // rep)
         if decode_shape:
             seg, tok0, n_tiles = None, None, batch.num_segments
