@@ -277,3 +277,18 @@ def test_greedy_decoding_on_the_device_across_context_buckets(tiny_folders):
     rest = engine.decode_steps(["g0", "g1"], firsts, 59)
     assert [[firsts[i]] + [row[i] for row in rest] for i in range(2)] == expect
     llm.cleanup()
+
+
+def test_the_references_benchmark_cases_on_a_tiny_model(tiny_folders):
+    """eval-32 (the same prompts rotated through the rows of a 32-request batch give the same outputs) and
+    token-accuracy (teacher forcing, bfloat16 against the float32 path) as bin/benchmark runs them."""
+    from tt_transformers_b200 import from_pretrained
+    from tt_transformers_b200.cli.benchmark import run_eval_32, run_token_accuracy
+
+    llm = from_pretrained(tiny_folders["D"], dtype="bfloat16", max_batch_size=32, max_seq_len=256)
+    result = run_eval_32(llm, repeats=3, new_tokens=16)
+    llm.cleanup()
+    assert result == {"repeats": 3, "prompts": 32, "deterministic": True}
+    accuracy = run_token_accuracy(lambda dtype: from_pretrained(tiny_folders["D"], dtype=dtype, max_batch_size=1,
+                                                                max_seq_len=512), prompt_len=200, forced=100)
+    assert accuracy["positions"] == 101 and accuracy["top5"] >= 0.99 and accuracy["top1"] >= 0.9, accuracy
