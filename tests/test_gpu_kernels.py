@@ -45,6 +45,25 @@ def test_embedding(kernels, twin, dtype, vocab, width, tokens):
     assert torch.equal(kernels.embedding(table, ids), twin.embedding(table, ids))
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_embedding_with_a_scale_and_softcap(kernels, twin, dtype):
+    g = torch.Generator(device="cuda").manual_seed(2)
+    for vocab, width in ((50, 24), (301, 100), (64, 1027)):           # widths with and without the 16-byte path
+        table = torch.randn(vocab, width, device="cuda", generator=g).to(dtype)
+        ids = torch.randint(0, vocab, (13,), device="cuda", generator=g, dtype=torch.int32)
+        got = kernels.embedding(table, ids, 5.5)
+        assert torch.allclose(got, table[ids.long()].float() * 5.5, rtol=1e-6, atol=0)
+    for rows, cols, cap in ((3, 1000, 30.0), (1, 128256, 50.0), (70, 33, 2.5)):
+        logits = torch.randn(rows, cols + 5, device="cuda", generator=g) * 3 * cap
+        view = logits[:, :cols]                                       # rows further apart than their length
+        want = cap * torch.tanh(view.double() / cap)
+        untouched = logits[:, cols:].clone()
+        kernels.softcap(view, cap)
+        assert float((view.double() - want).abs().max()) <= 2e-6 * cap
+        assert torch.equal(logits[:, cols:], untouched)
+        assert float(view.abs().max()) <= cap
+
+
 def test_embedding_flags_bad_token(kernels):
     from tt_transformers_b200.kernels import EngineDeviceError
 

@@ -132,3 +132,28 @@ def test_attention_part_with_its_cache(dtype, tol, heads, kv_heads, head_dim, wi
     rt.kernels.check_status()
     for rid in xs:
         close(torch.cat(got[rid]), ref[rid], tol)
+
+
+@pytest.mark.parametrize("dtype,tol", DTYPES)
+def test_embedding_and_head_parts(dtype, tol):
+    """The `table` embedding with a scale; the `linear` head with a weight of its own and tied to the embedding,
+    with a scale and a cap on its logits."""
+    g = torch.Generator().manual_seed(5)
+    table = (torch.randn(300, 72, generator=g) * 0.3).to(dtype).float()
+    own = (torch.randn(300, 72, generator=g) * 0.3).to(dtype).float()
+    emb = build_part("embedding", PartSpec("table", dict(vocab=300, width=72, weight_name="e", scale=72 ** 0.5)))
+    tied = build_part("head", PartSpec("linear", dict(vocab=300, width=72, weight_name=None, logit_cap=4.0)))
+    untied = build_part("head", PartSpec("linear", dict(vocab=300, width=72, weight_name="h", scale=0.25)))
+    assert tied.tied and not untied.tied and tied.tensor_specs() == [] and untied.tensor_specs()[0].name == "h"
+    tied.tie(emb)
+    rt = runtime(dtype)
+    for part in (emb, tied, untied):
+        part.bind({"e": table, "h": own}, rt)
+    assert tied.weight.data_ptr() == emb.table.data_ptr()            # the same storage, not a copy
+    ids = torch.tensor([0, 299, 17, 17, 5], dtype=torch.int32, device="cuda")
+    close(emb.forward(ids), table[ids.long().cpu()] * 72 ** 0.5, 1e-6)
+    h = torch.randn(6, 72, generator=g).to(dtype)
+    close(tied.forward(h.cuda()), 4.0 * torch.tanh(h.float() @ table.T / 4.0), tol)
+    close(untied.forward(h.cuda()), 0.25 * (h.float() @ own.T), tol)
+    with pytest.raises(ValueError):
+        build_part("head", PartSpec("linear", dict(vocab=3, width=2, weight_name=None, logit_cap=0.0)))
