@@ -70,3 +70,26 @@ def test_random_configuration_and_trace(tmp_path, seed):
                 err = helpers.relative_error(got[rid], ref[rid])
                 assert err < tol, (cfg, dtype, make.__name__, rid, err)
             engine.close()
+
+
+@pytest.mark.parametrize("seed", range(int(os.environ.get("TTB200_RANDOM_CONFIGS", "10"))))
+def test_random_configuration_generates_the_plain_tokens(tmp_path, seed):
+    """Greedy generation through the entry point (captured prompt steps for lone prompts, captured decode steps,
+    the step ahead of the host) for a randomly drawn configuration, in 32-bit: the plain implementation's tokens."""
+    import plain_llama
+    from tt_transformers_b200 import from_pretrained
+    from tt_transformers_b200.weights import write_model_folder
+
+    rng = random.Random(5000 + seed)
+    cfg = draw_config(rng)
+    std = min(0.06, 1.2 / cfg["hidden_size"] ** 0.5)
+    folder = write_model_folder(str(tmp_path / "m"), cfg, seed=seed, std=std, norm_std=0.1, dtype=torch.float32)
+    config, weights = plain_llama.read_model_folder(folder)
+    prompts = [helpers.random_tokens(cfg["vocab_size"], rng.randint(2, 70), seed * 10 + i) for i in range(3)]
+    expect = [plain_llama.greedy(config, weights, p, 7) for p in prompts]
+    llm = from_pretrained(folder, dtype="float32", page_size=rng.choice([8, 16, 32]), max_batch_size=4, max_seq_len=128)
+    assert llm.generate(prompts[:1], max_new_tokens=7) == expect[:1]           # alone: a captured prompt step
+    assert llm.engine.prompt_graphs.replays == 1
+    assert llm.generate(prompts, max_new_tokens=7) == expect                     # together: a mixed first step
+    assert llm.engine.cache.free_pages() == llm.engine.cache.num_pages
+    llm.cleanup()
