@@ -292,3 +292,28 @@ def test_the_references_benchmark_cases_on_a_tiny_model(tiny_folders):
     accuracy = run_token_accuracy(lambda dtype: from_pretrained(tiny_folders["D"], dtype=dtype, max_batch_size=1,
                                                                 max_seq_len=512), prompt_len=200, forced=100)
     assert accuracy["positions"] == 101 and accuracy["top5"] >= 0.99 and accuracy["top1"] >= 0.9, accuracy
+
+
+def test_abort_and_the_references_argument_names(tiny_folders):
+    from tt_transformers_b200 import SamplingParams, from_pretrained
+
+    with pytest.raises(TypeError):
+        from_pretrained()
+    with pytest.raises(ValueError):
+        from_pretrained(hf_model=tiny_folders["A"], optimizations="fast")
+    llm = from_pretrained(hf_model=tiny_folders["D"], optimizations="accuracy", max_batch_size=4, max_seq_len=128)
+    assert llm.engine.runtime.dtype == torch.float32
+    prompts = [helpers.random_tokens(512, n, 800 + n) for n in (9, 21, 14)]
+    alone = llm.generate([prompts[0], prompts[2]], max_new_tokens=20)
+    params = SamplingParams(max_new_tokens=20)
+    reqs = [llm.add_request(p, params) for p in prompts]
+    for _ in range(6):
+        llm.step()
+    llm.abort(reqs[1])                                     # in the middle of decoding, a step may be running ahead
+    while llm.has_unfinished():
+        llm.step()
+    assert reqs[1].finish_reason == "aborted" and 0 < len(reqs[1].output) < 20
+    assert [reqs[0].output, reqs[2].output] == alone       # the others are not disturbed
+    llm.engine.cache.audit()
+    assert llm.engine.cache.free_pages() == llm.engine.cache.num_pages
+    llm.cleanup()

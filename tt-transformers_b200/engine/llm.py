@@ -135,6 +135,16 @@ class LLM:
         self._next_id += 1
         return self._scheduler.add(self._next_id, prompt, params)
 
+    def abort(self, request: Request) -> None:
+        """Take a request out: its pages and slot are given back, its finish_reason becomes "aborted". A step
+        that was launched ahead with it is taken back first."""
+        if self._scheduler is None or request.finished:
+            return
+        if self._ahead is not None:
+            self._take_back(self._ahead)
+            self._ahead = None
+        self._scheduler.abort(request.request_id)
+
     def has_unfinished(self) -> bool:
         return self._scheduler is not None and self._scheduler.has_work()
 
@@ -268,13 +278,24 @@ def _load_tokenizer(folder: str):
         return None
 
 
-def from_pretrained(model: str, *, max_batch_size: int = 32, max_seq_len: int = 4096, n_layers: Optional[int] = None,
+def from_pretrained(model: Optional[str] = None, *, hf_model: Optional[str] = None, max_batch_size: int = 32,
+                    max_seq_len: int = 4096, n_layers: Optional[int] = None, optimizations: Optional[str] = None,
                     dtype: str = "bfloat16", page_size: int = 16, num_pages: Optional[int] = None,
                     max_step_tokens: int = 2048, max_chunk_tokens: int = 2048, cuda_graph: bool = True,
                     gpu_memory_fraction: Optional[float] = None, graph_batch_sizes=None, admission: str = "eager",
                     device: str = "cuda:0", kernels=None) -> LLM:
     """Load the model folder `model` (config.json + safetensors; the class is chosen by
-    config.json) and return an LLM ready to generate."""
+    config.json) and return an LLM ready to generate. `hf_model` is the reference's name for the same
+    argument (there a hub id, here a folder); `optimizations` is its choice of precision recipe
+    (src/tt_transformers/models/llama32_1b/hf_generator.py:380-394): "performance" computes in bfloat16,
+    "accuracy" in float32, and either overrides `dtype`."""
+    if (model is None) == (hf_model is None):
+        raise TypeError("give the model folder once: from_pretrained(folder) or from_pretrained(hf_model=folder)")
+    model = model if model is not None else hf_model
+    if optimizations is not None:
+        if optimizations not in ("performance", "accuracy"):
+            raise ValueError(f"optimizations must be 'performance' or 'accuracy', got {optimizations!r}")
+        dtype = "bfloat16" if optimizations == "performance" else "float32"
     dtype = {"bf16": "bfloat16", "fp32": "float32", torch.bfloat16: "bfloat16", torch.float32: "float32"}.get(dtype, dtype)
     config = EngineConfig(dtype=dtype, page_size=page_size, num_pages=num_pages, max_batch_size=max_batch_size,
                           max_seq_len=max_seq_len, max_step_tokens=max_step_tokens,
