@@ -457,6 +457,44 @@ def test_sample_draws_exactly_from_the_sets_the_references_host_sampler_allows(k
             assert float((freq - probs).abs().sum()) / 2 < 0.08, what         # total variation
 
 
+@pytest.mark.parametrize("vocab", [33, 257, 5000, 128256])
+def test_sample_top_k_with_many_equal_logits(kernels, twin, vocab):
+    """top_k up to the candidate list's length is found slice by slice (a radix select per slice, then per row).
+    Logits rounded to halves give long runs of equal values at every cut: the k largest with the lowest ids first
+    among equals, exactly as the plain twin picks them."""
+    g = torch.Generator(device="cuda").manual_seed(vocab)
+    rows = 4 if vocab > 10000 else 40
+    logits = torch.round(torch.randn(rows, vocab, device="cuda", generator=g) * 2) / 2
+    logits[1] = 0.0                                           # every logit equal: the first k ids
+    logits[2, ::3] = float("-inf")
+    temperature = torch.full((rows,), 1.3, device="cuda")
+    seeds = torch.arange(rows, device="cuda", dtype=torch.int64) * 31 + 7
+    for top_k, top_p in ((1, 1.0), (2, 1.0), (7, 1.0), (33, 0.8), (50, 1.0), (64, 0.5)):
+        for counter in range(3):
+            counters = torch.full((rows,), counter, device="cuda", dtype=torch.int32)
+            k = torch.full((rows,), top_k, device="cuda", dtype=torch.int32)
+            p = torch.full((rows,), top_p, device="cuda")
+            got = kernels.sample(logits, temperature, k, p, seeds, counters).cpu()
+            ref = twin.sample(logits, temperature, k, p, seeds, counters).cpu()
+            # a draw within rounding of a bin's edge may fall either way; the sets must be the same, so most picks are
+            assert float((got == ref).float().mean()) >= 0.9, (top_k, top_p, got.tolist(), ref.tolist())
+            assert int(got[1]) < min(top_k, vocab)            # all equal: one of the first k ids
+    # rows of one batch with every kind of setting: greedy, the whole vocabulary, a short list, a long one, top_p alone
+    kinds = [(0.0, 0, 1.0), (0.9, 0, 1.0), (0.9, 5, 1.0), (0.9, min(100, vocab), 1.0), (0.9, 0, 0.7), (0.9, 64, 0.9)]
+    t = torch.tensor([x[0] for x in kinds], device="cuda")
+    k = torch.tensor([x[1] for x in kinds], device="cuda", dtype=torch.int32)
+    p = torch.tensor([x[2] for x in kinds], device="cuda")
+    mixed = torch.randn(len(kinds), vocab, device="cuda", generator=g) * 2
+    sd = torch.arange(len(kinds), device="cuda", dtype=torch.int64) + 100
+    same = 0
+    for counter in range(5):
+        c = torch.full((len(kinds),), counter, device="cuda", dtype=torch.int32)
+        got, ref = kernels.sample(mixed, t, k, p, sd, c).cpu(), twin.sample(mixed, t, k, p, sd, c).cpu()
+        assert int(got[0]) == int(ref[0])
+        same += int((got == ref).sum())
+    assert same >= 27
+
+
 def test_sample_distribution(kernels):
     """Draws over many counters follow softmax(logits / temperature)."""
     logits = torch.tensor([[0.0, 1.0, 2.0, 3.0, -50.0]], device="cuda").repeat(4096, 1)

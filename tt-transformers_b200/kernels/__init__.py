@@ -86,7 +86,7 @@ class CudaKernels:
                      "ttb_gemv_mma", "ttb_gemv_mma_fused", "ttb_gemv_mma_parts", "ttb_argmax", "ttb_attention_decode_merges_in_kernel", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm",
                      "ttb_gemm_tcgen05", "ttb_paged_attention_tcgen05", "ttb_attention_tcgen05_supports",
                      "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge", "ttb_gemv_qkv_rope",
-                     "ttb_gemm_skinny_tcgen05", "ttb_gemm_skinny_tcgen05_rows", "ttb_softcap"):
+                     "ttb_gemm_skinny_tcgen05", "ttb_gemm_skinny_tcgen05_rows", "ttb_softcap", "ttb_sample_scratch_bytes"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -549,9 +549,15 @@ class CudaKernels:
                                             self._p(out), self._stream()), "argmax")
             self.launches += 1
             return out
+        # rows with a top_k up to the kernel's candidate list: candidates per slice of the vocabulary, then per row
+        scratch = None
+        if temperature is not None and top_k is not None:
+            scratch = torch.empty(int(self.lib.ttb_sample_scratch_bytes(rows)), dtype=torch.uint8, device=self.device)
         self._check(self.lib.ttb_sample(self._p(logits), logits.stride(0), rows, vocab, self._p(temperature),
                                         self._p(top_k), self._p(top_p), self._p(seeds), self._p(counters),
-                                        self._p(out), self._stream()), "sample")
+                                        self._p(out), self._p(scratch), self._stream()), "sample")
+        if scratch is not None:
+            self.launches += 2
         return out
 
     def uniform(self, seed: int, counter: int) -> float:
