@@ -317,3 +317,23 @@ def test_abort_and_the_references_argument_names(tiny_folders):
     llm.engine.cache.audit()
     assert llm.engine.cache.free_pages() == llm.engine.cache.num_pages
     llm.cleanup()
+
+
+def test_warmup_captures_every_step_ahead_of_time(tiny_folders):
+    from tt_transformers_b200 import from_pretrained
+
+    prompts = [helpers.random_tokens(512, n, 900 + n) for n in (12, 40, 7)]
+    plain = from_pretrained(tiny_folders["D"], dtype="float32", max_batch_size=4, max_seq_len=2048)
+    expect = plain.generate(prompts, max_new_tokens=10) + plain.generate(prompts[:1], max_new_tokens=10)
+    plain.cleanup()
+    llm = from_pretrained(tiny_folders["D"], dtype="float32", max_batch_size=4, max_seq_len=2048)
+    captured = llm.warmup()
+    # batch sizes 1, 2, 4 in the context buckets 1,024 and 2,048; prompt buckets 32 .. 512
+    assert captured == 3 * 2 + 5 and llm.engine.cache.free_pages() == llm.engine.cache.num_pages
+    assert llm.warmup() == 0
+    decode_graphs, prompt_graphs = dict(llm.engine.graphs._graphs), dict(llm.engine.prompt_graphs._graphs)
+    got = llm.generate(prompts, max_new_tokens=10) + llm.generate(prompts[:1], max_new_tokens=10)
+    assert got == expect
+    assert llm.engine.graphs._graphs.keys() == decode_graphs.keys()           # nothing was captured while generating
+    assert llm.engine.prompt_graphs._graphs.keys() == prompt_graphs.keys()
+    llm.cleanup()

@@ -263,6 +263,12 @@ class LLM:
                 self._scheduler = None
             self._busy = False
 
+    def warmup(self, **options) -> int:
+        """Capture every decode and prompt step ahead of time (Engine.warmup); call it before serving."""
+        if self._scheduler is not None and self._scheduler.has_work():
+            raise RuntimeError("warmup() wants an idle model")
+        return self.engine.warmup(**options)
+
     def cleanup(self) -> None:
         """Free the cache and the weights (the reference's cleanup(), hf_generation.py:416-436)."""
         self.engine.close()

@@ -302,6 +302,56 @@ class Engine:
         torch.cuda.current_stream(self.runtime.device).synchronize()
         return host.tolist()
 
+    def warmup(self, batch_sizes=None, context_buckets=None, prompts: bool = True) -> int:
+        """Capture ahead of time what would otherwise be captured at first use, so that no request waits for a
+        capture: decode steps for every captured batch size (or those given) and context bucket (or those given),
+        and the prompt steps of every length bucket. Needs an engine without live requests; takes pages for as
+        many one-token requests as the largest batch size and gives them back. Returns how many steps were
+        captured. The reference warms its traces up in the same way before serving
+        (src/tt_transformers/llm_runtime/config.py:18-75, WarmupConfig)."""
+        if self.graphs is None:
+            return 0
+        if self.cache.live_requests():
+            raise RuntimeError("warmup() wants an engine without live requests")
+        graphs, captured = self.graphs, 0
+        sizes = [s for s in (batch_sizes or graphs.sizes) if s <= self.config.max_batch_size]
+        if context_buckets is None:
+            context_buckets, bucket = [], graphs.MIN_CONTEXT_BUCKET
+            while bucket < self.max_seq_len:
+                context_buckets.append(bucket)
+                bucket *= 2
+            context_buckets.append(self.max_seq_len)
+        context_buckets = sorted({min(b, self.max_seq_len) for b in context_buckets})
+        ids = [("warmup", i) for i in range(max(sizes, default=0))]
+        try:
+            for rid in ids:
+                self.cache.admit(rid)
+                self.cache.reserve(rid, 1)
+            for size in sizes:
+                entries = [StepEntry(rid, [0], [0]) for rid in ids[:size]]
+                for bucket in context_buckets:
+                    if (size, bucket) not in graphs._graphs:
+                        graphs._graphs[(size, bucket)] = graphs._capture(size, bucket, entries)
+                        captured += 1
+        finally:
+            for rid in ids:
+                if self.cache.is_live(rid):
+                    self.cache.release(rid)
+        if prompts and self.prompt_graphs is not None:
+            for size in self.prompt_graphs.sizes:
+                if size in self.prompt_graphs._graphs:
+                    continue
+                rid = ("warmup", "prompt")
+                self.cache.admit(rid)
+                try:
+                    self.cache.reserve(rid, 2)
+                    self.prompt_graphs._graphs[size] = self.prompt_graphs._capture(size, [StepEntry(rid, [0, 0], [1])])
+                    captured += 1
+                finally:
+                    self.cache.release(rid)
+        torch.cuda.synchronize(self.runtime.device)
+        return captured
+
     def close(self) -> None:
         for rid in self.cache.live_requests():
             self.cache.release(rid)
