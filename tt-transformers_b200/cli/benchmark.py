@@ -14,6 +14,8 @@ The engine's own cases (one JSON object out; `--json FILE` also writes it to a f
     --case decode-sweep     decode steps over batch sizes 1, 8, 32, 64 and contexts 2,048, 8,192, 32,768 under ONE engine
                             whose context limit is 32,768 (cache filled with random numbers; combinations whose cache
                             exceeds 90 GB left out): step time and share of the HBM peak for each
+    --case prefill-sweep    one prompt of 128, 512, 2,048, 8,192 and 32,768 tokens through the step function in portions of
+                            at most 2,048 tokens: time, tokens/s and share of the bf16 peak (products and causal attention)
     --model {1b,3b,8b}      layer sizes (random weights); --n-layers cuts the model short
     --context N --steps K   context held while decoding, timed decode steps
 
@@ -50,7 +52,7 @@ import torch
 
 EXAMPLE_CASES = ("token-accuracy", "batch-1", "batch-32", "batch-32-ci", "eval-32")
 ENGINE_CASES = ("prefill-2048", "decode-b1", "decode-b8", "decode-b64", "mixed-3b", "decode-8b-b64", "token-match", "all")
-EXTRA_CASES = ("decode-sweep",)
+EXTRA_CASES = ("decode-sweep", "prefill-sweep")
 
 
 def _prompts(vocab, batch, seed=0, low=90, high=125):
@@ -143,6 +145,35 @@ def run_engine_case(case: str, model: str, context: int, steps: int, warmup: int
         engine.close()
         return {"case": case, "model": m.MODEL_NAMES.get(model or "1b"), "layers": layers, "context_limit": 32768 + 64,
                 "peaks": m.peaks()["source"], "rows": rows}
+    if case == "prefill-sweep":
+        from ..engine.step import StepEntry
+
+        cfg = measure.model_config(model or "1b")
+        layers = n_layers or cfg["num_hidden_layers"]
+        cfg = dict(cfg, num_hidden_layers=layers)
+        pk = measure.peaks()
+        portion = measure.PREFILL_TOKENS
+        engine = measure.make_engine(cfg, max_batch=1, context=32768 + 64)
+        prompts = measure.Prompts(cfg["vocab_size"])
+        rows = []
+        for n in (128, 512, 2048, 8192, 32768):
+            ids = prompts(n)
+
+            def once():
+                for at in range(0, n, portion):
+                    part = ids[at:at + portion]
+                    engine.step([StepEntry("p", part, [len(part) - 1] if at + portion >= n else [])])
+                engine.finish("p")
+
+            for _ in range(2):
+                once()
+            ms = measure.timed(once, 3)
+            flops = measure.prefill_flops(cfg, layers, n)
+            rows.append({"tokens": n, "ms": round(ms, 3), "tokens_per_s": round(n / ms * 1e3),
+                         "frac": round(flops / (ms * 1e-3) / (pk["bf16_tflops"] * 1e12), 3)})
+        engine.close()
+        return {"case": case, "model": measure.MODEL_NAMES.get(model or "1b"), "layers": layers, "portion": portion,
+                "peaks": pk["source"], "rows": rows}
     if case == "all":
         out = {}
         for each in ENGINE_CASES[:-1]:
