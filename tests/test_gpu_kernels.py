@@ -590,6 +590,37 @@ def test_tcgen05_product_that_streams_the_weights(kernels, twin, M, N, K):
         close(fused, twin.linear_swiglu(x.double(), w.double()), torch.bfloat16)
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 2048, 2048), (8, 8192, 2048), (5, 1000, 1544), (7, 520, 264), (2, 100, 48),
+                                   (8, 2048, 8192), (3, 6, 4104), (8, 3072, 3072), (4, 160, 24576)])
+def test_persistent_product_that_streams_the_weights_through_a_ring(kernels, twin, M, N, K):
+    """gemv_ring.cu (up to 8 rows): every kind of product it may be given (plain with either output type, the
+    SwiGLU pair) whether the engine routes that kind there or not; widths with fewer rows than blocks and with rows
+    no multiple of a tile, a reduction that is no multiple of a step of 512, x in shared memory (short K) and from
+    global memory (long K). The other skinny kernel is the second opinion beside float64."""
+    g = torch.Generator(device="cuda").manual_seed(12)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K) * 2).to(torch.bfloat16)
+    before = kernels.ring_gemv, kernels.RING_SWIGLU_MIN_ROWS
+    try:
+        kernels.ring_gemv, kernels.RING_SWIGLU_MIN_ROWS = 15, 1
+        launches = kernels.launches
+        got = kernels.linear(x, w)
+        got32 = kernels.linear(x, w, out_dtype=torch.float32)
+        fused = kernels.linear_swiglu(x, w) if N % 2 == 0 else None
+        assert kernels.launches - launches == (3 if N % 2 == 0 else 2), "one launch of this package's kernels per product"
+        kernels.ring_gemv = 0
+        other = kernels.linear(x, w)
+    finally:
+        kernels.ring_gemv, kernels.RING_SWIGLU_MIN_ROWS = before
+    ref = x.double() @ w.double().t()
+    close(got, ref, torch.bfloat16)
+    assert got32.dtype == torch.float32
+    close(got32, ref, torch.bfloat16)
+    close(got, other, torch.bfloat16)
+    if fused is not None:
+        close(fused, twin.linear_swiglu(x.double(), w.double()), torch.bfloat16)
+
+
 @pytest.mark.parametrize("M,N,K", [(17, 320, 96), (32, 2048, 2048), (40, 100, 1000), (64, 3072, 2048), (64, 2048, 8192)])
 def test_skinny_tensor_core_product_at_all_its_row_counts(kernels, twin, M, N, K):
     """The mma.sync weight-streaming kernel takes up to 64 rows, although the engine hands it 16 at most."""

@@ -65,6 +65,8 @@ class CudaKernels:
     # skinny kernel (measured at 9, 12 and 16 rows: down projection 10.8 to 11.1 us against 13.5 to 14.1, gate/up
     # with SwiGLU 14.5 to 15.5 against 17.3 to 18.6)
     SKINNY_TCGEN05_MIN_ROWS = 9
+    RING_ROWS = 8
+    RING_SWIGLU_MIN_ROWS = 6
 
     def __init__(self, device: torch.device):
         if not torch.cuda.is_available():
@@ -86,7 +88,8 @@ class CudaKernels:
                      "ttb_gemv_mma", "ttb_gemv_mma_fused", "ttb_gemv_mma_parts", "ttb_argmax", "ttb_attention_decode_merges_in_kernel", "ttb_paged_attention_mma_checked", "ttb_attention_mma_blocks_per_sm",
                      "ttb_gemm_tcgen05", "ttb_paged_attention_tcgen05", "ttb_attention_tcgen05_supports",
                      "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge", "ttb_gemv_qkv_rope",
-                     "ttb_gemm_skinny_tcgen05", "ttb_gemm_skinny_tcgen05_rows", "ttb_softcap", "ttb_sample_scratch_bytes"):
+                     "ttb_gemm_skinny_tcgen05", "ttb_gemm_skinny_tcgen05_rows", "ttb_softcap", "ttb_sample_scratch_bytes",
+                     "ttb_gemv_ring"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -106,6 +109,13 @@ class CudaKernels:
         # that follows there, which the next skinny product finishes (fuse_norm)
         self.fuse_norm = os.environ.get("TTB200_FUSE_NORM", "0") == "1"
         self.fuse_add = os.environ.get("TTB200_FUSE_ADD", "0") == "1"
+        # products of up to RING_ROWS rows by the persistent kernel of gemv_ring.cu, a bit for each kind:
+        # 1 gate/up with SwiGLU (from RING_SWIGLU_MIN_ROWS rows on), 2 plain products with a long reduction (down),
+        # 4 the other plain products with bfloat16 output (output projection), 8 products with float32 output (the
+        # LM head). Measured inside the decode step at Llama 3.2 1B sizes, ms a step at batch 1 / 2 / 4 / 8 against
+        # 0.793 / 0.842 / 0.928 / 1.106 without: bit 4 alone 0.774 / 0.824 / 0.907 / 1.076; bit 1 alone 0.814 /
+        # 0.857 / 0.930 / 1.094; bit 8 alone 0.797 / 0.845 / 0.932 / 1.109; bits 1 and 2 1.101 at batch 8.
+        self.ring_gemv = int(os.environ.get("TTB200_RING_GEMV", "5"))
         # bfloat16 products with more rows than the skinny kernel takes: the TMA + tcgen05 kernel of
         # gemm_tcgen05.cu or the library's product. None (TTB200_TCGEN05 unset or "auto"): the feed-forward's
         # gate/up product with its fused SwiGLU goes to the tcgen05 kernel from TCGEN05_SWIGLU_ROWS rows on
@@ -265,6 +275,12 @@ class CudaKernels:
                 if not fuse_add:
                     return out
                 return prepared if prepared is not None else ADDED
+            kind = 8 if out_dtype != torch.bfloat16 else (2 if K >= self.SKINNY_TCGEN05_MIN_K else 4)
+            if M <= self.RING_ROWS and (self.ring_gemv & kind):
+                out = torch.empty(M, N, dtype=out_dtype, device=self.device)
+                self._check(self.lib.ttb_gemv_ring(self._p(x), self._p(w), self._p(out), _dtype_code(out_dtype), M, N, K,
+                                                   x.stride(0), w.stride(0), N, 0, self._stream()), "gemv_ring")
+                return out
             # 9 to 16 rows, nothing fused, bfloat16 out (QKV and output projection): the library is as fast at
             # Llama 3.2 1B sizes and 1.1 to 1.3 times faster at 3B and 8B sizes (measured at 10 and 16 rows)
             if M <= self.SKINNY_ROWS or out_dtype != torch.bfloat16:
@@ -329,9 +345,11 @@ class CudaKernels:
                 and x.stride(0) % 8 == 0 and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1
                 and w_gate_up.stride(1) == 1):
             out = torch.empty(M, inter, dtype=x.dtype, device=self.device)
-            self._check(self.lib.ttb_gemv_mma(self._p(x), self._p(w_gate_up), self._p(out), _dtype_code(x.dtype), M,
-                                              inter, K, x.stride(0), w_gate_up.stride(0), inter, inter,
-                                              self._stream()), "gemv_mma_swiglu")
+            entry = (self.lib.ttb_gemv_ring if ((self.ring_gemv & 1) and self.RING_SWIGLU_MIN_ROWS <= M <= self.RING_ROWS)
+                     else self.lib.ttb_gemv_mma)
+            self._check(entry(self._p(x), self._p(w_gate_up), self._p(out), _dtype_code(x.dtype), M,
+                              inter, K, x.stride(0), w_gate_up.stride(0), inter, inter,
+                              self._stream()), "gemv_swiglu")
             return out
         if streams:
             out = torch.empty(M, inter, dtype=x.dtype, device=self.device)
