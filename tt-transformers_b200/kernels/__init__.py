@@ -67,6 +67,7 @@ class CudaKernels:
     SKINNY_TCGEN05_MIN_ROWS = 9
     RING_ROWS = 8
     RING_SWIGLU_MIN_ROWS = 6
+    RING_SWIGLU_ANY_ROWS_BYTES = 80 << 20
 
     def __init__(self, device: torch.device):
         if not torch.cuda.is_available():
@@ -110,7 +111,9 @@ class CudaKernels:
         self.fuse_norm = os.environ.get("TTB200_FUSE_NORM", "0") == "1"
         self.fuse_add = os.environ.get("TTB200_FUSE_ADD", "0") == "1"
         # products of up to RING_ROWS rows by the persistent kernel of gemv_ring.cu, a bit for each kind:
-        # 1 gate/up with SwiGLU (from RING_SWIGLU_MIN_ROWS rows on), 2 plain products with a long reduction (down),
+        # 1 gate/up with SwiGLU (from RING_SWIGLU_MIN_ROWS rows on, or at any number of rows when the matrix has
+        # RING_SWIGLU_ANY_ROWS_BYTES or more: at Llama 3.2 3B and 3.1 8B sizes it wins from one row on, 2.09 against
+        # 2.17 ms and 3.54 against 3.62 ms a step at batch 1), 2 plain products with a long reduction (down),
         # 4 the other plain products with bfloat16 output (output projection), 8 products with float32 output (the
         # LM head). Measured inside the decode step at Llama 3.2 1B sizes, ms a step at batch 1 / 2 / 4 / 8 against
         # 0.793 / 0.842 / 0.928 / 1.106 without: bit 4 alone 0.774 / 0.824 / 0.907 / 1.076; bit 1 alone 0.814 /
@@ -345,8 +348,9 @@ class CudaKernels:
                 and x.stride(0) % 8 == 0 and w_gate_up.stride(0) % 8 == 0 and x.stride(1) == 1
                 and w_gate_up.stride(1) == 1):
             out = torch.empty(M, inter, dtype=x.dtype, device=self.device)
-            entry = (self.lib.ttb_gemv_ring if ((self.ring_gemv & 1) and self.RING_SWIGLU_MIN_ROWS <= M <= self.RING_ROWS)
-                     else self.lib.ttb_gemv_mma)
+            ring = ((self.ring_gemv & 1) and M <= self.RING_ROWS
+                    and (M >= self.RING_SWIGLU_MIN_ROWS or 2 * inter * K * 2 >= self.RING_SWIGLU_ANY_ROWS_BYTES))
+            entry = self.lib.ttb_gemv_ring if ring else self.lib.ttb_gemv_mma
             self._check(entry(self._p(x), self._p(w_gate_up), self._p(out), _dtype_code(x.dtype), M,
                               inter, K, x.stride(0), w_gate_up.stride(0), inter, inter,
                               self._stream()), "gemv_swiglu")
