@@ -424,7 +424,7 @@ TTB_EXPORT int ttb_gemv_mma_fused(const void* x, const float* ssq_in, int ssq_pa
 
 
 // The QKV projection of a decode step fused with the rotation and the cache write.
-// x [M <= 8, K], w [(heads + 2 kv_heads) * head_dim, K] (queries, keys, values stacked), bfloat16;
+// x [M <= 16, K], w [(heads + 2 kv_heads) * head_dim, K] (queries, keys, values stacked), bfloat16;
 // q_out [M, heads * head_dim] gets the rotated queries; rotated keys and the values go to their
 // pages. head_dim a multiple of 16, full rotary (every pair of a head is rotated).
 // ssq_in != null: x is g * residual and the projection is divided by the rows' RMS (see above).
@@ -438,12 +438,19 @@ TTB_EXPORT int ttb_gemv_qkv_rope(const void* x, const float* ssq_in, int ssq_par
     if (!x || !w || !q_out || !positions || !inv_freq || !status) return TTB_ERR_ARGUMENT;
     if (write_kv && (!seg_of_token || !key_pages || !value_pages || !block_table)) return TTB_ERR_ARGUMENT;
     if (ssq_in && ssq_parts < 1) return TTB_ERR_ARGUMENT;
-    if (M > 8 || K < 8 || (K & 7) || (ldx & 7) || (ldw & 7) || !aligned16(x) || !aligned16(w)) return TTB_ERR_UNSUPPORTED;
+    if (M > 16 || K < 8 || (K & 7) || (ldx & 7) || (ldw & 7) || !aligned16(x) || !aligned16(w)) return TTB_ERR_UNSUPPORTED;
     if (head_dim < 16 || (head_dim & 15)) return TTB_ERR_UNSUPPORTED;
     GmRope rope = {positions, seg_of_token, inv_freq, block_table, (__nv_bfloat16*)key_pages, (__nv_bfloat16*)value_pages,
                    status, table_width, page_size, num_pages, heads, kv_heads, head_dim, write_kv};
     GmFuse fuse = {ssq_in, ssq_parts, eps, nullptr, 0, nullptr, nullptr, 0, nullptr};
     const int N = (heads + 2 * kv_heads) * head_dim;
+    if (M > 8) {            // two blocks of eight tokens against the same weight fragments
+        if (ssq_in)
+            return gemv_mma_launch<2, 1, GM_ROPE, 8, __nv_bfloat16, true>(x, w, q_out, M, N, K, ldx, ldw, heads * head_dim,
+                                                                          head_dim / 2, stream, &rope, &fuse);
+        return gemv_mma_launch<2, 1, GM_ROPE, 8, __nv_bfloat16>(x, w, q_out, M, N, K, ldx, ldw, heads * head_dim,
+                                                                head_dim / 2, stream, &rope);
+    }
     if (ssq_in)
         return gemv_mma_launch<1, 1, GM_ROPE, 8, __nv_bfloat16, true>(x, w, q_out, M, N, K, ldx, ldw, heads * head_dim,
                                                                       head_dim / 2, stream, &rope, &fuse);
