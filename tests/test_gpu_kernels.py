@@ -646,7 +646,9 @@ def test_skinny_tensor_core_product_at_all_its_row_counts(kernels, twin, M, N, K
     (8, 2, 64, 16, [(300, 1), (0, 1), (17, 1)], 128), (32, 8, 64, 16, [(8000, 1)] * 8, 2048),
     (6, 2, 128, 8, [(63, 1), (64, 1)], 96), (4, 4, 16, 4, [(5, 1), (6, 1), (7, 1), (0, 1), (100, 1)], 72),
     (3, 1, 32, 8, [(40, 1)], 96), (8, 2, 64, 16, [(10 * i + 3, 1) for i in range(13)], 264),
-    (6, 2, 128, 8, [(7 * i, 1) for i in range(16)], 512)])
+    (6, 2, 128, 8, [(7 * i, 1) for i in range(16)], 512),
+    (8, 2, 64, 16, [(11 * i + 1, 1) for i in range(23)], 2048), (6, 2, 128, 8, [(5 * i, 1) for i in range(64)], 520),
+    (5, 1, 32, 8, [(3 * i + 2, 1) for i in range(40)], 96), (32, 8, 64, 16, [(100 + i, 1) for i in range(33)], 2048)])
 def test_fused_qkv_projection_rotation_and_cache_write(kernels, twin, heads, kv_heads, head_dim, page_size, segments, width):
     """One kernel for a decode step's QKV product, rotation and cache write against the three steps one by one."""
     _, batch, view = make_paged_case(torch.bfloat16, heads, kv_heads, head_dim, page_size, segments, seed=21)

@@ -17,6 +17,12 @@
 // multicast. Every wait on an mbarrier is bounded: a role that runs out of patience records a code in
 // *error_flag and goes on to the block's barriers, so that nobody in the cluster waits for it forever.
 // Sizes: M up to 64, any N, K a multiple of 8, row strides of 16 bytes.
+//
+// ROPE: the fused QKV projection of a decode step with more tokens than the mma.sync skinny kernel takes. W holds
+// the query, key and value rows of all heads; a tile of 128 rows holds whole heads (head sizes that divide 128), so
+// the rank that finishes a row of X has both halves of every rotation pair (i, i + head_dim / 2) at hand: it rotates
+// queries and keys by the token's position (float32 angles, accurate sincosf), writes the queries out and puts keys
+// and values straight into their cache pages. No rotation kernel, no round trip of the projection through memory.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -100,16 +106,33 @@ __device__ __forceinline__ void sk_cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// What the fused QKV form needs beyond the product: positions, rotation frequencies and the cache.
+struct SkRope {
+    const int* positions;        // [M]
+    const int* seg_of_token;     // [M]
+    const float* inv_freq;       // [head_dim / 2]
+    const int* block_table;      // [segments, table_width]
+    __nv_bfloat16* key_pages;    // [num_pages, kv_heads, page_size, head_dim]
+    __nv_bfloat16* value_pages;
+    int* status;
+    int table_width, page_size, num_pages, heads, kv_heads, head_dim, write_kv;
+};
+
+#define SK_PLAIN 0
+#define SK_SWIGLU 1
+#define SK_ROPE 2
+
 struct SkBars {
     uint64_t full[SK_MAX_STAGES], empty[SK_MAX_STAGES], acc_full;
 };
 
 // grid (row tiles of W, 1, S), cluster (1, 1, S): blockIdx.z is the block's rank in its cluster and its slice of K.
-template <int NX, bool SWIGLU, typename TO>
+template <int NX, int MODE, typename TO>
 __global__ void __launch_bounds__(SK_THREADS)
 gemm_skinny_tcgen05_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                            TO* __restrict__ out, int M, int N, int K, int ldc, int up_offset, int k_per_split,
-                           int stages_n, int* __restrict__ error_flag) {
+                           int stages_n, int* __restrict__ error_flag, const SkRope rope) {
+    constexpr bool SWIGLU = MODE == SK_SWIGLU;
     constexpr int X_BYTES = NX * SK_BK * 2;
     constexpr int STAGE_BYTES = SK_W_BYTES + X_BYTES;
     extern __shared__ unsigned char sk_raw[];
@@ -219,7 +242,80 @@ gemm_skinny_tcgen05_kernel(const __grid_constant__ CUtensorMap map_w, const __gr
     __syncthreads();
     if (S > 1) sk_cluster_sync();
     // ---------------------------------------------------------------------- rank r finishes its share of the rows of X
-    {
+    if (MODE == SK_ROPE) {
+        // An item is four consecutive elements of the first half of one head of one row of X, and their rotation
+        // partners half a head further on: 128 / 8 items a row of X.
+        const int rows_per_rank = NX / S;
+        const int m_first = split * rows_per_rank, m_last = min(M, m_first + rows_per_rank);
+        const int hd = rope.head_dim, half = hd >> 1;
+        const int groups = half >> 2;                                 // items per head
+        const int per_row = (SK_BW / hd) * groups;                    // = 16
+        const int items = m_first < m_last ? (m_last - m_first) * per_row : 0;
+        for (int i = tid; i < items; i += SK_THREADS) {
+            const int m = m_first + i / per_row, rest = i % per_row;
+            const int t = (rest / groups) * hd + (rest % groups) * 4;         // column of the tile: head and pair index
+            const float* src = partial + m * SK_BW + t;
+            float4 p[8], q[8];
+            if (S > 1) {
+                const uint32_t a = sk_smem(src);
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+                    if (r < S) {
+                        p[r] = sk_ld_cluster4(a, r);
+                        q[r] = sk_ld_cluster4(a + half * 4, r);
+                    }
+            } else {
+                p[0] = *reinterpret_cast<const float4*>(src);
+                q[0] = *reinterpret_cast<const float4*>(src + half);
+            }
+            float lower[4] = {0.f, 0.f, 0.f, 0.f}, upper[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+                if (r < S) {
+                    lower[0] += p[r].x; lower[1] += p[r].y; lower[2] += p[r].z; lower[3] += p[r].w;
+                    upper[0] += q[r].x; upper[1] += q[r].y; upper[2] += q[r].z; upper[3] += q[r].w;
+                }
+            const int n = n0 + t;                                    // row of W = element of the QKV row
+            if (n >= N) continue;
+            const int head = n / hd, e = n - head * hd;              // e < half, a multiple of 4
+            const bool is_q = head < rope.heads, is_k = !is_q && head < rope.heads + rope.kv_heads;
+            const int pos = rope.positions[m];
+            if (is_q || is_k) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float sn, cs;
+                    sincosf((float)pos * rope.inv_freq[e + j], &sn, &cs);
+                    const float u = lower[j], v = upper[j];
+                    lower[j] = u * cs - v * sn;
+                    upper[j] = v * cs + u * sn;
+                }
+            }
+            __nv_bfloat162 l01 = __floats2bfloat162_rn(lower[0], lower[1]), l23 = __floats2bfloat162_rn(lower[2], lower[3]);
+            __nv_bfloat162 u01 = __floats2bfloat162_rn(upper[0], upper[1]), u23 = __floats2bfloat162_rn(upper[2], upper[3]);
+            uint2 lo2, up2;
+            lo2.x = *reinterpret_cast<uint32_t*>(&l01); lo2.y = *reinterpret_cast<uint32_t*>(&l23);
+            up2.x = *reinterpret_cast<uint32_t*>(&u01); up2.y = *reinterpret_cast<uint32_t*>(&u23);
+            __nv_bfloat16* dst = nullptr;
+            if (is_q) {
+                dst = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)m * ldc + n;
+            } else if (rope.write_kv) {
+                const int kvh = head - rope.heads - (is_k ? 0 : rope.kv_heads);
+                const int page_index = pos / rope.page_size;
+                int page = -1;
+                if (page_index < rope.table_width)
+                    page = rope.block_table[(size_t)rope.seg_of_token[m] * rope.table_width + page_index];
+                if ((unsigned)page >= (unsigned)rope.num_pages)
+                    atomicExch(rope.status, 0x2000000 + m);          // outside the pool: skip the write, say so
+                else
+                    dst = (is_k ? rope.key_pages : rope.value_pages) +
+                          (((size_t)page * rope.kv_heads + kvh) * rope.page_size + (pos - page_index * rope.page_size)) * hd + e;
+            }
+            if (dst != nullptr) {
+                *reinterpret_cast<uint2*>(dst) = lo2;
+                *reinterpret_cast<uint2*>(dst + half) = up2;
+            }
+        }
+    } else {
         // An item is four consecutive columns of one row of X. All of an item's loads from the other blocks are
         // issued before the first sum, so that they are in flight together; the sums run in the order of the ranks.
         const int rows_per_rank = NX / S;
@@ -323,10 +419,11 @@ static int sk_splits(int tiles, int K) {
     return s;
 }
 
-template <int NX, bool SWIGLU, typename TO>
+template <int NX, int MODE, typename TO>
 static int sk_launch(const CUtensorMap& map_w, const CUtensorMap& map_x, void* C, int M, int N, int K, int ldc,
-                     int up_offset, int* error_flag, cudaStream_t stream) {
-    auto kernel = gemm_skinny_tcgen05_kernel<NX, SWIGLU, TO>;
+                     int up_offset, int* error_flag, cudaStream_t stream, const SkRope* rope = nullptr) {
+    constexpr bool SWIGLU = MODE == SK_SWIGLU;
+    auto kernel = gemm_skinny_tcgen05_kernel<NX, MODE, TO>;
     const size_t stage_bytes = SK_W_BYTES + NX * SK_BK * 2;
     static TtbOncePerDevice configured;
     if (configured.pending()) {
@@ -365,7 +462,9 @@ static int sk_launch(const CUtensorMap& map_w, const CUtensorMap& map_x, void* C
     }
     cfg.attrs = attr;
     cfg.numAttrs = n_attr;
-    cudaLaunchKernelEx(&cfg, kernel, map_w, map_x, (TO*)C, M, N, K, ldc, up_offset, k_per_split, stages_n, error_flag);
+    const SkRope none = {};
+    cudaLaunchKernelEx(&cfg, kernel, map_w, map_x, (TO*)C, M, N, K, ldc, up_offset, k_per_split, stages_n, error_flag,
+                       rope ? *rope : none);
     return ttb_launch_status();
 }
 
@@ -387,10 +486,40 @@ TTB_EXPORT int ttb_gemm_skinny_tcgen05(const void* X, const void* W, void* C, in
     if (!sk_make_map(&map_x, X, M, K, ldx, nx)) return TTB_ERR_UNSUPPORTED;
 #define SK_ARGS map_w, map_x, C, M, N, K, ldc, swiglu_rows, error_flag, stream
     if (nx == 32) {
-        if (swiglu_rows) return f32 ? sk_launch<32, true, float>(SK_ARGS) : sk_launch<32, true, __nv_bfloat16>(SK_ARGS);
-        return f32 ? sk_launch<32, false, float>(SK_ARGS) : sk_launch<32, false, __nv_bfloat16>(SK_ARGS);
+        if (swiglu_rows) return f32 ? sk_launch<32, SK_SWIGLU, float>(SK_ARGS) : sk_launch<32, SK_SWIGLU, __nv_bfloat16>(SK_ARGS);
+        return f32 ? sk_launch<32, SK_PLAIN, float>(SK_ARGS) : sk_launch<32, SK_PLAIN, __nv_bfloat16>(SK_ARGS);
     }
-    if (swiglu_rows) return f32 ? sk_launch<64, true, float>(SK_ARGS) : sk_launch<64, true, __nv_bfloat16>(SK_ARGS);
-    return f32 ? sk_launch<64, false, float>(SK_ARGS) : sk_launch<64, false, __nv_bfloat16>(SK_ARGS);
+    if (swiglu_rows) return f32 ? sk_launch<64, SK_SWIGLU, float>(SK_ARGS) : sk_launch<64, SK_SWIGLU, __nv_bfloat16>(SK_ARGS);
+    return f32 ? sk_launch<64, SK_PLAIN, float>(SK_ARGS) : sk_launch<64, SK_PLAIN, __nv_bfloat16>(SK_ARGS);
 #undef SK_ARGS
+}
+
+// The QKV projection of a decode step fused with the rotation and the cache write, for up to 64 tokens.
+// X [M, K], W [(heads + 2 kv_heads) * head_dim, K] (queries, keys, values stacked), bfloat16; q_out [M, heads *
+// head_dim] gets the rotated queries; rotated keys and the values go to their pages [num_pages, kv_heads,
+// page_size, head_dim]. head_dim 16, 32, 64 or 128 (whole heads in a tile of 128 rows), full rotary (every pair
+// (i, i + head_dim / 2) of a head is rotated).
+TTB_EXPORT int ttb_gemm_skinny_tcgen05_qkv_rope(const void* X, const void* W, void* q_out, int M, int K, int ldx, int ldw,
+                                                const int* positions, const int* seg_of_token, const float* inv_freq,
+                                                int heads, int kv_heads, int head_dim, void* key_pages, void* value_pages,
+                                                const int* block_table, int table_width, int page_size, int num_pages,
+                                                int write_kv, int* status, int* error_flag, cudaStream_t stream) {
+    if (M == 0) return TTB_OK;
+    if (!X || !W || !q_out || !positions || !inv_freq || !status || !error_flag) return TTB_ERR_ARGUMENT;
+    if (write_kv && (!seg_of_token || !key_pages || !value_pages || !block_table)) return TTB_ERR_ARGUMENT;
+    if (M > 64 || K < 8 || (K & 7) || (ldx & 7) || (ldw & 7) || !aligned16(X) || !aligned16(W)) return TTB_ERR_UNSUPPORTED;
+    if (head_dim != 16 && head_dim != 32 && head_dim != 64 && head_dim != 128) return TTB_ERR_UNSUPPORTED;
+    if (heads < 1 || kv_heads < 1 || (reinterpret_cast<uintptr_t>(q_out) & 7u) || (reinterpret_cast<uintptr_t>(key_pages) & 7u) ||
+        (reinterpret_cast<uintptr_t>(value_pages) & 7u))
+        return TTB_ERR_UNSUPPORTED;
+    const int N = (heads + 2 * kv_heads) * head_dim;
+    const int nx = M <= 32 ? 32 : 64;
+    CUtensorMap map_w, map_x;
+    if (!sk_make_map(&map_w, W, N, K, ldw, 64)) return TTB_ERR_UNSUPPORTED;
+    if (!sk_make_map(&map_x, X, M, K, ldx, nx)) return TTB_ERR_UNSUPPORTED;
+    SkRope rope = {positions, seg_of_token, inv_freq, block_table, (__nv_bfloat16*)key_pages, (__nv_bfloat16*)value_pages,
+                   status, table_width, page_size, num_pages, heads, kv_heads, head_dim, write_kv};
+    if (nx == 32)
+        return sk_launch<32, SK_ROPE, __nv_bfloat16>(map_w, map_x, q_out, M, N, K, heads * head_dim, 0, error_flag, stream, &rope);
+    return sk_launch<64, SK_ROPE, __nv_bfloat16>(map_w, map_x, q_out, M, N, K, heads * head_dim, 0, error_flag, stream, &rope);
 }

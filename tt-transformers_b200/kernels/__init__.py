@@ -93,7 +93,7 @@ class CudaKernels:
                      "ttb_gemm_tcgen05", "ttb_paged_attention_tcgen05", "ttb_attention_tcgen05_supports",
                      "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge", "ttb_gemv_qkv_rope",
                      "ttb_gemm_skinny_tcgen05", "ttb_gemm_skinny_tcgen05_rows", "ttb_softcap", "ttb_sample_scratch_bytes",
-                     "ttb_gemv_ring"):
+                     "ttb_gemv_ring", "ttb_gemm_skinny_tcgen05_qkv_rope"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -122,6 +122,12 @@ class CudaKernels:
         # 0.793 / 0.842 / 0.928 / 1.106 without: bit 4 alone 0.774 / 0.824 / 0.907 / 1.076; bit 1 alone 0.814 /
         # 0.857 / 0.930 / 1.094; bit 8 alone 0.797 / 0.845 / 0.932 / 1.109; bits 1 and 2 1.101 at batch 8.
         self.ring_gemv = int(os.environ.get("TTB200_RING_GEMV", "5"))
+        # decode steps of 17 to 64 tokens: QKV projection, rotation and cache write in the weight-streaming tcgen05
+        # kernel (False: the library's product and the rotation kernel). One launch instead of two and no library on
+        # the way, at the same speed: ms a step with / without, context 8,192 unless said: 1B sizes batch 32 2.261 /
+        # 2.252, batch 64 3.543 / 3.552; 3B sizes batch 32 at 2,048 tokens 2.943 / 2.996; 8B sizes batch 64 at 4,096
+        # tokens 8.922 / 8.890
+        self.skinny_qkv_rope = os.environ.get("TTB200_SKINNY_QKV_ROPE", "1") == "1"
         # bfloat16 products with more rows than the skinny kernel takes: the TMA + tcgen05 kernel of
         # gemm_tcgen05.cu or the library's product. None (TTB200_TCGEN05 unset or "auto"): the feed-forward's
         # gate/up product with its fused SwiGLU goes to the tcgen05 kernel from TCGEN05_SWIGLU_ROWS rows on
@@ -383,6 +389,20 @@ class CudaKernels:
         norm = x if isinstance(x, DeferredNorm) else None
         if (norm is not None and not self.fuse_norm) or interleaved:
             return None
+        if (norm is None and self.skinny_qkv_rope and self.FUSED_QKV_ROWS < M <= self.SKINNY_TCGEN05_ROWS
+                and w_qkv.dtype == torch.bfloat16 and x.dtype == torch.bfloat16 and K % 8 == 0 and x.stride(1) == 1
+                and x.stride(0) % 8 == 0 and w_qkv.stride(1) == 1 and w_qkv.stride(0) % 8 == 0 and inv_freq is not None
+                and rotary_dim == head_dim and head_dim in (16, 32, 64, 128) and view is not None
+                and view.keys.dtype == torch.bfloat16 and view.keys.is_contiguous() and view.values.is_contiguous()
+                and x.data_ptr() % 16 == 0 and w_qkv.data_ptr() % 16 == 0):
+            q = torch.empty(M, heads * head_dim, dtype=w_qkv.dtype, device=self.device)
+            self._check(self.lib.ttb_gemm_skinny_tcgen05_qkv_rope(
+                self._p(x), self._p(w_qkv), self._p(q), M, K, x.stride(0), w_qkv.stride(0), self._p(batch.positions),
+                self._p(batch.seg_of_token), self._p(inv_freq), heads, kv_heads, head_dim, self._p(view.keys),
+                self._p(view.values), self._p(view.block_table), view.block_table.shape[1], view.page_size,
+                view.keys.shape[0], 1 if write_kv else 0, self._p(self.status), self._p(self.tc_error), self._stream()),
+                "gemm_skinny_tcgen05_qkv_rope")
+            return q
         src = norm.xg if norm is not None else x
         if not (w_qkv.dtype == torch.bfloat16 and M <= self.FUSED_QKV_ROWS and K % 8 == 0 and src.stride(1) == 1
                 and src.dtype == torch.bfloat16 and src.stride(0) % 8 == 0
