@@ -176,6 +176,28 @@ def test_trace_run_as_a_program(tiny_folders, tmp_path, dtype, tol, eager):
         assert helpers.relative_error(torch.stack(got[rid]), ref[rid]) < tol
 
 
+def test_the_demo_as_a_program(tiny_folders):
+    """bin/demo with the reference demo's options: a folder without a tokenizer takes token ids and prints token ids,
+    the same ones that greedy generation through the plain implementation gives."""
+    prompt = helpers.random_tokens(384, 23, 77)
+    config, weights = plain_llama.read_model_folder(tiny_folders["B"])
+    want = plain_llama.greedy(config, weights, prompt, 12)
+    proc = subprocess.run([sys.executable, os.path.join(ROOT, "bin", "demo"), "--hf-model", tiny_folders["B"], "--prompt",
+                           ",".join(map(str, prompt)), "--max-new-tokens", "12", "--max-seq-len", "256", "--dtype", "float32"],
+                          capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    got = [int(t) for t in proc.stdout.strip().split("\n")[-1].split()]
+    assert len(got) == 12 and all(0 <= t < 384 for t in got)
+    from tt_transformers_b200 import from_pretrained
+
+    llm = from_pretrained(tiny_folders["B"], dtype="float32", max_batch_size=1, max_seq_len=256)
+    try:
+        assert llm.generate([prompt], max_new_tokens=12)[0] == got
+    finally:
+        llm.cleanup()
+    assert got == want
+
+
 MODEL_SIZED = {
     "architectures": ["LlamaForCausalLM"],
     "hidden_size": 2048, "num_hidden_layers": 2, "num_attention_heads": 32, "num_key_value_heads": 8,
