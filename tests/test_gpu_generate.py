@@ -176,6 +176,54 @@ def test_trace_run_as_a_program(tiny_folders, tmp_path, dtype, tol, eager):
         assert helpers.relative_error(torch.stack(got[rid]), ref[rid]) < tol
 
 
+@pytest.mark.parametrize("name,dtype,tol", [("D", "float32", 1e-4), ("D", "bfloat16", 6e-2), ("E", "bfloat16", 6e-2)])
+def test_many_requests_arriving_at_random_into_a_scarce_pool(tiny_folders, name, dtype, tol):
+    """Two hundred requests of random lengths arrive a few per step; the page pool holds a fraction of what twelve live
+    requests may need, so requests give way and are computed again, while steps are decoded ahead of the host and
+    replayed from captured graphs. Every token that comes out must be the plain implementation's best token given the
+    tokens before it (or within the tolerance of it), and the cache's books must balance all the way."""
+    import random
+
+    from tt_transformers_b200 import from_pretrained
+    from tt_transformers_b200.sampling import SamplingParams
+
+    rng = random.Random(5)
+    config, weights = plain_llama.read_model_folder(tiny_folders[name])
+    vocab = config["vocab_size"]
+    llm = from_pretrained(tiny_folders[name], dtype=dtype, max_batch_size=12, max_seq_len=448, page_size=16, num_pages=90,
+                          max_step_tokens=192, max_chunk_tokens=96)
+    todo = []
+    for _ in range(200):
+        n = min(rng.choice([1, 2, 3, 5, 17, 40, 96, 130, 200, 260]) + rng.randrange(0, 7), 440)
+        todo.append(([rng.randrange(vocab) for _ in range(n)], rng.choice([1, 2, 8, 33, 64, 120])))
+    live, steps = [], 0
+    try:
+        while todo or llm.has_unfinished():
+            for _ in range(rng.choice([0, 1, 1, 2, 4, 8])):
+                if todo:
+                    prompt, new = todo.pop()
+                    live.append(llm.add_request(prompt, SamplingParams(temperature=0.0, max_new_tokens=new, ignore_eos=True)))
+            if llm.has_unfinished():
+                llm.step()
+                steps += 1
+            if steps % 64 == 0:
+                llm.engine.cache.audit()
+        llm.engine.kernels.check_status()
+        gave_way = llm._scheduler.preemptions
+    finally:
+        llm.cleanup()
+    assert gave_way > 10, "the pool was meant to be too small"
+    for r in live:
+        assert r.finish_reason in ("length", "context") and len(r.output) >= 1
+        seq = list(r.prompt) + list(r.output)
+        if len(seq) < 2:
+            continue
+        logits = plain_llama.forward(config, weights, seq[:-1])
+        for j, tok in enumerate(r.output):
+            row = logits[len(r.prompt) - 1 + j]
+            assert float(row.max() - row[tok]) <= tol * max(1.0, float(row.abs().max())), (len(r.prompt), j)
+
+
 def test_the_demo_as_a_program(tiny_folders):
     """bin/demo with the reference demo's options: a folder without a tokenizer takes token ids and prints token ids,
     the same ones that greedy generation through the plain implementation gives."""
